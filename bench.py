@@ -1,0 +1,368 @@
+"""Benchmark of the B200 MatMulNBits hot path (libtq4) on the north-star configs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2] [--impl ours|reference]
+
+A step is one MatMulNBits call (one pass of the hot path over one batch of activations). The
+default workload is the prefill-shaped config (C2: A f16 [512, 1024], K=1024, N=3072, 4-bit,
+block 32, f16 scales, packed zero points; metric TFLOP/s). Other workloads: c1 (decode, M=1,
+GB/s), c3m1 / c3m64 (151936-column lm_head, GB/s; N-sharded with an NCCL all-gather when run
+on several GPUs), c5-<K>x<N>-m<M> (Llama-3-8B shapes).
+
+Timing: W untimed warm-up steps, then exactly K steps between barriers and synchronizes, timed
+with CUDA events on the launching stream; max over ranks. Consecutive steps rotate over R
+independent copies of (weights, A, Y) whose total exceeds twice the L2, so no step reads
+another step's data from L2. `value` has the inputs resident in HBM; `e2e` times the same calls
+through the public API with A copied from pinned host memory and Y read back each step.
+
+`--impl reference` times the reference's arithmetic on the host cores instead (the CPU oracle's
+moved-weight path: weights dequantized once as lib/transmuter.ex:1230-1240 does, then a dense
+f32 BLAS product per call, as EXLA's CPU client runs a moved model).
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MatMulNBits q4 HBM GB/s (M=1), TFLOP/s (M>=256); q4 decoder decode tok/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c2")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def metric_value(cfg, seconds_per_call, full=True):
+    if cfg.metric == "TFLOP/s":
+        return cfg.flops() / seconds_per_call / 1e12
+    return cfg.algorithmic_bytes() / seconds_per_call / 1e9
+
+
+# ---- clocks ----------------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        self.t0 = time.time()
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        with open(self.file.name) as f:
+            rows = [r.strip().split(",") for r in f if r.strip()]
+        os.unlink(self.file.name)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---- reference (CPU) path --------------------------------------------------------------------
+def blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        info = [x for x in threadpool_info() if x.get("user_api") == "blas"]
+        return max(x.get("num_threads", 1) for x in info) if info else os.cpu_count()
+    except Exception:
+        return os.cpu_count()
+
+
+def cpu_reference(cfg, p, steps, warmup, budget_s):
+    """The oracle's moved-weight path on the host cores: W dequantized once (not timed), then a
+    dense f32 A @ W^T per call. Returns (value in the metric's unit, calls timed, sample text)."""
+    from oracle import matmul_nbits as o
+    t = cfg.scale_type
+    w = o.dequantize_weight(p["B"], p["scales"], p["zp"], cfg.k, cfg.n, cfg.bits, cfg.block_size, t)
+    w32 = np.ascontiguousarray(w.astype(np.float32))
+    a32 = np.ascontiguousarray(np.asarray(p["A"], np.float32))
+    for _ in range(max(1, warmup)):
+        a32 @ w32.T
+    times = []
+    t_end = time.perf_counter() + budget_s
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        y = a32 @ w32.T
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end:
+            break
+    sec = sum(times) / len(times)
+    del y
+    sample = (f"oracle moved-weight path (dequantize once, then numpy/BLAS f32 A@W^T), "
+              f"{len(times)} calls of the full {cfg.m}x{cfg.k}x{cfg.n} workload")
+    return metric_value(cfg, sec), len(times), sample
+
+
+# ---- our path --------------------------------------------------------------------------------
+def launches_per_call(cfg, m, sharded_world=1):
+    n = 1 if m <= 16 else -(-m // 16)
+    if sharded_world > 1 and not (m == 1 and cfg.n % (16 * sharded_world) == 0):
+        n += 1  # the unshard kernel after the all-gather
+    return n
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    from transmuter_b200 import workloads
+    if args.workload not in workloads.CONFIGS:
+        raise SystemExit(f"unknown workload {args.workload}; one of {sorted(workloads.CONFIGS)}")
+    cfg = workloads.CONFIGS[args.workload]
+    config = {"workload": cfg.name, "M": cfg.m, "K": cfg.k, "N": cfg.n, "bits": cfg.bits,
+              "block_size": cfg.block_size, "scales": cfg.scale_type, "zero_points": cfg.zp,
+              "activations": cfg.a_type, "parallelism": "single" if world == 1 else None}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        steps = args.steps or 20
+        p = workloads.make(cfg)
+        value, n_timed, sample = cpu_reference(cfg, p, steps, args.warmup, budget_s=120.0)
+        cores = blas_threads()
+        config["parallelism"] = "host cores"
+        line = {"impl": "reference", "metric": METRIC, "value": value, "unit": cfg.metric, "n_gpus": args.gpus,
+                "steps": steps, "warmup": args.warmup, "ms_per_step": metric_to_ms(cfg, value),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded; shapes and distributions of the config)", "config": config,
+                "cpu_baseline": {"value": value, "unit": cfg.metric, "cores": cores, "kind": "port",
+                                 "sample": sample + f" ({n_timed} of {steps} steps timed)"},
+                "e2e": {"value": value, "unit": cfg.metric, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    from transmuter_b200.quantized import PackedWeight
+    from transmuter_b200 import sharded as shd
+    TT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+
+    sharded_run = world > 1 and args.workload.startswith(("c3", "c5"))
+    # weak scaling (independent batches per rank) unless the workload is N-sharded
+    p = workloads.make(cfg, seed_name=cfg.name if (world == 1 or sharded_run) else f"{cfg.name}/rank{rank}")
+
+    def to_dev(x, t=None):
+        if x is None:
+            return None
+        tt = torch.from_numpy(np.ascontiguousarray(x))
+        return (tt.to(torch.bfloat16) if t == "bf16" else tt).to(dev)
+
+    attrs = (cfg.k, cfg.n, cfg.bits, cfg.block_size)
+    zp_t = cfg.scale_type if cfg.zp == "float" else None
+    per_copy = cfg.algorithmic_bytes() / (world if sharded_run else 1)
+    copies = max(2, int(np.ceil(2 * L2_BYTES / per_copy)))
+    copies = min(copies, 64)
+    comm = None
+    if sharded_run:
+        uid = shd.Comm.unique_id() if rank == 0 else bytes(128)
+        obj = [uid]
+        dist.broadcast_object_list(obj, src=0)
+        comm = shd.Comm(obj[0], world, rank, local_rank, timeout_ms=120000)
+        config["parallelism"] = f"N-sharded over {world} GPUs + NCCL all-gather"
+    else:
+        config["parallelism"] = "single GPU" if world == 1 else f"{world} independent replicas (dp{world})"
+    weights, acts, outs = [], [], []
+    b_d, s_d, z_d = to_dev(p["B"]), to_dev(p["scales"], cfg.scale_type), to_dev(p["zp"], zp_t)
+    for i in range(copies):
+        if sharded_run:
+            weights.append(shd.ShardedWeight(comm, attrs, b_d, s_d, z_d, dtype=TT[cfg.scale_type]))
+        else:
+            weights.append(PackedWeight(attrs, b_d, s_d, z_d, dtype=TT[cfg.scale_type], device=dev))
+        acts.append(to_dev(p["A"], cfg.a_type))
+        outs.append(torch.empty((cfg.m, cfg.n), dtype=TT[cfg.a_type], device=dev))
+    del b_d, s_d, z_d
+    config["l2"] = f"rotating {copies} copies of weights+A+Y ({copies * per_copy / 2**20:.0f} MiB > 2x L2)"
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        j = i % copies
+        weights[j].matmul(acts[j], out=outs[j])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # calibration for a default step count (about one second of timed work)
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    if args.steps is None:
+        t0 = time.perf_counter()
+        for i in range(20):
+            step(i)
+        torch.cuda.synchronize()
+        est = (time.perf_counter() - t0) / 20
+        steps = int(min(20000, max(50, 1.0 / max(est, 1e-6))))
+        if world > 1:
+            t = torch.tensor([steps], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN)
+            steps = int(t.item())
+    else:
+        steps = args.steps
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    sec_per_call = ms / 1e3 / steps
+    units = world if not sharded_run else 1
+    value = metric_value(cfg, sec_per_call) * units
+
+    # e2e through the public API: pinned host A in, Y out, every step
+    a_host = torch.from_numpy(np.ascontiguousarray(p["A"]))
+    a_host = (a_host.to(torch.bfloat16) if cfg.a_type == "bf16" else a_host).pin_memory()
+    y_host = torch.empty((cfg.m, cfg.n), dtype=TT[cfg.a_type]).pin_memory()
+    e2e_steps = max(10, min(steps, 2000))
+    for i in range(3):
+        acts[i % copies].copy_(a_host, non_blocking=True)
+        step(i)
+        y_host.copy_(outs[i % copies], non_blocking=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(e2e_steps):
+        j = i % copies
+        acts[j].copy_(a_host, non_blocking=True)
+        step(i)
+        y_host.copy_(outs[j], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = t.item()
+    e2e_value = metric_value(cfg, ms_e2e / 1e3 / e2e_steps) * units
+
+    # roofline of the dominant kernel (the MatMulNBits kernel is the whole step)
+    pk, pk_kind = peaks()
+    launches = launches_per_call(cfg, cfg.m, world if sharded_run else 1)
+    main_launches = 1 if cfg.m <= 16 else -(-cfg.m // 16)
+    if cfg.metric == "TFLOP/s":
+        achieved = cfg.flops() / main_launches / (sec_per_call / main_launches) / 1e12
+        peak = pk["bf16_tflops"]
+        bound, unit = "tensor", "TFLOP/s"
+    else:
+        achieved = cfg.algorithmic_bytes() / (world if sharded_run else 1) / sec_per_call / 1e9
+        peak = pk["hbm_gbs"]
+        bound, unit = "hbm", "GB/s"
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get(args.workload)
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": cfg.metric, "n_gpus": world, "steps": steps,
+                "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True,
+                "scaling": "strong" if sharded_run else "weak", "vs_baseline": None,
+                "dtype": cfg.a_type, "data": "synthetic (seeded; shapes and distributions of the config)",
+                "config": config,
+                "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                             "frac": achieved / peak, "traffic": traffic,
+                             "peak_source": f"{pk_kind} ({'burst' if bound == 'tensor' else 'copy'})"},
+                "e2e": {"value": e2e_value, "unit": cfg.metric,
+                        "h2d_bytes_per_step": int(a_host.numel() * a_host.element_size()),
+                        "d2h_bytes_per_step": int(y_host.numel() * y_host.element_size())},
+                "gpu_launches": steps * launches, "clocks": clocks}
+        if world == 1 and not args.no_cpu_baseline:
+            v, n_timed, sample = cpu_reference(cfg, p, 50, 1, budget_s=20.0)
+            line["cpu_baseline"] = {"value": v, "unit": cfg.metric, "cores": blas_threads(), "kind": "port",
+                                    "sample": sample}
+        print(json.dumps(line), flush=True)
+
+    for w in weights:
+        w.close()
+    if comm is not None:
+        comm.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def metric_to_ms(cfg, value):
+    if cfg.metric == "TFLOP/s":
+        return cfg.flops() / (value * 1e12) * 1e3
+    return cfg.algorithmic_bytes() / (value * 1e9) * 1e3
+
+
+if __name__ == "__main__":
+    main()

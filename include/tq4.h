@@ -1,0 +1,156 @@
+/*
+ * tq4 — B200-native (sm_100a) MatMulNBits for Transmuter.
+ *
+ * This is the C ABI that Transmuter's MatMulNBits operator binds (through an Erlang NIF in the
+ * reference's world, through ctypes in this repository's tests). Every entry point takes plain
+ * pointers and sizes, returns a tq4_status, and never aborts or traps: a failure leaves a
+ * message for tq4_last_error() on the calling thread.
+ *
+ * The operator (georgeguimaraes/transmuter, lib/transmuter/ops/quantized.ex:30-46) is
+ *     Y[..., N] = A[..., K] . W^T (+ bias)
+ * where W {N, K} is dequantized from B u8 [N, blocks, block_size*bits/8] (bits values per byte,
+ * lowest bits first), per-block scales [N*blocks] and optional zero points (absent -> 2^(bits-1),
+ * packed bits [N, ceil(blocks*bits/8)], or floats [N*blocks]): W = (q - zero) * scale in a float
+ * type T, one rounding per step, then sliced to K columns (quantized.ex:234-240,306-325;
+ * packed.ex:9-36). `accuracy_level` is not an input: the reference never reads it.
+ *
+ * Pointers named "device" must be CUDA device (or managed) memory of the handle's device; pointers
+ * to tq4_weight_create may be host or device memory. Streams are cudaStream_t passed as void*
+ * (NULL = the legacy default stream).
+ */
+#ifndef TQ4_H
+#define TQ4_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  TQ4_OK = 0,
+  TQ4_ERR_INVALID_ARGUMENT = 1, /* bad sizes, null pointers, inconsistent attributes */
+  TQ4_ERR_UNSUPPORTED = 2,      /* a valid operator the library does not implement (g_idx, bits) */
+  TQ4_ERR_CUDA = 3,             /* a CUDA runtime/driver call failed */
+  TQ4_ERR_NCCL = 4,             /* an NCCL call failed or NCCL is not loadable */
+  TQ4_ERR_OUT_OF_MEMORY = 5,
+  TQ4_ERR_TIMEOUT = 6,          /* a bounded wait (device or host) ran out */
+  TQ4_ERR_DEVICE = 7            /* a kernel reported an error through the device status word */
+} tq4_status;
+
+typedef enum { TQ4_F32 = 0, TQ4_F16 = 1, TQ4_BF16 = 2, TQ4_U8 = 3 } tq4_dtype;
+
+/* Zero points of block_zero_points/5 (quantized.ex:306-325). */
+typedef enum { TQ4_ZP_NONE = 0, TQ4_ZP_PACKED = 1, TQ4_ZP_FLOAT = 2 } tq4_zp_kind;
+
+/* The attributes and input types of one MatMulNBits node.
+ *   K, N, bits, block_size: the node attributes (quantized.ex:226-228; bits 2, 4 or 8;
+ *       block_size a power of two >= 16).
+ *   scale_dtype: type of the scales input (F32, F16 or BF16), N*ceil(K/block_size) values.
+ *   zp_kind / zp_dtype: zero points; zp_dtype is U8 for packed zero points (N rows of
+ *       ceil(blocks*bits/8) bytes) or the float type of float zero points (N*blocks values).
+ *   dequant_dtype: the float type T the weight is dequantized in. In the graph it is A's type
+ *       (quantized.ex:42); for a moved model it is the scales' type after :compute_type
+ *       (lib/transmuter.ex:1230-1233). */
+typedef struct {
+  int64_t K;
+  int64_t N;
+  int32_t bits;
+  int32_t block_size;
+  tq4_dtype scale_dtype;
+  tq4_zp_kind zp_kind;
+  tq4_dtype zp_dtype;
+  tq4_dtype dequant_dtype;
+} tq4_weight_desc;
+
+typedef struct tq4_weight tq4_weight;
+typedef struct tq4_comm tq4_comm;
+typedef struct tq4_sharded tq4_sharded;
+
+/* Bytes of each input that tq4_weight_create reads for `desc` (B, scales, zero points). */
+tq4_status tq4_weight_input_sizes(const tq4_weight_desc* desc, int64_t* b_bytes,
+                                  int64_t* scale_bytes, int64_t* zp_bytes);
+
+/* Replaces the load-time weight builder of Transmuter.move/2 (lib/transmuter.ex:1104-1182,
+ * dequantized_weight/6 at :1230-1240, and the EMLX packer lib/transmuter/emlx.ex:104-148):
+ * copies B, scales and zero points once to `device` and keeps them packed there, in the
+ * handle's own layout. `zp` may be NULL when desc->zp_kind is TQ4_ZP_NONE. Unlike packable?/2
+ * (lib/transmuter.ex:1209-1225), a K that is not a multiple of block_size is accepted. */
+tq4_status tq4_weight_create(const tq4_weight_desc* desc, const void* b, int64_t b_bytes,
+                             const void* scales, const void* zp, int device, tq4_weight** out);
+
+tq4_status tq4_weight_destroy(tq4_weight* w);
+
+/* The handle's attributes and the device bytes it holds. */
+tq4_status tq4_weight_info(const tq4_weight* w, tq4_weight_desc* desc, int64_t* device_bytes);
+
+/* Replaces the MatMulNBits clause (quantized.ex:30-46) for a weight the handle holds:
+ *   Y[M, N] = A[M, K] . W^T (+ bias[N]),  W = dequantize_weight(...) in desc.dequant_dtype.
+ * A (a_dtype F32/F16/BF16), bias (bias_dtype; NULL for none) and Y (y_dtype) are device
+ * pointers, row-major and dense. M >= 0 (M = 0 is a no-op). Calls with M <= 16 run the fused
+ * unpack-dequant-GEMV kernel; larger M run the tensor-core GEMM. */
+tq4_status tq4_matmul(const tq4_weight* w, const void* a, int64_t m, tq4_dtype a_dtype,
+                      const void* bias, tq4_dtype bias_dtype, void* y, tq4_dtype y_dtype,
+                      void* stream);
+
+/* dequantize_weight/4 (quantized.ex:234-240) on the device: W[N, K] in desc.dequant_dtype,
+ * bit-exact with the reference. `out` is a device pointer of N*K elements. */
+tq4_status tq4_dequantize(const tq4_weight* w, void* out, void* stream);
+
+/* GatherBlockQuantized (quantized.ex:49-66) over a handle's rows: out[i, :] = the dequantized
+ * row indices[i] of W, for a table stored as a MatMulNBits weight (tied embeddings). indices
+ * are int64 device values in [0, N); out is [count, K] in desc.dequant_dtype. */
+tq4_status tq4_gather_rows(const tq4_weight* w, const int64_t* indices, int64_t count, void* out,
+                           void* stream);
+
+/* Reads and clears the device status word that bounded waits and device-side checks write.
+ * Synchronizes the handle's device. *code = 0 when no kernel reported an error. */
+tq4_status tq4_device_status(int device, int32_t* code);
+
+/* The message of the last failure on the calling thread ("" when none). Returns the length
+ * of the full message; at most len-1 bytes and a NUL are written to buf. */
+size_t tq4_last_error(char* buf, size_t len);
+
+const char* tq4_status_string(tq4_status status);
+
+/* ---- N-sharded execution over NCCL (one process or thread per GPU) -------------------------
+ * The weight is split along N (rows of B, scales and zero points); each rank computes its
+ * columns of Y and an all-gather over NVLink assembles Y on every rank. No reference
+ * counterpart exists (the reference has no device collective); it serves the 151936-column
+ * lm_head and the Llama-shaped projections of the north star. */
+
+#define TQ4_UNIQUE_ID_BYTES 128
+
+/* Rank 0 makes the id and sends it to the other ranks by any host channel. */
+tq4_status tq4_comm_unique_id(unsigned char id[TQ4_UNIQUE_ID_BYTES]);
+
+/* Joins the communicator; waits at most timeout_ms for the other ranks (0 = 60000). */
+tq4_status tq4_comm_create(const unsigned char id[TQ4_UNIQUE_ID_BYTES], int nranks, int rank,
+                           int device, int timeout_ms, tq4_comm** out);
+
+tq4_status tq4_comm_destroy(tq4_comm* comm);
+
+/* Each rank owns share = ceil(N/P) rounded up to 16 rows: rows [rank*share, rank*share+share)
+ * of the FULL B, scales and zero points (clipped to N; the last ranks may own fewer or none)
+ * become this rank's handle. The inputs may be host or device memory. */
+tq4_status tq4_sharded_create(const tq4_weight_desc* desc, const void* b, int64_t b_bytes,
+                              const void* scales, const void* zp, tq4_comm* comm,
+                              tq4_sharded** out);
+
+/* This rank's first row and row count. */
+tq4_status tq4_sharded_rows(const tq4_sharded* s, int64_t* first, int64_t* count);
+
+/* Y[M, N] on every rank: the local MatMulNBits on this rank's rows, then an NCCL all-gather.
+ * A, bias (full N, or NULL) and Y are device pointers on the comm's device. */
+tq4_status tq4_sharded_matmul(const tq4_sharded* s, const void* a, int64_t m, tq4_dtype a_dtype,
+                              const void* bias, tq4_dtype bias_dtype, void* y, tq4_dtype y_dtype,
+                              void* stream);
+
+tq4_status tq4_sharded_destroy(tq4_sharded* s);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TQ4_H */

@@ -1,0 +1,253 @@
+"""GPU parity of the tq4 kernels against the CPU oracle, through the C ABI (ctypes).
+
+Bars (north star): dequantized weights bit-exact; outputs within rel-L2 1e-3 for f32
+activations and 5e-3 for f16/bf16 activations; the reference fixtures within the reference's
+own tolerance (ops_test.exs:582-598)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import matmul_nbits as o
+from tests.golden_cases import gather_cases, matmul_nbits_cases
+from transmuter_b200 import quantized, workloads
+from transmuter_b200.quantized import ArgumentError, Node, PackedWeight
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"f32": 1e-3, "f16": 5e-3, "bf16": 5e-3}
+TORCH = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+DEV = "cuda:0"
+
+
+def to_dev(x, t=None):
+    if x is None:
+        return None
+    tt = torch.from_numpy(np.ascontiguousarray(x))
+    if t == "bf16":
+        tt = tt.to(torch.bfloat16)
+    return tt.to(DEV)
+
+
+def as_np32(t):
+    return t.float().cpu().numpy()
+
+
+def device_status():
+    import ctypes
+    from transmuter_b200 import _lib
+    code = ctypes.c_int32()
+    _lib.check(_lib.load().tq4_device_status(0, ctypes.byref(code)))
+    return code.value
+
+
+def weight_for(cfg, p, dtype):
+    return PackedWeight((cfg.k, cfg.n, cfg.bits, cfg.block_size), to_dev(p["B"]),
+                        to_dev(p["scales"], cfg.scale_type), to_dev(p["zp"], cfg.scale_type if cfg.zp == "float" else None),
+                        dtype=TORCH[dtype], device=DEV)
+
+
+# ---- the reference's fixtures through the operator entry point ------------------------------
+
+@pytest.mark.parametrize("case", matmul_nbits_cases(), ids=lambda c: c["name"])
+def test_reference_fixture(case):
+    ins = (case["inputs"] + [None] * 6)[:6]
+    a, b, scales, zp, g_idx, bias = ins
+    node = Node("MatMulNBits", case["attrs"], case["input_names"])
+    inputs = [to_dev(a), to_dev(b), to_dev(scales), to_dev(zp), None, to_dev(bias)]
+    (y,) = quantized.apply(node, inputs)
+    y = as_np32(y)
+    diff, tol = o.within_reference_tolerance(y, case["Y"])
+    assert diff <= tol, (diff, tol)
+    assert o.rel_l2(y, case["Y"]) < 1e-3
+
+
+@pytest.mark.parametrize("case", matmul_nbits_cases(), ids=lambda c: c["name"])
+def test_reference_fixture_moved(case):
+    """The moved weight (Transmuter.move/2) gives the in-graph dequantize, bit for bit."""
+    a, b, scales, zp = (case["inputs"] + [None] * 4)[:4]
+    k, n, bits, bs = o.nbits_sizes(case["attrs"])
+    node = Node("MatMulNBits", case["attrs"], case["input_names"])
+    w = quantized.move_weight(node, to_dev(b), to_dev(scales), to_dev(zp), device=DEV)
+    got = as_np32(w.dequantize())
+    want = o.dequantize_weight(b, scales, zp, k, n, bits, bs, "f32")
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("case", gather_cases(), ids=lambda c: c["name"])
+def test_gather_block_quantized_fixture(case):
+    data, indices, scales, zp = case["inputs"][:4]
+    node = Node("GatherBlockQuantized", case["attrs"], case["input_names"])
+    (y,) = quantized.apply(node, [to_dev(data), to_dev(indices), to_dev(scales), to_dev(zp)])
+    np.testing.assert_array_equal(as_np32(y), case["Y"])
+
+
+# ---- bit-exact dequantize over the layout and type space -------------------------------------
+
+DEQ = [
+    # bits, bs, K, N, zp, scale type, T
+    (4, 32, 1024, 200, "none", "f32", "f32"),
+    (4, 16, 72, 40, "packed", "f32", "f32"),
+    (4, 32, 72, 17, "none", "f16", "f16"),
+    (4, 128, 4096, 64, "packed", "f16", "f16"),
+    (4, 256, 768, 33, "float", "f32", "f32"),
+    (4, 64, 320, 48, "float", "f16", "f16"),
+    (4, 32, 256, 24, "packed", "bf16", "bf16"),
+    (4, 32, 256, 24, "packed", "f16", "f32"),
+    (2, 16, 64, 8, "packed", "f32", "f32"),
+    (2, 32, 544, 31, "none", "f16", "f16"),
+    (2, 64, 512, 16, "float", "bf16", "bf16"),
+    (8, 32, 64, 8, "packed", "f32", "f32"),
+    (8, 16, 200, 21, "none", "f16", "f16"),
+    (8, 128, 384, 64, "float", "f32", "bf16"),
+]
+
+
+@pytest.mark.parametrize("bits,bs,k,n,zp,st,t", DEQ)
+def test_dequantize_bit_exact(bits, bs, k, n, zp, st, t):
+    cfg = workloads.Config(f"deq-{bits}-{bs}-{k}-{n}-{zp}-{st}-{t}", k, n, 1, bits=bits, block_size=bs,
+                           scale_type=st, zp=zp, scale_range=(0.001, 2.0))
+    p = workloads.make(cfg)
+    w = weight_for(cfg, p, t)
+    got = as_np32(w.dequantize())
+    want = o.dequantize_weight(p["B"], p["scales"], p["zp"], k, n, bits, bs, t).astype(np.float32)
+    assert got.shape == want.shape
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+# ---- GEMV (M <= 16) and the large-M path ------------------------------------------------------
+
+GEMV = [
+    # K, N, M, bits, bs, zp, scale type, A type, T, bias
+    (1024, 3072, 1, 4, 32, "none", "f32", "f32", "f32", False),
+    (1024, 3072, 1, 4, 32, "packed", "f16", "f16", "f16", False),
+    (1024, 3072, 16, 4, 32, "packed", "f16", "f16", "f16", True),
+    (4096, 1024, 1, 4, 128, "packed", "f16", "f16", "f16", False),
+    (4096, 1024, 7, 4, 128, "packed", "f16", "f16", "f16", False),
+    (14336, 512, 3, 4, 128, "packed", "f16", "f16", "f16", False),
+    (72, 16, 6, 4, 32, "none", "f32", "f32", "f32", True),
+    (512, 40, 6, 4, 256, "packed", "f32", "f32", "f32", False),
+    (1000, 333, 9, 4, 16, "float", "f32", "f32", "f32", True),
+    (2048, 500, 5, 4, 64, "packed", "bf16", "bf16", "bf16", False),
+    (2048, 500, 12, 4, 64, "none", "f32", "bf16", "f32", False),
+    (640, 100, 4, 2, 16, "packed", "f32", "f32", "f32", False),
+    (1024, 128, 16, 2, 128, "none", "f16", "f16", "f16", False),
+    (640, 100, 4, 8, 32, "packed", "f32", "f32", "f32", False),
+    (1024, 96, 11, 8, 16, "float", "f16", "bf16", "f16", True),
+    (256, 8, 1, 8, 256, "packed", "bf16", "bf16", "bf16", False),
+]
+
+
+def run_case(k, n, m, bits, bs, zp, st, at, t, bias, scale_range=(0.005, 0.02)):
+    cfg = workloads.Config(f"mm-{k}-{n}-{m}-{bits}-{bs}-{zp}-{st}-{at}-{t}-{bias}", k, n, m, bits=bits,
+                           block_size=bs, scale_type=st, zp=zp, a_type=at, bias=bias, scale_range=scale_range)
+    p = workloads.make(cfg)
+    w = weight_for(cfg, p, t)
+    a = to_dev(p["A"], at)
+    bias_t = to_dev(p["bias"], at) if bias else None
+    y = w.matmul(a, bias_t)
+    wd = o.dequantize_weight(p["B"], p["scales"], p["zp"], k, n, bits, bs, t)
+    want = np.asarray(p["A"], np.float64) @ wd.astype(np.float64).T
+    if bias:
+        want = want + np.asarray(p["bias"], np.float64)
+    return as_np32(y), want, cfg
+
+
+@pytest.mark.parametrize("k,n,m,bits,bs,zp,st,at,t,bias", GEMV)
+def test_gemv_parity(k, n, m, bits, bs, zp, st, at, t, bias):
+    got, want, _ = run_case(k, n, m, bits, bs, zp, st, at, t, bias)
+    assert got.shape == want.shape
+    assert np.isfinite(got).all()
+    assert o.rel_l2(got, want) < TOL[at], o.rel_l2(got, want)
+
+
+LARGE_M = [
+    (1024, 3072, 17, 4, 32, "packed", "f16", "f16", "f16", False),
+    (1024, 256, 64, 4, 32, "none", "f32", "f32", "f32", True),
+    (2048, 384, 200, 4, 128, "packed", "f16", "f16", "f16", True),
+    (1024, 512, 130, 4, 64, "packed", "bf16", "bf16", "bf16", False),
+    (512, 320, 33, 8, 32, "float", "f16", "f16", "f16", False),
+]
+
+
+@pytest.mark.parametrize("k,n,m,bits,bs,zp,st,at,t,bias", LARGE_M)
+def test_large_m_parity(k, n, m, bits, bs, zp, st, at, t, bias):
+    got, want, _ = run_case(k, n, m, bits, bs, zp, st, at, t, bias)
+    assert o.rel_l2(got, want) < TOL[at], o.rel_l2(got, want)
+
+
+def test_c1_full_size():
+    cfg = workloads.CONFIGS["c1"]
+    got, want, _ = run_case(cfg.k, cfg.n, cfg.m, 4, 32, "none", "f32", "f32", "f32", False)
+    assert o.rel_l2(got, want) < 1e-3
+
+
+def test_c2_full_size():
+    cfg = workloads.CONFIGS["c2"]
+    p = workloads.make(cfg)
+    w = weight_for(cfg, p, "f16")
+    y = as_np32(w.matmul(to_dev(p["A"])))
+    ref, _ = o.matmul_nbits(p["attrs"], p["A"], p["B"], p["scales"], p["zp"])
+    assert o.rel_l2(y, ref) < 5e-3
+
+
+def test_c3_lm_head_full_size_property():
+    """151936 x 1024 at M = 1 and 64: Y equals A . W^T with W from tq4_dequantize (itself checked
+    bit-exact against the oracle on sampled rows), in float64 on the CPU."""
+    cfg = workloads.CONFIGS["c3m64"]
+    p = workloads.make(cfg)
+    w = weight_for(cfg, p, "f32")
+    wd = w.dequantize()
+    rows = np.random.default_rng(1).choice(cfg.n, 64, replace=False)
+    sub = o.dequantize_weight(p["B"][rows], p["scales"].reshape(cfg.n, -1)[rows].reshape(-1), None,
+                              cfg.k, 64, 4, 32, "f32")
+    np.testing.assert_array_equal(as_np32(wd[torch.from_numpy(rows).to(DEV)]).view(np.uint32), sub.view(np.uint32))
+    a = to_dev(p["A"])
+    for m in (1, 64):
+        y = w.matmul(a[:m]).double()
+        want = a[:m].double() @ wd.double().T
+        err = ((y - want).norm() / want.norm()).item()
+        assert err < 1e-3, (m, err)
+
+
+def test_m_zero_is_a_noop_and_errors_are_status():
+    cfg = workloads.Config("err", 64, 8, 1)
+    p = workloads.make(cfg)
+    w = weight_for(cfg, p, "f32")
+    y = w.matmul(torch.zeros(0, 64, device=DEV))
+    assert y.shape == (0, 8)
+    with pytest.raises(ArgumentError):
+        w.matmul(torch.zeros(1, 63, device=DEV))
+    with pytest.raises(ArgumentError):
+        w.matmul(torch.zeros(1, 64, dtype=torch.float64, device=DEV))
+
+
+def test_repeated_calls_are_deterministic():
+    """Split-K reductions sum in a fixed order: the same call gives the same bits."""
+    cfg = workloads.CONFIGS["c5-4096x1024-m1"]
+    p = workloads.make(cfg)
+    w = weight_for(cfg, p, "f16")
+    a = to_dev(p["A"])
+    y0 = w.matmul(a)
+    for _ in range(3):
+        assert torch.equal(w.matmul(a), y0)
+
+
+def test_concurrent_streams_do_not_share_workspace():
+    cfg = workloads.CONFIGS["c5-4096x1024-m16"]
+    p = workloads.make(cfg)
+    w = weight_for(cfg, p, "f16")
+    a = to_dev(p["A"])
+    ref = w.matmul(a)
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    outs = []
+    for s in (s1, s2, s1, s2):
+        with torch.cuda.stream(s):
+            outs.append(w.matmul(a))
+    torch.cuda.synchronize()
+    for y in outs:
+        assert torch.equal(y, ref)
+
+
+def test_device_status_clean():
+    assert device_status() == 0

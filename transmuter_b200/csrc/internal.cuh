@@ -1,0 +1,116 @@
+// Host-side internals shared by the tq4 translation units: the weight handle, device buffers,
+// error reporting.
+#pragma once
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace tq4 {
+
+// Thread-local last error message (tq4_last_error).
+void set_error(const char* fmt, ...);
+
+inline int dtype_size(tq4_dtype t) {
+  switch (t) {
+    case TQ4_F32: return 4;
+    case TQ4_F16: return 2;
+    case TQ4_BF16: return 2;
+    case TQ4_U8: return 1;
+  }
+  return 0;
+}
+
+inline const char* dtype_name(tq4_dtype t) {
+  switch (t) {
+    case TQ4_F32: return "f32";
+    case TQ4_F16: return "f16";
+    case TQ4_BF16: return "bf16";
+    case TQ4_U8: return "u8";
+  }
+  return "?";
+}
+
+#define TQ4_TRY(expr)                      \
+  do {                                     \
+    tq4_status _s = (expr);                \
+    if (_s != TQ4_OK) return _s;           \
+  } while (0)
+
+#define TQ4_CUDA(expr)                                                                      \
+  do {                                                                                      \
+    cudaError_t _e = (expr);                                                                \
+    if (_e != cudaSuccess) {                                                                \
+      ::tq4::set_error("%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), __FILE__,    \
+                       __LINE__);                                                           \
+      return _e == cudaErrorMemoryAllocation ? TQ4_ERR_OUT_OF_MEMORY : TQ4_ERR_CUDA;        \
+    }                                                                                       \
+  } while (0)
+
+// A device allocation owned by a handle (freed on destruction).
+struct DeviceBuffer {
+  void* ptr = nullptr;
+  int64_t bytes = 0;
+  DeviceBuffer() = default;
+  DeviceBuffer(const DeviceBuffer&) = delete;
+  DeviceBuffer& operator=(const DeviceBuffer&) = delete;
+  ~DeviceBuffer() { release(); }
+  tq4_status alloc(int64_t n) {
+    release();
+    if (n <= 0) return TQ4_OK;
+    cudaError_t e = cudaMalloc(&ptr, (size_t)n);
+    if (e != cudaSuccess) {
+      ptr = nullptr;
+      set_error("cudaMalloc(%lld bytes) failed: %s", (long long)n, cudaGetErrorString(e));
+      return e == cudaErrorMemoryAllocation ? TQ4_ERR_OUT_OF_MEMORY : TQ4_ERR_CUDA;
+    }
+    bytes = n;
+    return TQ4_OK;
+  }
+  void release() {
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    bytes = 0;
+  }
+};
+
+}  // namespace tq4
+
+// The weight handle: the node's attributes and its device buffers in the handle's layout.
+struct tq4_weight {
+  tq4_weight_desc desc{};
+  int device = 0;
+  int64_t blocks = 0;      // ceil(K / block_size)
+  int64_t k_pad = 0;       // K rounded up to whole 64-byte groups
+  int64_t row_bytes = 0;   // k_pad * bits / 8, a multiple of 64
+  int64_t groups = 0;      // row_bytes / 64
+  int64_t n_pad = 0;       // N rounded up to 128 rows
+  int64_t blocks_pad = 0;  // blocks per row of the scale / zero-point arrays
+  int bs_log2 = 0;
+  float z_const = 0.f;     // 2^(bits-1) when the node has no zero points
+  cudaStream_t stream = nullptr;  // the handle's own stream (creation work only)
+  tq4::DeviceBuffer q;       // [n_pad][row_bytes]
+  tq4::DeviceBuffer scales;  // [n_pad][blocks_pad] in T
+  tq4::DeviceBuffer zps;     // [n_pad][blocks_pad] in T, or empty
+  int num_sms = 148;
+  // split-K workspaces of the GEMV, one per CUDA stream (a tq4::WorkspaceMap, made on first use)
+  void* ws_mutex = nullptr;
+};
+
+namespace tq4 {
+using Weight = tq4_weight;
+
+tq4_status prepare_weight(Weight& w, const void* b, const void* scales, const void* zp);
+tq4_status run_dequant(const Weight& w, const int64_t* rows, int64_t n_out, void* out, cudaStream_t st);
+// Y rows have a stride of `ldy` elements (N for a dense Y; the shard width for a sharded call).
+tq4_status run_gemv(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,
+                    tq4_dtype bias_t, void* y, tq4_dtype y_t, int64_t ldy, cudaStream_t st);
+tq4_status run_gemm(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,
+                    tq4_dtype bias_t, void* y, tq4_dtype y_t, int64_t ldy, cudaStream_t st);
+tq4_status run_matmul(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,
+                      tq4_dtype bias_t, void* y, tq4_dtype y_t, int64_t ldy, cudaStream_t st);
+}  // namespace tq4

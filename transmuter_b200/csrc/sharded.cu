@@ -1,0 +1,316 @@
+// N-sharded MatMulNBits over NCCL: each rank holds rows [first, first+count) of B, scales and
+// zero points, computes its columns of Y, and an all-gather over NVLink assembles Y on every
+// rank. The reference has no device collective; this serves the very wide projections (the
+// 151936-column lm_head) named by the north star.
+//
+// NCCL is loaded with dlopen at first use, so the library loads on hosts without NCCL and links
+// to whichever libnccl.so.2 the process already has (torch's, when torch is imported first).
+// Communicators are non-blocking: initialisation polls ncclCommGetAsyncError against a host
+// deadline and aborts the communicator when the deadline passes.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <mutex>
+#include <thread>
+
+#include "internal.cuh"
+
+namespace tq4 {
+
+struct NcclApi {
+  void* handle = nullptr;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+static NcclApi* nccl_api() {
+  static NcclApi api;
+  static bool tried = false;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (tried) return api.handle ? &api : nullptr;
+  tried = true;
+  const char* names[] = {"libnccl.so.2", "libnccl.so"};
+  for (const char* n : names) {
+    api.handle = dlopen(n, RTLD_NOW | RTLD_GLOBAL);
+    if (api.handle) break;
+  }
+  if (!api.handle) return nullptr;
+#define TQ4_SYM(field, name) api.field = reinterpret_cast<decltype(api.field)>(dlsym(api.handle, name))
+  TQ4_SYM(GetUniqueId, "ncclGetUniqueId");
+  TQ4_SYM(CommInitRankConfig, "ncclCommInitRankConfig");
+  TQ4_SYM(CommGetAsyncError, "ncclCommGetAsyncError");
+  TQ4_SYM(CommAbort, "ncclCommAbort");
+  TQ4_SYM(CommDestroy, "ncclCommDestroy");
+  TQ4_SYM(AllGather, "ncclAllGather");
+  TQ4_SYM(GetErrorString, "ncclGetErrorString");
+#undef TQ4_SYM
+  if (!api.GetUniqueId || !api.CommInitRankConfig || !api.CommGetAsyncError || !api.CommAbort ||
+      !api.CommDestroy || !api.AllGather || !api.GetErrorString) {
+    dlclose(api.handle);
+    api.handle = nullptr;
+    return nullptr;
+  }
+  return &api;
+}
+
+static tq4_status need_nccl(NcclApi** out) {
+  *out = nccl_api();
+  if (!*out) {
+    set_error("NCCL is not available (dlopen libnccl.so.2 failed or lacks symbols)");
+    return TQ4_ERR_NCCL;
+  }
+  return TQ4_OK;
+}
+
+// Waits until a non-blocking communicator leaves ncclInProgress, at most until `deadline`.
+static tq4_status nccl_wait(NcclApi* api, ncclComm_t comm,
+                            std::chrono::steady_clock::time_point deadline, const char* what) {
+  for (;;) {
+    ncclResult_t state = ncclSuccess;
+    ncclResult_t r = api->CommGetAsyncError(comm, &state);
+    if (r != ncclSuccess) state = r;
+    if (state == ncclSuccess) return TQ4_OK;
+    if (state != ncclInProgress) {
+      set_error("%s: %s", what, api->GetErrorString(state));
+      return TQ4_ERR_NCCL;
+    }
+    if (std::chrono::steady_clock::now() > deadline) {
+      set_error("%s: timed out waiting for the other ranks", what);
+      return TQ4_ERR_TIMEOUT;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
+}
+
+static ncclDataType_t nccl_type(tq4_dtype t) {
+  switch (t) {
+    case TQ4_F16: return ncclFloat16;
+    case TQ4_BF16: return ncclBfloat16;
+    default: return ncclFloat32;
+  }
+}
+
+// [P][M][share] (the all-gather order) -> Y [M][N]
+template <typename T>
+__global__ void unshard_kernel(const T* __restrict__ g, int64_t m, int64_t share, int nranks,
+                               int64_t n, T* __restrict__ y) {
+  const int64_t total = m * n;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / n, col = i % n;
+    const int64_t r = col / share, j = col % share;
+    y[i] = g[(r * m + row) * share + j];
+  }
+}
+
+}  // namespace tq4
+
+using namespace tq4;
+
+struct tq4_comm {
+  ncclComm_t comm = nullptr;
+  int nranks = 1, rank = 0, device = 0;
+  bool broken = false;
+};
+
+struct tq4_sharded {
+  tq4_comm* comm = nullptr;
+  tq4_weight* local = nullptr;  // null when this rank owns no rows
+  tq4_weight_desc desc{};       // the full weight
+  int64_t share = 0;            // rows per rank (a multiple of 16), the all-gather unit
+  int64_t first = 0, count = 0;
+  std::mutex mu;
+  DeviceBuffer part;    // this rank's [M][share] output
+  DeviceBuffer gather;  // [P][M][share]
+};
+
+extern "C" {
+
+tq4_status tq4_comm_unique_id(unsigned char id[TQ4_UNIQUE_ID_BYTES]) {
+  NcclApi* api;
+  TQ4_TRY(need_nccl(&api));
+  if (!id) {
+    set_error("tq4_comm_unique_id: null output");
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  ncclUniqueId uid;
+  ncclResult_t r = api->GetUniqueId(&uid);
+  if (r != ncclSuccess) {
+    set_error("ncclGetUniqueId: %s", api->GetErrorString(r));
+    return TQ4_ERR_NCCL;
+  }
+  static_assert(sizeof(uid.internal) == TQ4_UNIQUE_ID_BYTES, "NCCL unique id size");
+  memcpy(id, uid.internal, TQ4_UNIQUE_ID_BYTES);
+  return TQ4_OK;
+}
+
+tq4_status tq4_comm_create(const unsigned char id[TQ4_UNIQUE_ID_BYTES], int nranks, int rank,
+                           int device, int timeout_ms, tq4_comm** out) {
+  if (!out || !id || nranks < 1 || rank < 0 || rank >= nranks) {
+    set_error("tq4_comm_create: bad arguments (nranks=%d, rank=%d)", nranks, rank);
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  *out = nullptr;
+  NcclApi* api;
+  TQ4_TRY(need_nccl(&api));
+  TQ4_CUDA(cudaSetDevice(device));
+  ncclUniqueId uid;
+  memcpy(uid.internal, id, TQ4_UNIQUE_ID_BYTES);
+  ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+  config.blocking = 0;
+  tq4_comm* c = new tq4_comm();
+  c->nranks = nranks;
+  c->rank = rank;
+  c->device = device;
+  ncclResult_t r = api->CommInitRankConfig(&c->comm, nranks, uid, rank, &config);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    set_error("ncclCommInitRankConfig: %s", api->GetErrorString(r));
+    delete c;
+    return TQ4_ERR_NCCL;
+  }
+  const auto deadline = std::chrono::steady_clock::now() +
+                        std::chrono::milliseconds(timeout_ms > 0 ? timeout_ms : 60000);
+  tq4_status st = nccl_wait(api, c->comm, deadline, "ncclCommInitRankConfig");
+  if (st != TQ4_OK) {
+    api->CommAbort(c->comm);
+    delete c;
+    return st;
+  }
+  *out = c;
+  return TQ4_OK;
+}
+
+tq4_status tq4_comm_destroy(tq4_comm* c) {
+  if (!c) return TQ4_OK;
+  NcclApi* api = nccl_api();
+  if (api && c->comm) {
+    ncclResult_t state = ncclSuccess;
+    api->CommGetAsyncError(c->comm, &state);
+    if (c->broken || (state != ncclSuccess && state != ncclInProgress)) api->CommAbort(c->comm);
+    else api->CommDestroy(c->comm);
+  }
+  delete c;
+  return TQ4_OK;
+}
+
+tq4_status tq4_sharded_create(const tq4_weight_desc* d, const void* b, int64_t b_bytes,
+                              const void* scales, const void* zp, tq4_comm* comm,
+                              tq4_sharded** out) {
+  if (!out || !comm || !d) {
+    set_error("tq4_sharded_create: null argument");
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  *out = nullptr;
+  int64_t need_b = 0;
+  TQ4_TRY(tq4_weight_input_sizes(d, &need_b, nullptr, nullptr));
+  if (b_bytes != need_b || !b || !scales || (d->zp_kind != TQ4_ZP_NONE && !zp)) {
+    set_error("tq4_sharded_create: B has %lld bytes (expected %lld) or an input is missing",
+              (long long)b_bytes, (long long)need_b);
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  tq4_sharded* s = new tq4_sharded();
+  s->comm = comm;
+  s->desc = *d;
+  const int64_t P = comm->nranks;
+  s->share = ((d->N + P - 1) / P + 15) / 16 * 16;
+  s->first = std::min<int64_t>(d->N, comm->rank * s->share);
+  s->count = std::min<int64_t>(d->N - s->first, s->share);
+  if (s->count > 0) {
+    const int64_t blocks = (d->K + d->block_size - 1) / d->block_size;
+    const int64_t raw_row = blocks * d->block_size * d->bits / 8;
+    tq4_weight_desc ld = *d;
+    ld.N = s->count;
+    const uint8_t* bb = static_cast<const uint8_t*>(b) + s->first * raw_row;
+    const uint8_t* sb = static_cast<const uint8_t*>(scales) + s->first * blocks * dtype_size(d->scale_dtype);
+    const uint8_t* zb = nullptr;
+    if (d->zp_kind == TQ4_ZP_PACKED) zb = static_cast<const uint8_t*>(zp) + s->first * ((blocks * d->bits + 7) / 8);
+    if (d->zp_kind == TQ4_ZP_FLOAT) zb = static_cast<const uint8_t*>(zp) + s->first * blocks * dtype_size(d->zp_dtype);
+    tq4_status st = tq4_weight_create(&ld, bb, s->count * raw_row, sb, zb, comm->device, &s->local);
+    if (st != TQ4_OK) {
+      delete s;
+      return st;
+    }
+  }
+  *out = s;
+  return TQ4_OK;
+}
+
+tq4_status tq4_sharded_rows(const tq4_sharded* s, int64_t* first, int64_t* count) {
+  if (!s) {
+    set_error("tq4_sharded_rows: null handle");
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  if (first) *first = s->first;
+  if (count) *count = s->count;
+  return TQ4_OK;
+}
+
+tq4_status tq4_sharded_matmul(const tq4_sharded* cs, const void* a, int64_t m, tq4_dtype a_t,
+                              const void* bias, tq4_dtype bias_t, void* y, tq4_dtype y_t,
+                              void* stream) {
+  tq4_sharded* s = const_cast<tq4_sharded*>(cs);
+  if (!s || m < 0 || (m > 0 && (!a || !y))) {
+    set_error("tq4_sharded_matmul: bad arguments");
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  if (m == 0) return TQ4_OK;
+  NcclApi* api;
+  TQ4_TRY(need_nccl(&api));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t P = s->comm->nranks;
+  const int ys = dtype_size(y_t);
+  std::lock_guard<std::mutex> lock(s->mu);
+  TQ4_CUDA(cudaSetDevice(s->comm->device));
+  // Y itself is the gather target when it already has the [P][1][share] layout.
+  const bool direct = (m == 1 && s->share * P == s->desc.N);
+  if (s->part.bytes < m * s->share * ys) TQ4_TRY(s->part.alloc(m * s->share * ys));
+  if (!direct && s->gather.bytes < P * m * s->share * ys) TQ4_TRY(s->gather.alloc(P * m * s->share * ys));
+  if (s->local) {
+    const void* lb = bias ? static_cast<const uint8_t*>(bias) + s->first * dtype_size(bias_t) : nullptr;
+    TQ4_TRY(run_matmul(*s->local, a, m, a_t, lb, bias_t, s->part.ptr, y_t, s->share, st));
+  }
+  // rows of a short (or empty) shard beyond `count` are never read back: no clearing needed
+  void* dst = direct ? y : s->gather.ptr;
+  ncclResult_t r = api->AllGather(s->part.ptr, dst, (size_t)(m * s->share), nccl_type(y_t),
+                                  s->comm->comm, st);
+  if (r == ncclInProgress) {
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::seconds(60);
+    TQ4_TRY(nccl_wait(api, s->comm->comm, deadline, "ncclAllGather"));
+  } else if (r != ncclSuccess) {
+    s->comm->broken = true;
+    set_error("ncclAllGather: %s", api->GetErrorString(r));
+    return TQ4_ERR_NCCL;
+  }
+  if (!direct) {
+    const int64_t total = m * s->desc.N;
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+    switch (y_t) {
+      case TQ4_F32:
+        unshard_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(s->gather.ptr), m, s->share, (int)P, s->desc.N, static_cast<float*>(y));
+        break;
+      default:
+        unshard_kernel<uint16_t><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(s->gather.ptr), m, s->share, (int)P, s->desc.N, static_cast<uint16_t*>(y));
+        break;
+    }
+    TQ4_CUDA(cudaGetLastError());
+  }
+  return TQ4_OK;
+}
+
+tq4_status tq4_sharded_destroy(tq4_sharded* s) {
+  if (!s) return TQ4_OK;
+  if (s->local) tq4_weight_destroy(s->local);
+  s->part.release();
+  s->gather.release();
+  delete s;
+  return TQ4_OK;
+}
+
+}  // extern "C"
