@@ -171,6 +171,7 @@ tq4_status tq4_weight_create(const tq4_weight_desc* d, const void* b, int64_t b_
   if (st == TQ4_OK) st = w->scales.alloc(w->n_pad * w->blocks_pad * tsz);
   if (st == TQ4_OK && d->zp_kind != TQ4_ZP_NONE) st = w->zps.alloc(w->n_pad * w->blocks_pad * tsz);
   if (st == TQ4_OK) st = prepare_weight(*w, b, scales, zp);
+  if (st == TQ4_OK) st = make_weight_maps(*w);
   cudaSetDevice(prev);
   if (st != TQ4_OK) {
     tq4_weight_destroy(w);

@@ -10,13 +10,14 @@
 // the segment's max |a| so that a' cannot overflow f16). The per-element work is one LOP3 and
 // one f16x2/bf16x2 op per two weights; zero points and scales are applied once per segment.
 //
-// Work split: a CTA of 8 warps owns 16*WN weight rows and a K range of whole 64-byte groups;
-// each warp owns 16 rows (mma.sync m16n8k16, weights as the A operand) and every WK-th group of
-// the range (WK = 8/WN). Activations, per-segment factors and the CTA's scales / zero points are
-// staged once in shared memory; the packed weights stream from HBM with 128-bit non-allocating
-// loads, two groups ahead. Warps that share rows reduce through shared memory; CTAs that share
-// rows (split-K) reduce through a float workspace, the last CTA of a row tile doing the sum in a
-// fixed order (deterministic) and resetting its counter.
+// Work split: a tile is 16*WN weight rows x a K range of whole 64-byte groups; persistent CTAs
+// of 8 warps walk the tiles. Each warp owns 16 rows of the tile (mma.sync m16n8k16, weights as
+// the A operand) and every WK-th group of the range (WK = 8/WN). Activations and per-segment
+// factors are staged in shared memory once per K range; each tile's scales / zero points arrive
+// by cp.async while its first weights are in flight; the packed weights stream from HBM with
+// 128-bit non-allocating loads, two groups ahead. Warps that share rows reduce through shared
+// memory; tiles that share rows (split-K) reduce through a float workspace, the last CTA of a
+// row tile doing the sum in a fixed order (deterministic) and resetting its counter.
 #include <map>
 #include <memory>
 #include <mutex>
@@ -45,6 +46,7 @@ struct GemvArgs {
   int groups_per_split;  // CTA K range in groups
   int wn;                // warps along N: 1, 2, 4 or 8
   int ksplit;
+  int ctas_n;            // row tiles; the persistent grid walks ctas_n * ksplit tiles
   int64_t n_pad;
   float* ws;
   int* counters;
@@ -160,88 +162,75 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int w) {
 constexpr int kGemvThreads = 256;
 constexpr int kPrefetch = 2;  // groups per load batch (two batches in flight)
 
-template <int BITS, tq4_dtype AT, int ST_BYTES, int MT>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs p) {
-  constexpr bool BF = (AT == TQ4_BF16);
-  constexpr int G = 512 / BITS;  // elements per 64-byte group
-  constexpr int STEPS = G / 16;
-  constexpr int STEPS_PER_WORD = 32 / BITS / 4;  // 2 (4-bit), 4 (2-bit), 1 (8-bit)
-  constexpr int MP = 8 * MT;
-  extern __shared__ __align__(16) uint8_t smem[];
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const int wn = p.wn, wk = 8 / wn;
-  const int warp_n = warp % wn, warp_k = warp / wn;
-  const int rows_cta = 16 * wn;
-  const int64_t cta_row0 = (int64_t)blockIdx.x * rows_cta;
-  const int64_t row0 = cta_row0 + warp_n * 16;
-  const int split = blockIdx.y;
-  const int g_begin = split * p.groups_per_split;
-  const int g_end = min(p.groups, g_begin + p.groups_per_split);
-  const int kr = (g_end - g_begin) * G;
-  const int k0 = g_begin * G;
-  const int seg_log2 = p.seg_log2;
-  const int seg = 1 << seg_log2;
-  const int nseg = kr >> seg_log2;
-  const int sk = kr + 16;
-  const int b_first = k0 >> p.bs_log2;
-  const int nblk = ((k0 + kr - 1) >> p.bs_log2) - b_first + 1;
-  const bool has_zp = p.zps != nullptr;
-
-  uint16_t* act = reinterpret_cast<uint16_t*>(smem);
-  float* segE = reinterpret_cast<float*>(smem + (size_t)MP * sk * 2);
-  float* segZA = segE + MP * nseg;
-  float* sc = segZA + MP * nseg;                       // [rows_cta][nblk] as f32
-  float* zc = sc + rows_cta * nblk;                    // same (if zero points)
-
-  // -- issue the first weight loads before staging (they overlap the staging latency)
-  const uint8_t* rowg = p.q + (row0 + g) * p.row_bytes + t * 16;
-  const uint8_t* rowg8 = rowg + 8 * p.row_bytes;
-  uint4 xa[kPrefetch], xb[kPrefetch];     // the batch being computed
-  uint4 na[kPrefetch], nb[kPrefetch];     // the next batch, in flight
-  const int c_first = g_begin + warp_k;
+// Four consecutive activations A[m][k..k+3] as f32 (zeros past K). `vec` when a 4-wide load is
+// aligned (K % 4 == 0).
+template <tq4_dtype AT>
+__device__ __forceinline__ void load_act4(const void* a, int64_t m, int64_t k, int K, bool vec,
+                                          float (&out)[4]) {
+  const int64_t i = m * K + k;
+  if (vec && k + 3 < K) {
+    if constexpr (AT == TQ4_F32) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a) + i));
+      out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
+    } else {
+      const uint2 v = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(a) + i));
+      const uint32_t h[4] = {v.x & 0xFFFF, v.x >> 16, v.y & 0xFFFF, v.y >> 16};
 #pragma unroll
-  for (int d = 0; d < kPrefetch; ++d) {
-    const int c = c_first + d * wk;
-    xa[d] = xb[d] = make_uint4(0, 0, 0, 0);
-    if (c < g_end) {
-      xa[d] = ld_stream(rowg + (int64_t)c * 64);
-      xb[d] = ld_stream(rowg8 + (int64_t)c * 64);
+      for (int e = 0; e < 4; ++e)
+        out[e] = (AT == TQ4_BF16) ? __uint_as_float(h[e] << 16) : __half2float(__ushort_as_half((uint16_t)h[e]));
     }
+    return;
   }
-
-  // -- stage the CTA's scales and zero points (as f32)
-  for (int i = threadIdx.x; i < rows_cta * nblk; i += kGemvThreads) {
-    const int r = i / nblk, bb = i % nblk;
-    const int64_t src = (cta_row0 + r) * p.blocks_pad + b_first + bb;
-    sc[i] = scale_to_f32(p.scales, src, ST_BYTES, p.st_bf16);
-    if (has_zp) zc[i] = scale_to_f32(p.zps, src, ST_BYTES, p.st_bf16);
-  }
-
-  // -- stage the activations: a' = A/E in the MMA type, per-segment E and E*sum(a')
-  {
-    const int vec_per_row = kr / 4;
-    const int total_vec = MP * vec_per_row;  // a multiple of 32: whole warps iterate together
-    const int L = seg >> 2;                  // lanes per segment (<= 32)
-    for (int v = threadIdx.x; v < total_vec; v += kGemvThreads) {
-      const int m = v / vec_per_row;
-      const int kk = (v % vec_per_row) * 4;
-      const int64_t k = (int64_t)k0 + kk;
-      float a4[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        a4[i] = 0.f;
-        if (m < p.M && k + i < p.K) a4[i] = load_as_f32(p.a, (int64_t)m * p.K + k + i, AT);
+  for (int e = 0; e < 4; ++e) out[e] = (k + e < K) ? load_as_f32(a, i + e, AT) : 0.f;
+}
+
+// Stages A[0:M][k0 : k0+kr] into shared memory as the MMA type (a' = A / E), with the
+// per-segment factors E and E * sum(a'). Rows >= M are left as they are: their outputs are
+// never stored, and an MMA output element depends only on its own activation row.
+template <tq4_dtype AT>
+__device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int kr, int sk,
+                                                  int nseg, uint16_t* act, float* segE,
+                                                  float* segZA) {
+  constexpr bool BF = (AT == TQ4_BF16);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int vec_per_row = kr / 4;
+  const int total = p.M * vec_per_row;
+  const int total_pad = (total + 31) & ~31;  // whole warps take part in the shuffles
+  const int L = (1 << p.seg_log2) >> 2;      // lanes per segment (<= 32)
+  const bool vec = (p.K & 3) == 0;
+  for (int base = 0; base < total_pad; base += 4 * kGemvThreads) {
+    float a4[4][4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {  // issue all loads first
+      const int v = base + u * kGemvThreads + threadIdx.x;
+      if (v < total) {
+        load_act4<AT>(p.a, v / vec_per_row, (int64_t)k0 + (v % vec_per_row) * 4, p.K, vec, a4[u]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) a4[u][e] = 0.f;
       }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (base + u * kGemvThreads + warp * 32 >= total_pad) continue;  // warp-uniform
+      const int v = base + u * kGemvThreads + threadIdx.x;
+      const int m = v / vec_per_row, kk = (v % vec_per_row) * 4;
       float e_scale = 1.f, inv = 1.f;
       if constexpr (AT == TQ4_F32) {
-        float mx = fmaxf(fmaxf(fabsf(a4[0]), fabsf(a4[1])), fmaxf(fabsf(a4[2]), fabsf(a4[3])));
+        float mx = fmaxf(fmaxf(fabsf(a4[u][0]), fabsf(a4[u][1])), fmaxf(fabsf(a4[u][2]), fabsf(a4[u][3])));
         for (int off = 1; off < L; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
         if (mx > 0.f && mx <= 3.402823466e38f) {
           int ex;
-          frexpf(mx, &ex);  // mx = f * 2^ex, f in [0.5, 1)
-          const int s = max(-126, min(127, ex - 15));  // mx / 2^s in [2^14, 2^15)
+          frexpf(mx, &ex);                                // mx = f * 2^ex, f in [0.5, 1)
+          const int s = max(-126, min(127, ex - 15));     // mx / 2^s in [2^14, 2^15)
           e_scale = ldexpf(1.f, s);
           inv = ldexpf(1.f, -s);
         }
@@ -249,172 +238,276 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs p) {
       uint16_t h[4];
       float sum = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int e = 0; e < 4; ++e) {
         if constexpr (BF) {
-          const __nv_bfloat16 b = __float2bfloat16_rn(a4[i] * inv);
-          h[i] = __bfloat16_as_ushort(b);
+          const __nv_bfloat16 b = __float2bfloat16_rn(a4[u][e] * inv);
+          h[e] = __bfloat16_as_ushort(b);
           sum += __bfloat162float(b);
         } else {
-          const __half b = __float2half_rn(a4[i] * inv);
-          h[i] = __half_as_ushort(b);
+          const __half b = __float2half_rn(a4[u][e] * inv);
+          h[e] = __half_as_ushort(b);
           sum += __half2float(b);
         }
       }
       for (int off = 1; off < L; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-      uint2 packed;
-      packed.x = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
-      packed.y = (uint32_t)h[2] | ((uint32_t)h[3] << 16);
-      *reinterpret_cast<uint2*>(act + m * sk + kk) = packed;
-      if ((lane & (L - 1)) == 0) {
-        const int s_idx = kk >> seg_log2;
-        segE[m * nseg + s_idx] = e_scale;
-        segZA[m * nseg + s_idx] = e_scale * sum;
+      if (v < total) {
+        uint2 packed;
+        packed.x = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
+        packed.y = (uint32_t)h[2] | ((uint32_t)h[3] << 16);
+        *reinterpret_cast<uint2*>(act + m * sk + kk) = packed;
+        if ((lane & (L - 1)) == 0) {
+          const int s_idx = kk >> p.seg_log2;
+          segE[m * nseg + s_idx] = e_scale;
+          segZA[m * nseg + s_idx] = e_scale * sum;
+        }
       }
     }
   }
-  __syncthreads();
+}
 
-  // -- main loop: this warp's groups c = c_first + i*wk, batches of kPrefetch, two in flight
-  float acc[MT][4];
-  float blk[MT][4];
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) acc[mt][i] = blk[mt][i] = 0.f;
+// Shared-memory plan of one CTA (identical on host and device).
+struct GemvSmem {
+  int sk, nseg, nblk_max, sc_pitch;  // sc_pitch: bytes per row of the staged scales
+  int act_off, segE_off, segZA_off, sc_off, zc_off, red_off, total;
+};
 
-  const int rl_g = warp_n * 16 + g;  // row of this thread's weights within the CTA
-  for (int cb = c_first; cb < g_end; cb += kPrefetch * wk) {
-    // issue the next batch before computing this one
-    const int cn = cb + kPrefetch * wk;
+__host__ __device__ inline GemvSmem gemv_smem_plan(int mt, int kr_max, int seg, int bs, int rows_cta,
+                                                   int st_bytes, bool zp) {
+  GemvSmem s{};
+  const int mp = 8 * mt;
+  s.sk = kr_max + 16;
+  s.nseg = kr_max / seg;
+  s.nblk_max = (kr_max + bs - 1) / bs + 1;
+  s.sc_pitch = ((s.nblk_max * st_bytes + 15) / 16 + 1) * 16;  // room to align the copy to 16 B
+  s.act_off = 0;
+  s.segE_off = s.act_off + mp * s.sk * 2;
+  s.segZA_off = s.segE_off + mp * s.nseg * 4;
+  s.sc_off = (s.segZA_off + mp * s.nseg * 4 + 15) / 16 * 16;
+  s.zc_off = s.sc_off + rows_cta * s.sc_pitch;
+  s.red_off = s.zc_off + (zp ? rows_cta * s.sc_pitch : 0);
+  s.total = s.red_off + 8 * 32 * mt * 4 * 4;
+  return s;
+}
+
+template <int BITS, tq4_dtype AT, int ST_BYTES, int MT>
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs p) {
+  constexpr bool BF = (AT == TQ4_BF16);
+  constexpr int G = 512 / BITS;  // elements per 64-byte group
+  constexpr int STEPS = G / 16;
+  constexpr int STEPS_PER_WORD = 32 / BITS / 4;  // 2 (4-bit), 4 (2-bit), 1 (8-bit)
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ int s_last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int wn = p.wn, wk = 8 / wn;
+  const int warp_n = warp % wn, warp_k = warp / wn;
+  const int rows_cta = 16 * wn;
+  const int seg_log2 = p.seg_log2;
+  const int seg = 1 << seg_log2;
+  const bool has_zp = p.zps != nullptr;
+  const GemvSmem L = gemv_smem_plan(MT, p.groups_per_split * G, seg, 1 << p.bs_log2, rows_cta,
+                                    ST_BYTES, has_zp);
+  uint16_t* act = reinterpret_cast<uint16_t*>(smem + L.act_off);
+  float* segE = reinterpret_cast<float*>(smem + L.segE_off);
+  float* segZA = reinterpret_cast<float*>(smem + L.segZA_off);
+  uint8_t* sc = smem + L.sc_off;
+  uint8_t* zc = smem + L.zc_off;
+  float* red = reinterpret_cast<float*>(smem + L.red_off);
+  const int sk = L.sk, nseg = L.nseg;
+
+  const int tiles = p.ctas_n * p.ksplit;
+  int staged_split = -1;
+  for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const int split = tile / p.ctas_n, rt = tile % p.ctas_n;
+    const int64_t cta_row0 = (int64_t)rt * rows_cta;
+    const int64_t row0 = cta_row0 + warp_n * 16;
+    const int g_begin = split * p.groups_per_split;
+    const int g_end = min(p.groups, g_begin + p.groups_per_split);
+    const int kr = (g_end - g_begin) * G;
+    const int k0 = g_begin * G;
+    const int b_first = k0 >> p.bs_log2;
+    const int nblk = ((k0 + kr - 1) >> p.bs_log2) - b_first + 1;
+
+    // -- scales / zero points of this tile: 16-byte cp.async over the aligned span of each row
+    const int64_t span_lo = ((int64_t)b_first * ST_BYTES) & ~15LL;
+    const int64_t span_hi = (((int64_t)(b_first + nblk) * ST_BYTES) + 15) & ~15LL;
+    const int c16 = (int)((span_hi - span_lo) >> 4);
+    const int sc_shift = (int)(((int64_t)b_first * ST_BYTES - span_lo) / ST_BYTES);  // entries
+    for (int i = threadIdx.x; i < rows_cta * c16; i += kGemvThreads) {
+      const int r = i / c16, c = i % c16;
+      const int64_t src = (cta_row0 + r) * p.blocks_pad * ST_BYTES + span_lo + c * 16;
+      cp_async16(sc + r * L.sc_pitch + c * 16, static_cast<const uint8_t*>(p.scales) + src);
+      if (has_zp) cp_async16(zc + r * L.sc_pitch + c * 16, static_cast<const uint8_t*>(p.zps) + src);
+    }
+
+    // -- the first weight batch
+    const uint8_t* rowg = p.q + (row0 + g) * p.row_bytes + t * 16;
+    const uint8_t* rowg8 = rowg + 8 * p.row_bytes;
+    uint4 xa[kPrefetch], xb[kPrefetch];  // the batch being computed
+    uint4 na[kPrefetch], nb[kPrefetch];  // the next batch, in flight
+    const int c_first = g_begin + warp_k;
 #pragma unroll
     for (int d = 0; d < kPrefetch; ++d) {
-      const int c = cn + d * wk;
-      na[d] = nb[d] = make_uint4(0, 0, 0, 0);
+      const int c = c_first + d * wk;
+      xa[d] = xb[d] = make_uint4(0, 0, 0, 0);
       if (c < g_end) {
-        na[d] = ld_stream(rowg + (int64_t)c * 64);
-        nb[d] = ld_stream(rowg8 + (int64_t)c * 64);
+        xa[d] = ld_stream(rowg + (int64_t)c * 64);
+        xb[d] = ld_stream(rowg8 + (int64_t)c * 64);
       }
     }
-#pragma unroll
-    for (int d = 0; d < kPrefetch; ++d) {
-      const int c = cb + d * wk;
-      if (c >= g_end) break;
-      const int kc = (c - g_begin) * G;  // group's first element within the CTA range
-#pragma unroll
-      for (int j = 0; j < STEPS; ++j) {
-        const int w = j / STEPS_PER_WORD;
-        uint32_t a0, a1, a2, a3;
-        weight_pairs<BITS, BF>(word_of(xa[d], w), j, a0, a2);
-        weight_pairs<BITS, BF>(word_of(xb[d], w), j, a1, a3);
-        const int kk = kc + 16 * j + 4 * t;
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          const uint2 bv = *reinterpret_cast<const uint2*>(act + (mt * 8 + g) * sk + kk);
-          mma16816<BF>(blk[mt], a0, a1, a2, a3, bv.x, bv.y);
-        }
-        if ((((j + 1) * 16) & (seg - 1)) == 0) {  // end of a segment
-          const int s_idx = (kc + (j + 1) * 16 - seg) >> seg_log2;
-          const int bb = ((k0 + s_idx * seg) >> p.bs_log2) - b_first;
-          const float s_g = sc[rl_g * nblk + bb], s_g8 = sc[(rl_g + 8) * nblk + bb];
-          const float z_g = has_zp ? zc[rl_g * nblk + bb] : p.z_const;
-          const float z_g8 = has_zp ? zc[(rl_g + 8) * nblk + bb] : p.z_const;
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-            const int m0 = mt * 8 + 2 * t;
-            const float E0 = segE[m0 * nseg + s_idx], ZA0 = segZA[m0 * nseg + s_idx];
-            const float E1 = segE[(m0 + 1) * nseg + s_idx], ZA1 = segZA[(m0 + 1) * nseg + s_idx];
-            acc[mt][0] = fmaf(s_g, fmaf(E0, blk[mt][0], -z_g * ZA0), acc[mt][0]);
-            acc[mt][1] = fmaf(s_g, fmaf(E1, blk[mt][1], -z_g * ZA1), acc[mt][1]);
-            acc[mt][2] = fmaf(s_g8, fmaf(E0, blk[mt][2], -z_g8 * ZA0), acc[mt][2]);
-            acc[mt][3] = fmaf(s_g8, fmaf(E1, blk[mt][3], -z_g8 * ZA1), acc[mt][3]);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) blk[mt][i] = 0.f;
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int d = 0; d < kPrefetch; ++d) {
-      xa[d] = na[d];
-      xb[d] = nb[d];
-    }
-  }
 
-  // -- reduce the warps that share rows (fixed order)
-  __syncthreads();  // all warps are done with the staged data
-  float* red = reinterpret_cast<float*>(smem);  // [8 warps][32 lanes][MT*4]
-  if (wk > 1) {
-    if (warp_k > 0) {
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) red[(warp * 32 + lane) * (MT * 4) + mt * 4 + i] = acc[mt][i];
+    // -- activations, once per K range
+    if (split != staged_split) {
+      stage_activations<AT>(p, k0, kr, sk, nseg, act, segE, segZA);
+      staged_split = split;
     }
+    cp_async_wait_all();
     __syncthreads();
-    if (warp_k == 0) {
-      for (int kk = 1; kk < wk; ++kk) {
-        const int src = (kk * wn + warp_n) * 32 + lane;
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) acc[mt][i] += red[src * (MT * 4) + mt * 4 + i];
-      }
-    }
-  }
 
-  const int64_t n_g = row0 + g, n_g8 = row0 + g + 8;
-  if (p.ksplit == 1) {
-    if (warp_k == 0) {
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int m = mt * 8 + 2 * t + (i & 1);
-          const int64_t n = (i < 2) ? n_g : n_g8;
-          if (m < p.M && n < p.N) {
-            float v = acc[mt][i];
-            if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
-            store_from_f32(p.y, (int64_t)m * p.ldy + n, p.y_t, v);
-          }
-        }
-      }
-    }
-    return;
-  }
-
-  // -- split-K: write this CTA's partial, the last CTA of the row tile sums them in order
-  if (warp_k == 0) {
+    // -- main loop over this warp's groups
+    float acc[MT][4], blk[MT][4];
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int m = mt * 8 + 2 * t + (i & 1);
-        const int64_t n = (i < 2) ? n_g : n_g8;
-        if (m < p.M) p.ws[((int64_t)split * p.M + m) * p.n_pad + n] = acc[mt][i];
+      for (int i = 0; i < 4; ++i) acc[mt][i] = blk[mt][i] = 0.f;
+    const int rl_g = warp_n * 16 + g;
+    const uint8_t* sc_g = sc + rl_g * L.sc_pitch;
+    const uint8_t* sc_g8 = sc + (rl_g + 8) * L.sc_pitch;
+    const uint8_t* zc_g = zc + rl_g * L.sc_pitch;
+    const uint8_t* zc_g8 = zc + (rl_g + 8) * L.sc_pitch;
+
+    for (int cb = c_first; cb < g_end; cb += kPrefetch * wk) {
+      const int cn = cb + kPrefetch * wk;
+#pragma unroll
+      for (int d = 0; d < kPrefetch; ++d) {
+        const int c = cn + d * wk;
+        na[d] = nb[d] = make_uint4(0, 0, 0, 0);
+        if (c < g_end) {
+          na[d] = ld_stream(rowg + (int64_t)c * 64);
+          nb[d] = ld_stream(rowg8 + (int64_t)c * 64);
+        }
       }
+#pragma unroll
+      for (int d = 0; d < kPrefetch; ++d) {
+        const int c = cb + d * wk;
+        if (c >= g_end) break;
+        const int kc = (c - g_begin) * G;
+#pragma unroll
+        for (int j = 0; j < STEPS; ++j) {
+          const int w = j / STEPS_PER_WORD;
+          uint32_t a0, a1, a2, a3;
+          weight_pairs<BITS, BF>(word_of(xa[d], w), j, a0, a2);
+          weight_pairs<BITS, BF>(word_of(xb[d], w), j, a1, a3);
+          const int kk = kc + 16 * j + 4 * t;
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const uint2 bv = *reinterpret_cast<const uint2*>(act + (mt * 8 + g) * sk + kk);
+            mma16816<BF>(blk[mt], a0, a1, a2, a3, bv.x, bv.y);
+          }
+          if ((((j + 1) * 16) & (seg - 1)) == 0) {  // end of a segment
+            const int s_idx = (kc + (j + 1) * 16 - seg) >> seg_log2;
+            const int bb = ((k0 + s_idx * seg) >> p.bs_log2) - b_first + sc_shift;
+            const float s_g = scale_to_f32(sc_g, bb, ST_BYTES, p.st_bf16);
+            const float s_g8 = scale_to_f32(sc_g8, bb, ST_BYTES, p.st_bf16);
+            const float z_g = has_zp ? scale_to_f32(zc_g, bb, ST_BYTES, p.st_bf16) : p.z_const;
+            const float z_g8 = has_zp ? scale_to_f32(zc_g8, bb, ST_BYTES, p.st_bf16) : p.z_const;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+              const int m0 = mt * 8 + 2 * t;
+              const float E0 = segE[m0 * nseg + s_idx], ZA0 = segZA[m0 * nseg + s_idx];
+              const float E1 = segE[(m0 + 1) * nseg + s_idx], ZA1 = segZA[(m0 + 1) * nseg + s_idx];
+              acc[mt][0] = fmaf(s_g, fmaf(E0, blk[mt][0], -z_g * ZA0), acc[mt][0]);
+              acc[mt][1] = fmaf(s_g, fmaf(E1, blk[mt][1], -z_g * ZA1), acc[mt][1]);
+              acc[mt][2] = fmaf(s_g8, fmaf(E0, blk[mt][2], -z_g8 * ZA0), acc[mt][2]);
+              acc[mt][3] = fmaf(s_g8, fmaf(E1, blk[mt][3], -z_g8 * ZA1), acc[mt][3]);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) blk[mt][i] = 0.f;
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int d = 0; d < kPrefetch; ++d) {
+        xa[d] = na[d];
+        xb[d] = nb[d];
+      }
+    }
+
+    // -- reduce the warps that share rows (fixed order)
+    if (wk > 1) {
+      if (warp_k > 0) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) red[(warp * 32 + lane) * (MT * 4) + mt * 4 + i] = acc[mt][i];
+      }
+      __syncthreads();
+      if (warp_k == 0) {
+        for (int kk = 1; kk < wk; ++kk) {
+          const int src = (kk * wn + warp_n) * 32 + lane;
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[mt][i] += red[src * (MT * 4) + mt * 4 + i];
+        }
+      }
+    }
+
+    const int64_t n_g = row0 + g, n_g8 = row0 + g + 8;
+    if (p.ksplit == 1) {
+      if (warp_k == 0) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int m = mt * 8 + 2 * t + (i & 1);
+            const int64_t n = (i < 2) ? n_g : n_g8;
+            if (m < p.M && n < p.N) {
+              float v = acc[mt][i];
+              if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
+              store_from_f32(p.y, (int64_t)m * p.ldy + n, p.y_t, v);
+            }
+          }
+        }
+      }
+    } else {
+      // split-K: write this tile's partial; the last CTA of the row tile sums them in order
+      if (warp_k == 0) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int m = mt * 8 + 2 * t + (i & 1);
+            const int64_t n = (i < 2) ? n_g : n_g8;
+            if (m < p.M) p.ws[((int64_t)split * p.M + m) * p.n_pad + n] = acc[mt][i];
+          }
+      }
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        const int prev = atomicAdd(&p.counters[rt], 1);
+        s_last = (prev == p.ksplit - 1);
+        if (prev >= p.ksplit) report(kDevTimeoutSplitK);  // a counter left non-zero earlier
+      }
+      __syncthreads();
+      if (s_last) {
+        __threadfence();
+        const int outputs = rows_cta * p.M;
+        for (int i = threadIdx.x; i < outputs; i += kGemvThreads) {
+          const int m = i / rows_cta;
+          const int64_t n = cta_row0 + (i % rows_cta);
+          if (n >= p.N) continue;
+          float v = 0.f;
+          for (int s = 0; s < p.ksplit; ++s) v += __ldcg(&p.ws[((int64_t)s * p.M + m) * p.n_pad + n]);
+          if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
+          store_from_f32(p.y, (int64_t)m * p.ldy + n, p.y_t, v);
+        }
+        if (threadIdx.x == 0) p.counters[rt] = 0;
+      }
+    }
+    __syncthreads();  // the tile's shared data (scales, reduction) is free again
   }
-  __threadfence();
-  __syncthreads();
-  __shared__ int s_last;
-  if (threadIdx.x == 0) {
-    const int prev = atomicAdd(&p.counters[blockIdx.x], 1);
-    s_last = (prev == p.ksplit - 1);
-    if (prev >= p.ksplit) report(kDevTimeoutSplitK);  // a counter left non-zero by a failed call
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  const int outputs = rows_cta * p.M;
-  for (int i = threadIdx.x; i < outputs; i += kGemvThreads) {
-    const int m = i / rows_cta;
-    const int64_t n = cta_row0 + (i % rows_cta);
-    if (n >= p.N) continue;
-    float v = 0.f;
-    for (int s = 0; s < p.ksplit; ++s) v += __ldcg(&p.ws[((int64_t)s * p.M + m) * p.n_pad + n]);
-    if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
-    store_from_f32(p.y, (int64_t)m * p.ldy + n, p.y_t, v);
-  }
-  if (threadIdx.x == 0) p.counters[blockIdx.x] = 0;
 }
 
 // ---- host side --------------------------------------------------------------------------------
@@ -422,14 +515,6 @@ struct GemvPlan {
   int wn, ksplit, groups_per_split, mt, ctas_n;
   size_t smem;
 };
-
-static size_t gemv_smem(int mt, int kr, int seg, int rows_cta, int nblk, bool zp) {
-  const int mp = 8 * mt;
-  size_t bytes = (size_t)mp * (kr + 16) * 2 + (size_t)2 * mp * (kr / seg) * 4 +
-                 (size_t)rows_cta * nblk * 4 * (zp ? 2 : 1);
-  const size_t red = (size_t)8 * 32 * mt * 4 * 4;
-  return std::max(bytes, red);
-}
 
 static GemvPlan plan_gemv(const Weight& w, int64_t m) {
   GemvPlan pl{};
@@ -453,54 +538,60 @@ static GemvPlan plan_gemv(const Weight& w, int64_t m) {
   int ksplit = 1;
   if (pl.ctas_n < target) ksplit = (int)std::min<int64_t>((target + pl.ctas_n - 1) / pl.ctas_n,
                                                          std::max<int64_t>(1, groups / wk));
-  // shared-memory budget: shrink the per-CTA K range until the staging fits
   const size_t budget = 100 * 1024;
   const bool zp = w.zps.ptr != nullptr;
+  const int st_bytes = w.desc.dequant_dtype == TQ4_F32 ? 4 : 2;
   const int rows_cta = 16 * pl.wn;
   for (;;) {
     const int gps = (int)((groups + ksplit - 1) / ksplit);
-    const int kr = gps * G;
-    const int nblk = (kr + w.desc.block_size - 1) / w.desc.block_size + 1;
-    const size_t smem = gemv_smem(pl.mt, kr, seg, rows_cta, nblk, zp);
-    if (smem <= budget || gps == 1) {
+    const GemvSmem s = gemv_smem_plan(pl.mt, gps * G, seg, w.desc.block_size, rows_cta, st_bytes, zp);
+    if ((size_t)s.total <= budget || gps == 1) {
       pl.groups_per_split = gps;
-      pl.smem = smem;
+      pl.smem = s.total;
       break;
     }
     ++ksplit;
   }
-  // every split must own at least one group
   pl.ksplit = (int)((groups + pl.groups_per_split - 1) / pl.groups_per_split);
   return pl;
 }
 
 template <int BITS, tq4_dtype AT, int ST, int MT>
-static cudaError_t launch_gemv_t(const GemvArgs& args, dim3 grid, size_t smem, cudaStream_t st) {
+static cudaError_t launch_gemv_t(const GemvArgs& args, int tiles, int sms, size_t smem, cudaStream_t st) {
   auto kern = gemv_kernel<BITS, AT, ST, MT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
+  // attribute and occupancy once per instantiation (the shared-memory budget is fixed)
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024 + 1024);
+    if (e != cudaSuccess) return e;
+    int n = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kGemvThreads, 100 * 1024);
+    if (e != cudaSuccess) return e;
+    per_sm = std::max(1, n);
+  }
+  const int grid = std::min(tiles, per_sm * sms);
   kern<<<grid, kGemvThreads, smem, st>>>(args);
   return cudaGetLastError();
 }
 
 template <int BITS, tq4_dtype AT>
-static cudaError_t launch_gemv_st(const GemvArgs& args, int st_bytes, int mt, dim3 grid, size_t smem,
-                                  cudaStream_t st) {
+static cudaError_t launch_gemv_st(const GemvArgs& args, int st_bytes, int mt, int tiles, int sms,
+                                  size_t smem, cudaStream_t st) {
   if (st_bytes == 4) {
-    return mt == 1 ? launch_gemv_t<BITS, AT, 4, 1>(args, grid, smem, st)
-                   : launch_gemv_t<BITS, AT, 4, 2>(args, grid, smem, st);
+    return mt == 1 ? launch_gemv_t<BITS, AT, 4, 1>(args, tiles, sms, smem, st)
+                   : launch_gemv_t<BITS, AT, 4, 2>(args, tiles, sms, smem, st);
   }
-  return mt == 1 ? launch_gemv_t<BITS, AT, 2, 1>(args, grid, smem, st)
-                 : launch_gemv_t<BITS, AT, 2, 2>(args, grid, smem, st);
+  return mt == 1 ? launch_gemv_t<BITS, AT, 2, 1>(args, tiles, sms, smem, st)
+                 : launch_gemv_t<BITS, AT, 2, 2>(args, tiles, sms, smem, st);
 }
 
 template <int BITS>
 static cudaError_t launch_gemv_bits(const GemvArgs& args, tq4_dtype a_t, int st_bytes, int mt,
-                                    dim3 grid, size_t smem, cudaStream_t st) {
+                                    int tiles, int sms, size_t smem, cudaStream_t st) {
   switch (a_t) {
-    case TQ4_F16: return launch_gemv_st<BITS, TQ4_F16>(args, st_bytes, mt, grid, smem, st);
-    case TQ4_BF16: return launch_gemv_st<BITS, TQ4_BF16>(args, st_bytes, mt, grid, smem, st);
-    default: return launch_gemv_st<BITS, TQ4_F32>(args, st_bytes, mt, grid, smem, st);
+    case TQ4_F16: return launch_gemv_st<BITS, TQ4_F16>(args, st_bytes, mt, tiles, sms, smem, st);
+    case TQ4_BF16: return launch_gemv_st<BITS, TQ4_BF16>(args, st_bytes, mt, tiles, sms, smem, st);
+    default: return launch_gemv_st<BITS, TQ4_F32>(args, st_bytes, mt, tiles, sms, smem, st);
   }
 }
 
@@ -514,9 +605,10 @@ struct WorkspaceMap {
   std::map<cudaStream_t, std::unique_ptr<Workspace>> by_stream;
 };
 
+static std::mutex g_ws_create_mu;
+
 static WorkspaceMap& workspaces(const Weight& w) {
-  static std::mutex create_mu;
-  std::lock_guard<std::mutex> lock(create_mu);
+  std::lock_guard<std::mutex> lock(g_ws_create_mu);
   Weight& mw = const_cast<Weight&>(w);
   if (!mw.ws_mutex) mw.ws_mutex = new WorkspaceMap();
   return *static_cast<WorkspaceMap*>(mw.ws_mutex);
@@ -544,8 +636,8 @@ tq4_status gemv_workspace(const Weight& w, cudaStream_t st, int64_t ws_bytes, in
 }
 
 tq4_status run_gemv_with(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,
-                         tq4_dtype bias_t, void* y, tq4_dtype y_t, int64_t ldy, cudaStream_t st, float* ws,
-                         int* counters, int64_t ws_capacity_floats, int64_t ctr_capacity) {
+                         tq4_dtype bias_t, void* y, tq4_dtype y_t, int64_t ldy, cudaStream_t st,
+                         float* ws, int* counters, int64_t ws_capacity_floats, int64_t ctr_capacity) {
   const GemvPlan pl = plan_gemv(w, m);
   GemvArgs args{};
   args.q = static_cast<const uint8_t*>(w.q.ptr);
@@ -574,6 +666,7 @@ tq4_status run_gemv_with(const Weight& w, const void* a, int64_t m, tq4_dtype a_
   args.groups_per_split = pl.groups_per_split;
   args.wn = pl.wn;
   args.ksplit = pl.ksplit;
+  args.ctas_n = pl.ctas_n;
   args.n_pad = w.n_pad;
   if (pl.ksplit > 1) {
     const int64_t need = (int64_t)pl.ksplit * m * w.n_pad;
@@ -585,12 +678,12 @@ tq4_status run_gemv_with(const Weight& w, const void* a, int64_t m, tq4_dtype a_
     args.ws = ws;
     args.counters = counters;
   }
-  const dim3 grid(pl.ctas_n, pl.ksplit);
+  const int tiles = pl.ctas_n * pl.ksplit;
   const int st_bytes = w.desc.dequant_dtype == TQ4_F32 ? 4 : 2;
   cudaError_t e;
-  if (w.desc.bits == 4) e = launch_gemv_bits<4>(args, a_t, st_bytes, pl.mt, grid, pl.smem, st);
-  else if (w.desc.bits == 2) e = launch_gemv_bits<2>(args, a_t, st_bytes, pl.mt, grid, pl.smem, st);
-  else e = launch_gemv_bits<8>(args, a_t, st_bytes, pl.mt, grid, pl.smem, st);
+  if (w.desc.bits == 4) e = launch_gemv_bits<4>(args, a_t, st_bytes, pl.mt, tiles, w.num_sms, pl.smem, st);
+  else if (w.desc.bits == 2) e = launch_gemv_bits<2>(args, a_t, st_bytes, pl.mt, tiles, w.num_sms, pl.smem, st);
+  else e = launch_gemv_bits<8>(args, a_t, st_bytes, pl.mt, tiles, w.num_sms, pl.smem, st);
   if (e != cudaSuccess) {
     set_error("GEMV launch failed: %s", cudaGetErrorString(e));
     return TQ4_ERR_CUDA;

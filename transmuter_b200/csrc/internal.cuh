@@ -99,12 +99,16 @@ struct tq4_weight {
   int num_sms = 148;
   // split-K workspaces of the GEMV, one per CUDA stream (a tq4::WorkspaceMap, made on first use)
   void* ws_mutex = nullptr;
+  // TMA descriptors of the packed rows for the GEMM's tile widths (128, 96, 64), made at creation
+  alignas(64) CUtensorMap wmaps[3];
+  bool wmaps_ok = false;
 };
 
 namespace tq4 {
 using Weight = tq4_weight;
 
 tq4_status prepare_weight(Weight& w, const void* b, const void* scales, const void* zp);
+tq4_status make_weight_maps(Weight& w);
 tq4_status run_dequant(const Weight& w, const int64_t* rows, int64_t n_out, void* out, cudaStream_t st);
 // Y rows have a stride of `ldy` elements (N for a dense Y; the shard width for a sharded call).
 tq4_status run_gemv(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,
