@@ -94,6 +94,18 @@ tq4_status tq4_matmul(const tq4_weight* w, const void* a, int64_t m, tq4_dtype a
                       const void* bias, tq4_dtype bias_dtype, void* y, tq4_dtype y_dtype,
                       void* stream);
 
+/* tq4_matmul for M <= 16 that allocates no device memory. No counterpart in the reference: it
+ * serves callers that cannot call cudaMalloc, such as a NIF sharing the GPU with EXLA's client
+ * (which reserves most device memory up front) or a decode loop that must not risk the device
+ * synchronization of cudaMalloc/cudaFree. Its split-K scratch is a static 2 MiB device array
+ * (plus 64 KiB of counters) that every GPU loading the library holds until exit; a call that
+ * would need more is rejected with TQ4_ERR_INVALID_ARGUMENT, and M > 16 with
+ * TQ4_ERR_UNSUPPORTED. The first call on a device looks up the array's device address (make it
+ * before any stream capture). Calls share the array: calls that overlap on the GPU race. */
+tq4_status tq4_matmul_noalloc(const tq4_weight* w, const void* a, int64_t m, tq4_dtype a_dtype,
+                              const void* bias, tq4_dtype bias_dtype, void* y, tq4_dtype y_dtype,
+                              void* stream);
+
 /* dequantize_weight/4 (quantized.ex:234-240) on the device: W[N, K] in desc.dequant_dtype,
  * bit-exact with the reference. `out` is a device pointer of N*K elements. */
 tq4_status tq4_dequantize(const tq4_weight* w, void* out, void* stream);

@@ -22,7 +22,7 @@ UNIQUE_ID_BYTES = 128
 # Every symbol include/tq4.h declares (the CPU tests check the library exports each one).
 EXPORTS = [
     "tq4_weight_input_sizes", "tq4_weight_create", "tq4_weight_destroy", "tq4_weight_info",
-    "tq4_matmul", "tq4_dequantize", "tq4_gather_rows", "tq4_device_status", "tq4_last_error",
+    "tq4_matmul", "tq4_matmul_noalloc", "tq4_dequantize", "tq4_gather_rows", "tq4_device_status", "tq4_last_error",
     "tq4_status_string", "tq4_comm_unique_id", "tq4_comm_create", "tq4_comm_destroy",
     "tq4_sharded_create", "tq4_sharded_rows", "tq4_sharded_matmul", "tq4_sharded_destroy",
 ]
@@ -66,6 +66,7 @@ def load():
             "tq4_weight_destroy": [vp],
             "tq4_weight_info": [vp, P(WeightDesc), P(i64)],
             "tq4_matmul": [vp, vp, i64, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int, vp],
+            "tq4_matmul_noalloc": [vp, vp, i64, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int, vp],
             "tq4_dequantize": [vp, vp, vp],
             "tq4_gather_rows": [vp, vp, i64, vp, vp],
             "tq4_device_status": [ctypes.c_int, P(i32)],

@@ -5,3 +5,4 @@
 #include "gemm.cu"
 #include "api.cu"
 #include "sharded.cu"
+#include "noalloc.cu"
