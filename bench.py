@@ -269,7 +269,7 @@ def main():
     # graph's stream is warmed first so no workspace is allocated during capture.
     gstream = torch.cuda.Stream(dev)
     with torch.cuda.stream(gstream):
-        for i in range(max(3, args.warmup)):
+        for i in range(max(3, args.warmup, copies)):  # every copy: its workspaces exist before capture
             step(i)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()

@@ -161,6 +161,33 @@ def test_gemv_parity(k, n, m, bits, bs, zp, st, at, t, bias):
     assert o.rel_l2(got, want) < TOL[at], o.rel_l2(got, want)
 
 
+@pytest.mark.parametrize("at,bs,bits,zp", [("f32", 128, 4, "none"), ("f32", 32, 4, "packed"), ("f16", 128, 4, "packed"),
+                                           ("bf16", 128, 4, "none"), ("f32", 64, 2, "none"), ("f32", 64, 8, "packed")])
+@pytest.mark.parametrize("kind", ["positive", "huge", "tiny", "mixed_rows"])
+def test_gemv_activation_extremes(at, bs, bits, zp, kind):
+    """All-positive activations (the magic-number offset does not cancel), huge and tiny
+    magnitudes (the per-segment power-of-two activation scale), and rows of very different size."""
+    k, n, m = 4096, 256, 5
+    cfg = workloads.Config(f"ext-{at}-{bs}-{bits}-{zp}", k, n, m, bits=bits, block_size=bs, zp=zp,
+                           scale_type="f32" if at == "f32" else at, a_type=at)
+    p = workloads.make(cfg)
+    r = np.random.default_rng(7)
+    a = r.random((m, k), dtype=np.float32) * 3.0  # positive
+    if kind == "huge":
+        a = (r.standard_normal((m, k)) * (1e3 if at == "f16" else 1e30)).astype(np.float32)
+    elif kind == "tiny":
+        a = (r.standard_normal((m, k)) * (1e-3 if at == "f16" else 1e-30)).astype(np.float32)
+    elif kind == "mixed_rows":
+        a = r.standard_normal((m, k)).astype(np.float32) * np.array([[1e-3], [1.0], [50.0], [1e-2], [7.0]], np.float32)
+    a = o.as_type(a, at) if at != "f32" else a
+    w = weight_for(cfg, p, cfg.scale_type)
+    y = as_np32(w.matmul(to_dev(np.asarray(a, np.float32) if at == "bf16" else a, at)))
+    wd = o.dequantize_weight(p["B"], p["scales"], p["zp"], k, n, bits, bs, cfg.scale_type)
+    want = np.asarray(a, np.float64) @ wd.astype(np.float64).T
+    for row in range(m):  # each row on its own scale
+        assert o.rel_l2(y[row], want[row]) < TOL[at], (row, o.rel_l2(y[row], want[row]))
+
+
 LARGE_M = [
     (1024, 3072, 17, 4, 32, "packed", "f16", "f16", "f16", False),
     (1024, 256, 64, 4, 32, "none", "f32", "f32", "f32", True),

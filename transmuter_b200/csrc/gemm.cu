@@ -3,14 +3,17 @@
 //
 //   Y[M, N] = A[M, K] . W^T,  W = (q - z) * s  (dequantize_weight/4, quantized.ex:234-240)
 //
-// CTA tile 128 (M) x BN (N), one 64-byte packed group (128 4-bit weights) of K per stage:
-//   warp 0   TMA producer: A tile (two 64-column boxes, 128B swizzle) and the packed W tile
-//            (BN rows x 64 bytes) into stage s, completing on full[s].
+// CTA tile 128 (M) x BN (N), one 64-byte packed group (128 4-bit weights) of K per stage, 2-4
+// stages (as many as fit shared memory):
+//   warp 0   TMA producer: A tile (two 64-column boxes, 128B swizzle), the packed W tile
+//            (BN rows x 64 bytes) and the stage's block-major scales / zero points (BN rows x
+//            the stage's blocks) into stage s, completing on full[s].
 //   warp 1   TMEM allocation, and one thread that issues tcgen05.mma (M=128, N=BN, K=16) x 8
 //            per stage into the f32 accumulator in TMEM; tcgen05.commit frees the stage.
-//   warps 2-5 dequantize the packed tile into the MMA operand (A's type; W = RN_T(RN_T(q-z)*s)
+//   warps 2-9 dequantize the packed tile into the MMA operand (A's type; W = RN_T(RN_T(q-z)*s)
 //            exactly as the reference when T is A's type) in the 128B-swizzled K-major layout,
-//            then run the epilogue: tcgen05.ld of their 32 TMEM lanes, bias, conversion, store.
+//            then run the epilogue: tcgen05.ld of their 32 TMEM lanes (warps w and w+4 split the
+//            columns), bias, conversion, vector stores.
 // Every mbarrier wait is bounded by a clock deadline; a wait that runs out writes the device
 // status word, raises the CTA's abort flag and the CTA winds down (no trap, no endless spin).
 #include "internal.cuh"
@@ -165,15 +168,18 @@ __device__ __forceinline__ uint32_t deq_pair(uint32_t qp, float z, float s) {
   }
 }
 
+
 struct GemmArgs {
-  const void* scales;  // [n_pad][blocks_pad] in T
-  const void* zps;     // same or null
-  int64_t blocks_pad;
   float z_const;
+  int has_zp;
   int bs_log2;
+  int nb;          // scale blocks per stage (the TMA box height)
   int M, N, K;
-  int64_t n_pad;
-  int ktiles;  // 64-byte groups per row
+  int ktiles;      // 64-byte groups per row
+  int stages;
+  int stage_bytes;
+  int sc_off, zc_off;  // offsets of the staged scales / zero points within a stage
+  int st_bytes;
   const void* bias;
   tq4_dtype bias_t;
   void* y;
@@ -181,45 +187,49 @@ struct GemmArgs {
   int64_t ldy;
 };
 
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;  // producer, MMA, 8 dequant / epilogue warps
 constexpr int BM = 128;
+constexpr int kMaxStages = 4;
 
-template <int BN, int STAGES>
-struct GemmSmem {
-  static constexpr int A_BYTES = BM * 128 * 2;         // 128 rows x 128 k x 2 B (two SW128 halves)
-  static constexpr int W16_BYTES = BN * 128 * 2;       // BN rows x 128 k x 2 B (two SW128 halves)
-  static constexpr int WP_BYTES = BN * 64;             // packed
-  static constexpr int STAGE = A_BYTES + W16_BYTES + WP_BYTES;
-  static constexpr int BAR_OFF = STAGE * STAGES;
-  static constexpr int TOTAL = BAR_OFF + 8 * (3 * STAGES + 1) + 16;
+template <int BN>
+struct GemmTile {
+  static constexpr int A_BYTES = BM * 128 * 2;    // 128 rows x 128 k x 2 B (two SW128 halves)
+  static constexpr int W16_BYTES = BN * 128 * 2;  // BN rows x 128 k x 2 B (two SW128 halves)
+  static constexpr int WP_BYTES = BN * 64;        // packed
+  static constexpr int FIXED = A_BYTES + W16_BYTES + WP_BYTES;
+  static constexpr int TMEM_COLS = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
 };
 
-template <int BN, int STAGES, bool BF, tq4_dtype T>
+template <int BN, bool BF, tq4_dtype T>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_z,
                 const GemmArgs p) {
-  using L = GemmSmem<BN, STAGES>;
+  using L = GemmTile<BN>;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw_addr);
-  const uint32_t bars = base + L::BAR_OFF;
+  const int S = p.stages;
+  const uint32_t bars = base + S * p.stage_bytes;
   auto full = [&](int s) { return bars + 8 * s; };
-  auto deq = [&](int s) { return bars + 8 * (STAGES + s); };
-  auto empty = [&](int s) { return bars + 8 * (2 * STAGES + s); };
-  const uint32_t accum = bars + 8 * (3 * STAGES);
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + L::BAR_OFF + 8 * (3 * STAGES + 1));
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::BAR_OFF + 8 * (3 * STAGES + 1) + 4);
+  auto deq = [&](int s) { return bars + 8 * (kMaxStages + s); };
+  auto empty = [&](int s) { return bars + 8 * (2 * kMaxStages + s); };
+  const uint32_t accum = bars + 8 * (3 * kMaxStages);
+  uint8_t* tail = smem + S * p.stage_bytes + 8 * (3 * kMaxStages + 1);
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(tail);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
   const int KT = p.ktiles;
+  const uint32_t tx_bytes = L::A_BYTES + L::WP_BYTES + BN * p.nb * p.st_bytes * (p.has_zp ? 2 : 1);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(full(s), 1);
-      mbar_init(deq(s), 128);
+      mbar_init(deq(s), 256);
       mbar_init(empty(s), 1);
     }
     mbar_init(accum, 1);
@@ -227,8 +237,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    constexpr uint32_t cols = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32((const void*)tmem_slot)), "r"(cols));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32((const void*)tmem_slot)), "r"((uint32_t)L::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
@@ -241,20 +250,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       int issued = 0;
       for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (kt / STAGES) & 1;
+        const int s = kt % S;
+        const uint32_t ph = (kt / S) & 1;
         if (!mbar_wait(empty(s), ph ^ 1, abort_flag, kDevTimeoutStageEmpty)) break;
-        const uint32_t st = base + s * L::STAGE;
-        mbar_expect_tx(full(s), L::A_BYTES + L::WP_BYTES);
+        const uint32_t st = base + s * p.stage_bytes;
+        const int b0 = (kt * 128) >> p.bs_log2;
+        mbar_expect_tx(full(s), tx_bytes);
         tma_load_2d(st, &map_a, kt * 128, m0, full(s));
         tma_load_2d(st + L::A_BYTES / 2, &map_a, kt * 128 + 64, m0, full(s));
         tma_load_2d(st + L::A_BYTES + L::W16_BYTES, &map_w, kt * 64, n0, full(s));
+        tma_load_2d(st + p.sc_off, &map_s, n0, b0, full(s));
+        if (p.has_zp) tma_load_2d(st + p.zc_off, &map_z, n0, b0, full(s));
         issued = kt + 1;
       }
       // the copies still in flight complete before the CTA exits (bounded)
-      for (int kt = max(0, issued - STAGES); kt < issued; ++kt) {
+      for (int kt = max(0, issued - S); kt < issued; ++kt) {
         const long long t0 = clock64();
-        while (!mbar_try(full(kt % STAGES), (kt / STAGES) & 1) && clock64() - t0 < kWaitCycles) {
+        while (!mbar_try(full(kt % S), (kt / S) & 1) && clock64() - t0 < kWaitCycles) {
         }
       }
     }
@@ -265,13 +277,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                  ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
       bool ok = true;
       for (int kt = 0; kt < KT && ok; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (kt / STAGES) & 1;
+        const int s = kt % S;
+        const uint32_t ph = (kt / S) & 1;
         ok = mbar_wait(full(s), ph, abort_flag, kDevTimeoutTmaFull) &&
              mbar_wait(deq(s), ph, abort_flag, kDevTimeoutDequant);
         if (!ok) break;
         asm volatile("tcgen05.fence::after_thread_sync;");
-        const uint32_t a_base = base + s * L::STAGE;
+        const uint32_t a_base = base + s * p.stage_bytes;
         const uint32_t w_base = a_base + L::A_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
@@ -286,33 +298,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ---------------- dequant warps (then epilogue) ----------------
-    const int tid = threadIdx.x - 64;  // 0..127
-    const bool has_zp = p.zps != nullptr;
-    const int st_bytes = (T == TQ4_F32) ? 4 : 2;
+    const int tid = threadIdx.x - 64;  // 0..255
     for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % STAGES;
-      const uint32_t ph = (kt / STAGES) & 1;
+      const int s = kt % S;
+      const uint32_t ph = (kt / S) & 1;
       if (!mbar_wait(full(s), ph, abort_flag, kDevTimeoutTmaFull)) break;
-      uint8_t* st = smem + s * L::STAGE;
+      uint8_t* st = smem + s * p.stage_bytes;
       const uint8_t* wp = st + L::A_BYTES + L::W16_BYTES;
       uint8_t* w16 = st + L::A_BYTES;
-      for (int task = tid; task < BN * 4; task += 128) {
+      const uint8_t* sc = st + p.sc_off;
+      const uint8_t* zc = st + p.zc_off;
+      const int b0 = (kt * 128) >> p.bs_log2;
+      for (int task = tid; task < BN * 4; task += 256) {
         const int r = task >> 2, t = task & 3;
         const uint4 v = *reinterpret_cast<const uint4*>(wp + r * 64 + t * 16);
-        const int64_t n = (int64_t)n0 + r;
-        const bool in_rows = n < p.n_pad;  // the last tile may reach past the padded rows
-        const int64_t srow = n * p.blocks_pad;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint32_t x = (j < 2) ? v.x : (j < 4) ? v.y : (j < 6) ? v.z : v.w;
-          const int b = (kt * 128 + 16 * j) >> p.bs_log2;
-          const float sc = in_rows ? scale_to_f32(p.scales, srow + b, st_bytes, T == TQ4_BF16) : 0.f;
-          const float z = (has_zp && in_rows) ? scale_to_f32(p.zps, srow + b, st_bytes, T == TQ4_BF16) : p.z_const;
+          const int lb = ((kt * 128 + 16 * j) >> p.bs_log2) - b0;  // staged block row
+          const float scv = scale_to_f32(sc, lb * BN + r, p.st_bytes, T == TQ4_BF16);
+          const float z = p.has_zp ? scale_to_f32(zc, lb * BN + r, p.st_bytes, T == TQ4_BF16) : p.z_const;
           uint32_t q0, q1;
           q_pairs4(x, j, BF, q0, q1);
           uint2 out;
-          out.x = deq_pair<BF, T>(q0, z, sc);
-          out.y = deq_pair<BF, T>(q1, z, sc);
+          out.x = deq_pair<BF, T>(q0, z, scv);
+          out.y = deq_pair<BF, T>(q1, z, scv);
           // k within the group = 16j + 4t: half j/4, 16-byte chunk 2(j%4) + t/2, 8-byte half t%2
           const int chunk = 2 * (j & 3) + (t >> 1);
           uint8_t* dst = w16 + (j >> 2) * (BN * 128) + r * 128 + ((chunk ^ (r & 7)) << 4) + ((t & 1) << 3);
@@ -335,22 +345,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     asm volatile("tcgen05.fence::after_thread_sync;");
-    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    const int quarter = warp & 3;                // TMEM lanes 32*quarter .. +31
+    const int half = (warp - 2) >> 2;            // columns [half*BN/2, (half+1)*BN/2)
     const int row = m0 + quarter * 32 + lane;
     if (__all_sync(0xffffffffu, ok && !*abort_flag)) {
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
+      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 16) {
         uint32_t r[16];
         tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + c, r);
         if (row < p.M) {
+          const int64_t nb0 = (int64_t)n0 + c;
+          float v[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int64_t n = (int64_t)n0 + c + i;
-            if (n < p.N) {
-              float v = __uint_as_float(r[i]);
-              if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
-              store_from_f32(p.y, (int64_t)row * p.ldy + n, p.y_t, v);
+            v[i] = __uint_as_float(r[i]);
+            if (p.bias && nb0 + i < p.N) v[i] = round_to(v[i], p.y_t) + load_as_f32(p.bias, nb0 + i, p.bias_t);
+          }
+          const int64_t off = (int64_t)row * p.ldy + nb0;
+          const bool whole = nb0 + 16 <= p.N;
+          const uintptr_t addr = reinterpret_cast<uintptr_t>(p.y) + off * (p.y_t == TQ4_F32 ? 4 : 2);
+          const bool aligned = (addr & 15) == 0;  // 16-byte vector stores
+          if (whole && aligned && p.y_t != TQ4_F32) {
+            uint32_t h[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              if (p.y_t == TQ4_BF16) {
+                __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+                h[i] = *reinterpret_cast<uint32_t*>(&b2);
+              } else {
+                __half2 h2 = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+                h[i] = *reinterpret_cast<uint32_t*>(&h2);
+              }
             }
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + off);
+            dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+            dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+          } else if (whole && aligned && p.y_t == TQ4_F32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.y) + off);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (nb0 + i < p.N) store_from_f32(p.y, off + i, p.y_t, v[i]);
           }
         }
       }
@@ -361,8 +398,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;");
-    constexpr uint32_t cols = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(cols));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)L::TMEM_COLS));
   }
 }
 
@@ -408,31 +444,87 @@ static tq4_status make_map(CUtensorMap* map, CUtensorMapDataType dt, const void*
   return TQ4_OK;
 }
 
-template <int BN, int STAGES, bool BF, tq4_dtype T>
-static tq4_status launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mw, const GemmArgs& args,
+static const int kTileWidths[3] = {128, 96, 64};
+
+static int gemm_scale_blocks(const Weight& w) { return std::max(1, 128 >> w.bs_log2); }
+
+// Descriptors of a new handle, one set per GEMM tile width (4-bit weights only): the packed rows
+// (box BN x 64 bytes) and the block-major scales / zero points (box BN rows x the stage's blocks).
+tq4_status make_weight_maps(Weight& w) {
+  w.wmaps_ok = false;
+  if (w.desc.bits != 4 || encode_fn() == nullptr) return TQ4_OK;
+  const int st = dtype_size(w.desc.dequant_dtype);
+  const CUtensorMapDataType sdt = st == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  const int nb = gemm_scale_blocks(w);
+  for (int i = 0; i < 3; ++i) {
+    const int bn = kTileWidths[i];
+    TQ4_TRY(make_map(&w.wmaps[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, w.q.ptr, w.row_bytes, w.n_pad,
+                     w.row_bytes, 64, bn, CU_TENSOR_MAP_SWIZZLE_NONE));
+    TQ4_TRY(make_map(&w.smaps[i], sdt, w.scales.ptr, w.n_pad, w.blocks_pad, w.n_pad * st, bn, nb,
+                     CU_TENSOR_MAP_SWIZZLE_NONE));
+    if (w.zps.ptr)
+      TQ4_TRY(make_map(&w.zmaps[i], sdt, w.zps.ptr, w.n_pad, w.blocks_pad, w.n_pad * st, bn, nb,
+                       CU_TENSOR_MAP_SWIZZLE_NONE));
+    else
+      w.zmaps[i] = w.smaps[i];  // never loaded
+  }
+  w.wmaps_ok = true;
+  return TQ4_OK;
+}
+
+constexpr int kSmemLimit = 232448;  // 227 KB of dynamic shared memory per CTA
+
+struct GemmPlan {
+  int stages, stage_bytes, sc_off, zc_off, smem;
+};
+
+template <int BN>
+static GemmPlan plan_gemm_smem(const Weight& w) {
+  using L = GemmTile<BN>;
+  GemmPlan pl{};
+  const int st = dtype_size(w.desc.dequant_dtype);
+  const int sc_bytes = BN * gemm_scale_blocks(w) * st;
+  pl.sc_off = L::FIXED;
+  pl.zc_off = pl.sc_off + (sc_bytes + 127) / 128 * 128;
+  const int end = pl.zc_off + (w.zps.ptr ? sc_bytes : 0);
+  pl.stage_bytes = (end + 1023) / 1024 * 1024;
+  const int fixed = 1024 + 8 * (3 * kMaxStages + 1) + 16;
+  pl.stages = std::min(kMaxStages, (kSmemLimit - fixed) / pl.stage_bytes);
+  pl.smem = fixed + pl.stages * pl.stage_bytes;
+  return pl;
+}
+
+template <int BN, bool BF, tq4_dtype T>
+static tq4_status launch_gemm_t(const CUtensorMap& ma, const Weight& w, int map_i, GemmArgs args,
                                 cudaStream_t st) {
-  using L = GemmSmem<BN, STAGES>;
-  auto kern = gemm_kernel<BN, STAGES, BF, T>;
-  const int smem = L::TOTAL + 1024;
-  static bool attr_set = false;  // once per instantiation
+  const GemmPlan pl = plan_gemm_smem<BN>(w);
+  if (pl.stages < 2) {
+    set_error("GEMM: the stage does not fit shared memory");
+    return TQ4_ERR_UNSUPPORTED;
+  }
+  args.stages = pl.stages;
+  args.stage_bytes = pl.stage_bytes;
+  args.sc_off = pl.sc_off;
+  args.zc_off = pl.zc_off;
+  auto kern = gemm_kernel<BN, BF, T>;
+  static bool attr_set = false;  // once per instantiation, at the largest size it can ask for
   if (!attr_set) {
-    TQ4_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    TQ4_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
     attr_set = true;
   }
   const dim3 grid((args.N + BN - 1) / BN, (args.M + BM - 1) / BM);
-  kern<<<grid, kGemmThreads, smem, st>>>(ma, mw, args);
+  kern<<<grid, kGemmThreads, pl.smem, st>>>(ma, w.wmaps[map_i], w.smaps[map_i], w.zmaps[map_i], args);
   TQ4_CUDA(cudaGetLastError());
   return TQ4_OK;
 }
 
 template <int BN, bool BF>
-static tq4_status launch_gemm_bn(const CUtensorMap& ma, const CUtensorMap& mw, const GemmArgs& args,
-                                 tq4_dtype t, cudaStream_t st) {
-  constexpr int STAGES = 3;
-  switch (t) {
-    case TQ4_F16: return launch_gemm_t<BN, STAGES, BF, TQ4_F16>(ma, mw, args, st);
-    case TQ4_BF16: return launch_gemm_t<BN, STAGES, BF, TQ4_BF16>(ma, mw, args, st);
-    default: return launch_gemm_t<BN, STAGES, BF, TQ4_F32>(ma, mw, args, st);
+static tq4_status launch_gemm_bn(const CUtensorMap& ma, const Weight& w, int map_i,
+                                 const GemmArgs& args, cudaStream_t st) {
+  switch (w.desc.dequant_dtype) {
+    case TQ4_F16: return launch_gemm_t<BN, BF, TQ4_F16>(ma, w, map_i, args, st);
+    case TQ4_BF16: return launch_gemm_t<BN, BF, TQ4_BF16>(ma, w, map_i, args, st);
+    default: return launch_gemm_t<BN, BF, TQ4_F32>(ma, w, map_i, args, st);
   }
 }
 
@@ -440,28 +532,16 @@ static tq4_status launch_gemm_bn(const CUtensorMap& ma, const CUtensorMap& mw, c
 static bool gemm_eligible(const Weight& w, const void* a, tq4_dtype a_t) {
   if (w.desc.bits != 4) return false;
   if (a_t != TQ4_F16 && a_t != TQ4_BF16) return false;
-  if ((w.desc.K * 2) % 16 != 0) return false;                // TMA row stride
+  if ((w.desc.K * 2) % 16 != 0) return false;                    // TMA row stride
   if ((reinterpret_cast<uintptr_t>(a) & 15) != 0) return false;  // TMA base address
   return w.wmaps_ok;
-}
-
-// The packed-row descriptors of a new handle, one per GEMM tile width (4-bit weights only).
-tq4_status make_weight_maps(Weight& w) {
-  w.wmaps_ok = false;
-  if (w.desc.bits != 4 || encode_fn() == nullptr) return TQ4_OK;
-  const int widths[3] = {128, 96, 64};
-  for (int i = 0; i < 3; ++i)
-    TQ4_TRY(make_map(&w.wmaps[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, w.q.ptr, w.row_bytes, w.n_pad,
-                     w.row_bytes, 64, widths[i], CU_TENSOR_MAP_SWIZZLE_NONE));
-  w.wmaps_ok = true;
-  return TQ4_OK;
 }
 
 static int choose_bn(const Weight& w, int64_t m) {
   // fill the SMs: prefer the widest tile whose grid still covers them
   const int64_t mt = (m + BM - 1) / BM;
   const int sms = w.num_sms;
-  for (int bn : {128, 96, 64}) {
+  for (int bn : kTileWidths) {
     const int64_t tiles = mt * ((w.desc.N + bn - 1) / bn);
     if (tiles >= sms * 3 / 4) return bn;
   }
@@ -471,31 +551,29 @@ static int choose_bn(const Weight& w, int64_t m) {
 tq4_status run_gemm_tc(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,
                        tq4_dtype bias_t, void* y, tq4_dtype y_t, int64_t ldy, cudaStream_t st) {
   const int bn = choose_bn(w, m);
+  const int map_i = bn == 128 ? 0 : (bn == 96 ? 1 : 2);
   CUtensorMap ma;
   const CUtensorMapDataType adt = a_t == TQ4_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   TQ4_TRY(make_map(&ma, adt, a, w.desc.K, m, w.desc.K * 2, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B));
-  const CUtensorMap& mw = w.wmaps[bn == 128 ? 0 : (bn == 96 ? 1 : 2)];
   GemmArgs args{};
-  args.scales = w.scales.ptr;
-  args.zps = w.zps.ptr;
-  args.blocks_pad = w.blocks_pad;
   args.z_const = w.z_const;
+  args.has_zp = w.zps.ptr != nullptr;
   args.bs_log2 = w.bs_log2;
+  args.nb = gemm_scale_blocks(w);
   args.M = (int)m;
   args.N = (int)w.desc.N;
   args.K = (int)w.desc.K;
-  args.n_pad = w.n_pad;
   args.ktiles = (int)w.groups;
+  args.st_bytes = dtype_size(w.desc.dequant_dtype);
   args.bias = bias;
   args.bias_t = bias_t;
   args.y = y;
   args.y_t = y_t;
   args.ldy = ldy;
   const bool bf = a_t == TQ4_BF16;
-  const tq4_dtype t = w.desc.dequant_dtype;
-  if (bn == 128) return bf ? launch_gemm_bn<128, true>(ma, mw, args, t, st) : launch_gemm_bn<128, false>(ma, mw, args, t, st);
-  if (bn == 96) return bf ? launch_gemm_bn<96, true>(ma, mw, args, t, st) : launch_gemm_bn<96, false>(ma, mw, args, t, st);
-  return bf ? launch_gemm_bn<64, true>(ma, mw, args, t, st) : launch_gemm_bn<64, false>(ma, mw, args, t, st);
+  if (bn == 128) return bf ? launch_gemm_bn<128, true>(ma, w, map_i, args, st) : launch_gemm_bn<128, false>(ma, w, map_i, args, st);
+  if (bn == 96) return bf ? launch_gemm_bn<96, true>(ma, w, map_i, args, st) : launch_gemm_bn<96, false>(ma, w, map_i, args, st);
+  return bf ? launch_gemm_bn<64, true>(ma, w, map_i, args, st) : launch_gemm_bn<64, false>(ma, w, map_i, args, st);
 }
 
 // Rows of A in slices of 16 through the fused GEMV kernel (2- and 8-bit weights, f32

@@ -2,22 +2,26 @@
 //
 // Math (the MatMulNBits clause, quantized.ex:30-46 with dequantize_weight/4 at :234-240):
 //   Y[m][n] = sum_k A[m][k] * (q[n][k] - z[n][b(k)]) * s[n][b(k)]
-// is evaluated per "segment" (a run of seg = min(block_size, group, 128) elements of one block):
-//   Y[m][n] = sum_seg s[n][b] * ( E[m][seg] * P[m][n][seg] - z[n][b] * ZA[m][seg] )
-//   P = sum_{k in seg} q[n][k] * a'[m][k]      (tensor cores, exact integer q, f32 accumulate)
-//   a' = f16/bf16(A / E),  ZA = E * sum_{k in seg} a'[m][k]
-// E is 1 for f16/bf16 activations and an exact power of two for f32 activations (chosen from
-// the segment's max |a| so that a' cannot overflow f16). The per-element work is one LOP3 and
-// one f16x2/bf16x2 op per two weights; zero points and scales are applied once per segment.
+// is evaluated per "segment" (a run of seg = min(block_size, group, 128) weights of one block).
+// The weights enter the tensor cores as magic-number floats O + q*c(k)^-1 straight out of one
+// LOP3 (O = 1024 for f16, 128 for bf16; c(k) is 1/16, 1/4, ... for the nibbles the mask leaves
+// shifted, and the staged activation at k is multiplied by c(k) to match). With the staged
+// activations v(k) = RN(A[m][k] / E * c(k)) (E an exact power of two per segment chosen so that
+// v cannot overflow f16),
+//   P[m][n][seg] = sum_{k in seg} (O + q/c(k)) v(k)            (mma.sync, f32 accumulate)
+//   Y[m][n]     += s[n][b] * ( E*P - E*O*SV - z[n][b] * E*SA ),  SV = sum v, SA = sum v/c
+// so zero points, scales and the magic offset cost a few FMAs per segment and each pair of
+// weights costs one LOP3 (plus one shift per 32-bit word).
 //
 // Work split: a tile is 16*WN weight rows x a K range of whole 64-byte groups; persistent CTAs
 // of 8 warps walk the tiles. Each warp owns 16 rows of the tile (mma.sync m16n8k16, weights as
 // the A operand) and every WK-th group of the range (WK = 8/WN). Activations and per-segment
 // factors are staged in shared memory once per K range; each tile's scales / zero points arrive
-// by cp.async while its first weights are in flight; the packed weights stream from HBM with
-// 128-bit non-allocating loads, two groups ahead. Warps that share rows reduce through shared
-// memory; tiles that share rows (split-K) reduce through a float workspace, the last CTA of a
-// row tile doing the sum in a fixed order (deterministic) and resetting its counter.
+// by cp.async (block-major, so each block's rows are one contiguous run) while its first weights
+// are in flight; the packed weights stream from HBM with 128-bit non-allocating loads, two
+// groups ahead. Warps that share rows reduce through shared memory; tiles that share rows
+// (split-K) reduce through a float workspace, the last CTA of a row tile doing the sum in a
+// fixed order (deterministic) and resetting its counter.
 #include <map>
 #include <memory>
 #include <mutex>
@@ -29,9 +33,8 @@ namespace tq4 {
 struct GemvArgs {
   const uint8_t* q;
   int64_t row_bytes;
-  const void* scales;  // [n_pad][blocks_pad] in T
+  const void* scales;  // [blocks_pad][n_pad] in T
   const void* zps;     // same, or null
-  int64_t blocks_pad;
   float z_const;
   int st_bf16;         // 2-byte scale storage is bf16 (else f16)
   int K, N, M;
@@ -53,64 +56,56 @@ struct GemvArgs {
 };
 
 // ---- weight fragments --------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t f16x2_sub(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-__device__ __forceinline__ uint32_t f16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t r;
-  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
-  return r;
-}
-__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
   return r;
 }
 
-// Pair (e0, e1) -> p0 and pair (e2, e3) -> p1 of step j (within its word) of one row's word x,
-// as exact integers q in f16x2 (BF = false) or bf16x2 (BF = true).
-template <int BITS, bool BF>
+// Magic-number weights of step j (within its word) of one row's word x: p0 holds the pair
+// (e0, e1), p1 the pair (e2, e3), each as O + q/c in f16x2 (BF = false) or bf16x2 (BF = true).
+// PRECISE (f32 activations) keeps the offset small against the weights: every 4-bit pair comes
+// out as 1024 + 16 q (one more shift per word) and 2-bit weights come out as exact q, so the
+// f32 accumulator never carries terms much larger than the result it is building.
+template <int BITS, bool BF, bool PRECISE>
 __device__ __forceinline__ void weight_pairs(uint32_t x, int j, uint32_t& p0, uint32_t& p1) {
   if constexpr (BITS == 4) {
     const uint32_t src = (j & 1) ? (x >> 8) : x;
-    if constexpr (!BF) {
-      p0 = f16x2_sub(lop3_and_or(src, 0x000F000Fu, 0x64006400u), 0x64006400u);
-      // 1024 + 16 q -> q via q = r/16 - 64 (exact)
-      p1 = f16x2_fma(lop3_and_or(src, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD400D400u);
+    if constexpr (!BF && PRECISE) {
+      p0 = lop3_and_or((j & 1) ? (x >> 4) : (x << 4), 0x00F000F0u, 0x64006400u);  // 1024 + 16 q
+      p1 = lop3_and_or(src, 0x00F000F0u, 0x64006400u);                           // 1024 + 16 q
+    } else if constexpr (!BF) {
+      p0 = lop3_and_or(src, 0x000F000Fu, 0x64006400u);  // 1024 + q
+      p1 = lop3_and_or(src, 0x00F000F0u, 0x64006400u);  // 1024 + 16 q
     } else {
-      p0 = bf16x2_sub(lop3_and_or(src, 0x000F000Fu, 0x43004300u), 0x43004300u);
-      p1 = bf16x2_sub(lop3_and_or(src >> 4, 0x000F000Fu, 0x43004300u), 0x43004300u);
+      p0 = lop3_and_or(src, 0x000F000Fu, 0x43004300u);       // 128 + q
+      p1 = lop3_and_or(src >> 4, 0x000F000Fu, 0x43004300u);  // 128 + q
     }
   } else if constexpr (BITS == 2) {
     const int sub = j & 3;
     if constexpr (!BF) {
       const uint32_t src = (sub >= 2) ? (x >> 8) : x;
       const int i0 = 2 * (sub & 1);
-      // mask 3 << 2i yields 1024 + 4^i q; scale back by 4^-i and subtract 1024 * 4^-i.
-      const uint32_t m0 = 0x00030003u << (2 * i0), m1 = 0x00030003u << (2 * i0 + 2);
-      const uint32_t sc0 = (i0 == 0) ? 0x3C003C00u : 0x2C002C00u;  // 1, 1/16
-      const uint32_t of0 = (i0 == 0) ? 0xE400E400u : 0xD400D400u;  // -1024, -64
-      const uint32_t sc1 = (i0 == 0) ? 0x34003400u : 0x24002400u;  // 1/4, 1/64
-      const uint32_t of1 = (i0 == 0) ? 0xDC00DC00u : 0xCC00CC00u;  // -256, -16
-      p0 = f16x2_fma(lop3_and_or(src, m0, 0x64006400u), sc0, of0);
-      p1 = f16x2_fma(lop3_and_or(src, m1, 0x64006400u), sc1, of1);
+      p0 = lop3_and_or(src, 0x00030003u << (2 * i0), 0x64006400u);      // 1024 + 4^i0 q
+      p1 = lop3_and_or(src, 0x00030003u << (2 * i0 + 2), 0x64006400u);  // 1024 + 4^(i0+1) q
+      if constexpr (PRECISE) {  // exact q: r * 4^-i - 1024 * 4^-i
+        const uint32_t sc0 = (i0 == 0) ? 0x3C003C00u : 0x2C002C00u;  // 1, 1/16
+        const uint32_t of0 = (i0 == 0) ? 0xE400E400u : 0xD400D400u;  // -1024, -64
+        const uint32_t sc1 = (i0 == 0) ? 0x34003400u : 0x24002400u;  // 1/4, 1/64
+        const uint32_t of1 = (i0 == 0) ? 0xDC00DC00u : 0xCC00CC00u;  // -256, -16
+        asm("fma.rn.f16x2 %0, %0, %1, %2;" : "+r"(p0) : "r"(sc0), "r"(of0));
+        asm("fma.rn.f16x2 %0, %0, %1, %2;" : "+r"(p1) : "r"(sc1), "r"(of1));
+      }
     } else {
       const int pos0 = 2 * sub;
-      p0 = bf16x2_sub(lop3_and_or(x >> (2 * pos0), 0x00030003u, 0x43004300u), 0x43004300u);
-      p1 = bf16x2_sub(lop3_and_or(x >> (2 * pos0 + 2), 0x00030003u, 0x43004300u), 0x43004300u);
+      p0 = lop3_and_or(x >> (2 * pos0), 0x00030003u, 0x43004300u);
+      p1 = lop3_and_or(x >> (2 * pos0 + 2), 0x00030003u, 0x43004300u);
     }
   } else {  // 8 bits: the word is one step, bytes e0..e3
     if constexpr (!BF) {
-      p0 = f16x2_sub(prmt(x, 0x64646464u, 0x4140u), 0x64006400u);
-      p1 = f16x2_sub(prmt(x, 0x64646464u, 0x4342u), 0x64006400u);
-    } else {
+      p0 = prmt(x, 0x64646464u, 0x4140u);  // 1024 + q
+      p1 = prmt(x, 0x64646464u, 0x4342u);
+    } else {  // exact q through f32 (bf16 cannot hold 128 + q for q >= 128)
       const float f0 = __uint_as_float(prmt(x, 0x4B000000u, 0x7540u)) - 8388608.f;
       const float f1 = __uint_as_float(prmt(x, 0x4B000000u, 0x7541u)) - 8388608.f;
       const float f2 = __uint_as_float(prmt(x, 0x4B000000u, 0x7542u)) - 8388608.f;
@@ -120,6 +115,27 @@ __device__ __forceinline__ void weight_pairs(uint32_t x, int j, uint32_t& p0, ui
       p1 = *reinterpret_cast<uint32_t*>(&h1);
     }
   }
+}
+
+// The offset O of the magic-number weights and the activation factor c(k) that matches the
+// weight at position k (k is the position within the 64-byte group's elements).
+template <int BITS, bool BF, bool PRECISE>
+__device__ __forceinline__ float magic_offset() {
+  if constexpr (BITS == 8 && BF) return 0.f;
+  if constexpr (BITS == 2 && !BF && PRECISE) return 0.f;
+  return BF ? 128.f : 1024.f;
+}
+template <int BITS, bool BF, bool PRECISE>
+__device__ __forceinline__ float act_factor(int k) {
+  if constexpr (BF) return 1.f;
+  if constexpr (BITS == 4 && PRECISE) return 0.0625f;
+  if constexpr (BITS == 4) return (k & 2) ? 0.0625f : 1.f;
+  if constexpr (BITS == 2 && PRECISE) return 1.f;
+  if constexpr (BITS == 2) {
+    const int i = 2 * ((k >> 4) & 1) + ((k >> 1) & 1);
+    return i == 0 ? 1.f : (i == 1 ? 0.25f : (i == 2 ? 0.0625f : 0.015625f));
+  }
+  return 1.f;
 }
 
 template <bool BF>
@@ -192,13 +208,13 @@ __device__ __forceinline__ void load_act4(const void* a, int64_t m, int64_t k, i
   for (int e = 0; e < 4; ++e) out[e] = (k + e < K) ? load_as_f32(a, i + e, AT) : 0.f;
 }
 
-// Stages A[0:M][k0 : k0+kr] into shared memory as the MMA type (a' = A / E), with the
-// per-segment factors E and E * sum(a'). Rows >= M are left as they are: their outputs are
-// never stored, and an MMA output element depends only on its own activation row.
-template <tq4_dtype AT>
-__device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int kr, int sk,
-                                                  int nseg, uint16_t* act, float* segE,
-                                                  float* segZA) {
+// Stages A[0:M][k0 : k0+kr] into shared memory as v(k) = RN(A / E * c(k)) in the MMA type, with
+// the per-segment factors {E, E*O*SV - (no zero points ? z*E*SA : 0), E*SA} as float4 [seg][m].
+// Rows >= M are left as they are: their outputs are never stored, and an MMA output element
+// depends only on its own activation row.
+template <int BITS, tq4_dtype AT>
+__device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int kr, int sk, int mp,
+                                                  uint16_t* act, float4* segf) {
   constexpr bool BF = (AT == TQ4_BF16);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int vec_per_row = kr / 4;
@@ -206,6 +222,9 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int
   const int total_pad = (total + 31) & ~31;  // whole warps take part in the shuffles
   const int L = (1 << p.seg_log2) >> 2;      // lanes per segment (<= 32)
   const bool vec = (p.K & 3) == 0;
+  constexpr bool PRECISE = (AT == TQ4_F32);
+  const float O = magic_offset<BITS, BF, PRECISE>();
+  const bool fold_z = p.zps == nullptr;
   for (int base = 0; base < total_pad; base += 4 * kGemvThreads) {
     float a4[4][4];
 #pragma unroll
@@ -223,33 +242,38 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int
       if (base + u * kGemvThreads + warp * 32 >= total_pad) continue;  // warp-uniform
       const int v = base + u * kGemvThreads + threadIdx.x;
       const int m = v / vec_per_row, kk = (v % vec_per_row) * 4;
+      float mx = fmaxf(fmaxf(fabsf(a4[u][0]), fabsf(a4[u][1])), fmaxf(fabsf(a4[u][2]), fabsf(a4[u][3])));
+      for (int off = 1; off < L; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
       float e_scale = 1.f, inv = 1.f;
-      if constexpr (AT == TQ4_F32) {
-        float mx = fmaxf(fmaxf(fabsf(a4[u][0]), fabsf(a4[u][1])), fmaxf(fabsf(a4[u][2]), fabsf(a4[u][3])));
-        for (int off = 1; off < L; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        if (mx > 0.f && mx <= 3.402823466e38f) {
-          int ex;
-          frexpf(mx, &ex);                                // mx = f * 2^ex, f in [0.5, 1)
-          const int s = max(-126, min(127, ex - 15));     // mx / 2^s in [2^14, 2^15)
-          e_scale = ldexpf(1.f, s);
-          inv = ldexpf(1.f, -s);
-        }
+      if (mx > 0.f && mx <= 3.402823466e38f) {
+        int ex;
+        frexpf(mx, &ex);                             // mx = f * 2^ex, f in [0.5, 1)
+        const int s = max(-126, min(127, ex - 15));  // mx / 2^s in [2^14, 2^15)
+        e_scale = ldexpf(1.f, s);
+        inv = ldexpf(1.f, -s);
       }
       uint16_t h[4];
-      float sum = 0.f;
+      float sv = 0.f, sa = 0.f;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
+        const float c = act_factor<BITS, BF, PRECISE>(kk + e);  // kk: a multiple of 4
+        float val;
         if constexpr (BF) {
-          const __nv_bfloat16 b = __float2bfloat16_rn(a4[u][e] * inv);
+          const __nv_bfloat16 b = __float2bfloat16_rn(a4[u][e] * inv * c);
           h[e] = __bfloat16_as_ushort(b);
-          sum += __bfloat162float(b);
+          val = __bfloat162float(b);
         } else {
-          const __half b = __float2half_rn(a4[u][e] * inv);
+          const __half b = __float2half_rn(a4[u][e] * inv * c);
           h[e] = __half_as_ushort(b);
-          sum += __half2float(b);
+          val = __half2float(b);
         }
+        sv += val;
+        sa += val / c;  // exact: c is a power of two
       }
-      for (int off = 1; off < L; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      for (int off = 1; off < L; off <<= 1) {
+        sv += __shfl_xor_sync(0xffffffffu, sv, off);
+        sa += __shfl_xor_sync(0xffffffffu, sa, off);
+      }
       if (v < total) {
         uint2 packed;
         packed.x = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
@@ -257,8 +281,9 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int
         *reinterpret_cast<uint2*>(act + m * sk + kk) = packed;
         if ((lane & (L - 1)) == 0) {
           const int s_idx = kk >> p.seg_log2;
-          segE[m * nseg + s_idx] = e_scale;
-          segZA[m * nseg + s_idx] = e_scale * sum;
+          const float za = e_scale * sa;
+          const float x = e_scale * O * sv + (fold_z ? p.z_const * za : 0.f);
+          segf[s_idx * mp + m] = make_float4(e_scale, x, za, 0.f);
         }
       }
     }
@@ -267,8 +292,8 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int
 
 // Shared-memory plan of one CTA (identical on host and device).
 struct GemvSmem {
-  int sk, nseg, nblk_max, sc_pitch;  // sc_pitch: bytes per row of the staged scales
-  int act_off, segE_off, segZA_off, sc_off, zc_off, red_off, total;
+  int sk, nseg, nblk_max;
+  int act_off, seg_off, sc_off, zc_off, red_off, total;
 };
 
 __host__ __device__ inline GemvSmem gemv_smem_plan(int mt, int kr_max, int seg, int bs, int rows_cta,
@@ -278,13 +303,11 @@ __host__ __device__ inline GemvSmem gemv_smem_plan(int mt, int kr_max, int seg, 
   s.sk = kr_max + 16;
   s.nseg = kr_max / seg;
   s.nblk_max = (kr_max + bs - 1) / bs + 1;
-  s.sc_pitch = ((s.nblk_max * st_bytes + 15) / 16 + 1) * 16;  // room to align the copy to 16 B
   s.act_off = 0;
-  s.segE_off = s.act_off + mp * s.sk * 2;
-  s.segZA_off = s.segE_off + mp * s.nseg * 4;
-  s.sc_off = (s.segZA_off + mp * s.nseg * 4 + 15) / 16 * 16;
-  s.zc_off = s.sc_off + rows_cta * s.sc_pitch;
-  s.red_off = s.zc_off + (zp ? rows_cta * s.sc_pitch : 0);
+  s.seg_off = (s.act_off + mp * s.sk * 2 + 15) / 16 * 16;
+  s.sc_off = s.seg_off + s.nseg * mp * 16;
+  s.zc_off = s.sc_off + (s.nblk_max * rows_cta * st_bytes + 15) / 16 * 16;
+  s.red_off = s.zc_off + (zp ? (s.nblk_max * rows_cta * st_bytes + 15) / 16 * 16 : 0);
   s.total = s.red_off + 8 * 32 * mt * 4 * 4;
   return s;
 }
@@ -295,6 +318,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs p)
   constexpr int G = 512 / BITS;  // elements per 64-byte group
   constexpr int STEPS = G / 16;
   constexpr int STEPS_PER_WORD = 32 / BITS / 4;  // 2 (4-bit), 4 (2-bit), 1 (8-bit)
+  constexpr int MP = 8 * MT;
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ int s_last;
 
@@ -309,12 +333,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs p)
   const GemvSmem L = gemv_smem_plan(MT, p.groups_per_split * G, seg, 1 << p.bs_log2, rows_cta,
                                     ST_BYTES, has_zp);
   uint16_t* act = reinterpret_cast<uint16_t*>(smem + L.act_off);
-  float* segE = reinterpret_cast<float*>(smem + L.segE_off);
-  float* segZA = reinterpret_cast<float*>(smem + L.segZA_off);
+  float4* segf = reinterpret_cast<float4*>(smem + L.seg_off);
   uint8_t* sc = smem + L.sc_off;
   uint8_t* zc = smem + L.zc_off;
   float* red = reinterpret_cast<float*>(smem + L.red_off);
-  const int sk = L.sk, nseg = L.nseg;
+  const int sk = L.sk;
 
   const int tiles = p.ctas_n * p.ksplit;
   int staged_split = -1;
@@ -329,16 +352,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs p)
     const int b_first = k0 >> p.bs_log2;
     const int nblk = ((k0 + kr - 1) >> p.bs_log2) - b_first + 1;
 
-    // -- scales / zero points of this tile: 16-byte cp.async over the aligned span of each row
-    const int64_t span_lo = ((int64_t)b_first * ST_BYTES) & ~15LL;
-    const int64_t span_hi = (((int64_t)(b_first + nblk) * ST_BYTES) + 15) & ~15LL;
-    const int c16 = (int)((span_hi - span_lo) >> 4);
-    const int sc_shift = (int)(((int64_t)b_first * ST_BYTES - span_lo) / ST_BYTES);  // entries
-    for (int i = threadIdx.x; i < rows_cta * c16; i += kGemvThreads) {
-      const int r = i / c16, c = i % c16;
-      const int64_t src = (cta_row0 + r) * p.blocks_pad * ST_BYTES + span_lo + c * 16;
-      cp_async16(sc + r * L.sc_pitch + c * 16, static_cast<const uint8_t*>(p.scales) + src);
-      if (has_zp) cp_async16(zc + r * L.sc_pitch + c * 16, static_cast<const uint8_t*>(p.zps) + src);
+    // -- scales / zero points of this tile: per block, the tile's rows are one contiguous run
+    const int c16 = rows_cta * ST_BYTES / 16;  // 16-byte chunks per block
+    for (int i = threadIdx.x; i < nblk * c16; i += kGemvThreads) {
+      const int bb = i / c16, c = i % c16;
+      const int64_t src = ((int64_t)(b_first + bb) * p.n_pad + cta_row0) * ST_BYTES + c * 16;
+      cp_async16(sc + (bb * rows_cta) * ST_BYTES + c * 16, static_cast<const uint8_t*>(p.scales) + src);
+      if (has_zp) cp_async16(zc + (bb * rows_cta) * ST_BYTES + c * 16, static_cast<const uint8_t*>(p.zps) + src);
     }
 
     // -- the first weight batch
@@ -359,7 +379,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs p)
 
     // -- activations, once per K range
     if (split != staged_split) {
-      stage_activations<AT>(p, k0, kr, sk, nseg, act, segE, segZA);
+      stage_activations<BITS, AT>(p, k0, kr, sk, MP, act, segf);
       staged_split = split;
     }
     cp_async_wait_all();
@@ -372,10 +392,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs p)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[mt][i] = blk[mt][i] = 0.f;
     const int rl_g = warp_n * 16 + g;
-    const uint8_t* sc_g = sc + rl_g * L.sc_pitch;
-    const uint8_t* sc_g8 = sc + (rl_g + 8) * L.sc_pitch;
-    const uint8_t* zc_g = zc + rl_g * L.sc_pitch;
-    const uint8_t* zc_g8 = zc + (rl_g + 8) * L.sc_pitch;
 
     for (int cb = c_first; cb < g_end; cb += kPrefetch * wk) {
       const int cn = cb + kPrefetch * wk;
@@ -397,8 +413,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs p)
         for (int j = 0; j < STEPS; ++j) {
           const int w = j / STEPS_PER_WORD;
           uint32_t a0, a1, a2, a3;
-          weight_pairs<BITS, BF>(word_of(xa[d], w), j, a0, a2);
-          weight_pairs<BITS, BF>(word_of(xb[d], w), j, a1, a3);
+          weight_pairs<BITS, BF, AT == TQ4_F32>(word_of(xa[d], w), j, a0, a2);
+          weight_pairs<BITS, BF, AT == TQ4_F32>(word_of(xb[d], w), j, a1, a3);
           const int kk = kc + 16 * j + 4 * t;
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
@@ -407,20 +423,20 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs p)
           }
           if ((((j + 1) * 16) & (seg - 1)) == 0) {  // end of a segment
             const int s_idx = (kc + (j + 1) * 16 - seg) >> seg_log2;
-            const int bb = ((k0 + s_idx * seg) >> p.bs_log2) - b_first + sc_shift;
-            const float s_g = scale_to_f32(sc_g, bb, ST_BYTES, p.st_bf16);
-            const float s_g8 = scale_to_f32(sc_g8, bb, ST_BYTES, p.st_bf16);
-            const float z_g = has_zp ? scale_to_f32(zc_g, bb, ST_BYTES, p.st_bf16) : p.z_const;
-            const float z_g8 = has_zp ? scale_to_f32(zc_g8, bb, ST_BYTES, p.st_bf16) : p.z_const;
+            const int bb = ((k0 + s_idx * seg) >> p.bs_log2) - b_first;
+            const float s_g = scale_to_f32(sc, bb * rows_cta + rl_g, ST_BYTES, p.st_bf16);
+            const float s_g8 = scale_to_f32(sc, bb * rows_cta + rl_g + 8, ST_BYTES, p.st_bf16);
+            const float z_g = has_zp ? scale_to_f32(zc, bb * rows_cta + rl_g, ST_BYTES, p.st_bf16) : 0.f;
+            const float z_g8 = has_zp ? scale_to_f32(zc, bb * rows_cta + rl_g + 8, ST_BYTES, p.st_bf16) : 0.f;
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
               const int m0 = mt * 8 + 2 * t;
-              const float E0 = segE[m0 * nseg + s_idx], ZA0 = segZA[m0 * nseg + s_idx];
-              const float E1 = segE[(m0 + 1) * nseg + s_idx], ZA1 = segZA[(m0 + 1) * nseg + s_idx];
-              acc[mt][0] = fmaf(s_g, fmaf(E0, blk[mt][0], -z_g * ZA0), acc[mt][0]);
-              acc[mt][1] = fmaf(s_g, fmaf(E1, blk[mt][1], -z_g * ZA1), acc[mt][1]);
-              acc[mt][2] = fmaf(s_g8, fmaf(E0, blk[mt][2], -z_g8 * ZA0), acc[mt][2]);
-              acc[mt][3] = fmaf(s_g8, fmaf(E1, blk[mt][3], -z_g8 * ZA1), acc[mt][3]);
+              const float4 F0 = segf[s_idx * MP + m0], F1 = segf[s_idx * MP + m0 + 1];
+              // s * (E*P - X - z*ZA); without zero points X already holds z_const*ZA
+              acc[mt][0] = fmaf(s_g, fmaf(-z_g, F0.z, fmaf(F0.x, blk[mt][0], -F0.y)), acc[mt][0]);
+              acc[mt][1] = fmaf(s_g, fmaf(-z_g, F1.z, fmaf(F1.x, blk[mt][1], -F1.y)), acc[mt][1]);
+              acc[mt][2] = fmaf(s_g8, fmaf(-z_g8, F0.z, fmaf(F0.x, blk[mt][2], -F0.y)), acc[mt][2]);
+              acc[mt][3] = fmaf(s_g8, fmaf(-z_g8, F1.z, fmaf(F1.x, blk[mt][3], -F1.y)), acc[mt][3]);
 #pragma unroll
               for (int i = 0; i < 4; ++i) blk[mt][i] = 0.f;
             }
@@ -644,7 +660,6 @@ tq4_status run_gemv_with(const Weight& w, const void* a, int64_t m, tq4_dtype a_
   args.row_bytes = w.row_bytes;
   args.scales = w.scales.ptr;
   args.zps = w.zps.ptr;
-  args.blocks_pad = w.blocks_pad;
   args.z_const = w.z_const;
   args.st_bf16 = w.desc.dequant_dtype == TQ4_BF16;
   args.K = (int)w.desc.K;

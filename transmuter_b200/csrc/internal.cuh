@@ -94,13 +94,16 @@ struct tq4_weight {
   float z_const = 0.f;     // 2^(bits-1) when the node has no zero points
   cudaStream_t stream = nullptr;  // the handle's own stream (creation work only)
   tq4::DeviceBuffer q;       // [n_pad][row_bytes]
-  tq4::DeviceBuffer scales;  // [n_pad][blocks_pad] in T
-  tq4::DeviceBuffer zps;     // [n_pad][blocks_pad] in T, or empty
+  tq4::DeviceBuffer scales;  // [blocks_pad][n_pad] in T (block-major)
+  tq4::DeviceBuffer zps;     // [blocks_pad][n_pad] in T, or empty
   int num_sms = 148;
   // split-K workspaces of the GEMV, one per CUDA stream (a tq4::WorkspaceMap, made on first use)
   void* ws_mutex = nullptr;
-  // TMA descriptors of the packed rows for the GEMM's tile widths (128, 96, 64), made at creation
+  // TMA descriptors for the GEMM's tile widths (128, 96, 64), made at creation: packed rows,
+  // block-major scales and zero points
   alignas(64) CUtensorMap wmaps[3];
+  alignas(64) CUtensorMap smaps[3];
+  alignas(64) CUtensorMap zmaps[3];
   bool wmaps_ok = false;
 };
 

@@ -55,8 +55,9 @@ __global__ void repack_kernel(const uint8_t* __restrict__ raw, int64_t raw_row_b
   }
 }
 
-// scales / float zero points [N][blocks] of type `src_t` -> [n_pad][blocks_pad] in T with one
-// rounding (Nx.as_type, quantized.ex:237 and :314). Padding entries are 0.
+// scales / float zero points [N][blocks] of type `src_t` -> [blocks_pad][n_pad] (block-major, so
+// a run of rows of one block is contiguous) in T with one rounding (Nx.as_type,
+// quantized.ex:237 and :314). Padding entries are 0.
 template <typename T>
 __global__ void convert_blocks_kernel(const void* __restrict__ src, tq4_dtype src_t, int64_t n,
                                       int64_t blocks, T* __restrict__ dst, int64_t n_pad,
@@ -64,7 +65,7 @@ __global__ void convert_blocks_kernel(const void* __restrict__ src, tq4_dtype sr
   const int64_t total = n_pad * blocks_pad;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / blocks_pad, b = i % blocks_pad;
+    const int64_t b = i / n_pad, r = i % n_pad;
     float v = 0.f;
     if (r < n && b < blocks) v = load_as_f32(src, r * blocks + b, src_t);
     dst[i] = from_f32<T>(v);
@@ -72,7 +73,8 @@ __global__ void convert_blocks_kernel(const void* __restrict__ src, tq4_dtype sr
 }
 
 // Packed zero points: row r holds ceil(blocks*bits/8) bytes (the reshape to {N, :auto} of
-// quantized.ex:316-322); value b of the row is unpacked like B and cast to T (exact).
+// quantized.ex:316-322); value b of the row is unpacked like B and cast to T (exact), stored
+// block-major like the scales.
 template <typename T>
 __global__ void unpack_zp_kernel(const uint8_t* __restrict__ zp, int64_t zp_row_bytes, int bits,
                                  int64_t n, int64_t blocks, T* __restrict__ dst, int64_t n_pad,
@@ -81,7 +83,7 @@ __global__ void unpack_zp_kernel(const uint8_t* __restrict__ zp, int64_t zp_row_
   const int64_t total = n_pad * blocks_pad;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / blocks_pad, b = i % blocks_pad;
+    const int64_t b = i / n_pad, r = i % n_pad;
     float v = 0.f;
     if (r < n && b < blocks) {
       const uint8_t byte = zp[r * zp_row_bytes + b / per];
@@ -112,7 +114,7 @@ __device__ __forceinline__ T dequant_one(uint32_t q, float z, float s) {
 template <int BITS, typename T>
 __global__ void dequant_kernel(const uint8_t* __restrict__ q, int64_t row_bytes,
                                const T* __restrict__ scales, const T* __restrict__ zps,
-                               float z_const, int64_t blocks_pad, int bs_log2, int64_t n,
+                               float z_const, int64_t n_pad, int bs_log2, int64_t n,
                                int64_t k, const int64_t* __restrict__ rows, int64_t n_rows,
                                T* __restrict__ out) {
   const int64_t total = n * k;
@@ -130,8 +132,8 @@ __global__ void dequant_kernel(const uint8_t* __restrict__ q, int64_t row_bytes,
     packed_position<BITS>(kk, byte, shift);
     const uint32_t v = (q[r * row_bytes + byte] >> shift) & ((1u << BITS) - 1);
     const int64_t b = kk >> bs_log2;
-    const float s = to_f32(scales[r * blocks_pad + b]);
-    const float z = zps ? to_f32(zps[r * blocks_pad + b]) : z_const;
+    const float s = to_f32(scales[b * n_pad + r]);
+    const float z = zps ? to_f32(zps[b * n_pad + r]) : z_const;
     out[i] = dequant_one<BITS, T>(v, z, s);
   }
 }
@@ -215,7 +217,7 @@ static void launch_dequant(const Weight& w, const int64_t* rows, int64_t n_out, 
   const int64_t total = n_out * w.desc.K;
   dequant_kernel<BITS, T><<<grid_for(total, 256), 256, 0, st>>>(
       static_cast<const uint8_t*>(w.q.ptr), w.row_bytes, static_cast<const T*>(w.scales.ptr),
-      static_cast<const T*>(w.zps.ptr), w.z_const, w.blocks_pad, w.bs_log2, n_out, w.desc.K, rows,
+      static_cast<const T*>(w.zps.ptr), w.z_const, w.n_pad, w.bs_log2, n_out, w.desc.K, rows,
       w.desc.N, static_cast<T*>(out));
 }
 
