@@ -97,7 +97,7 @@ tq4_status tq4_matmul(const tq4_weight* w, const void* a, int64_t m, tq4_dtype a
 /* tq4_matmul for M <= 16 that allocates no device memory. No counterpart in the reference: it
  * serves callers that cannot call cudaMalloc, such as a NIF sharing the GPU with EXLA's client
  * (which reserves most device memory up front) or a decode loop that must not risk the device
- * synchronization of cudaMalloc/cudaFree. Its split-K scratch is a static 2 MiB device array
+ * synchronization of cudaMalloc/cudaFree. Its split-K scratch is a static 4 MiB device array
  * (plus 64 KiB of counters) that every GPU loading the library holds until exit; a call that
  * would need more is rejected with TQ4_ERR_INVALID_ARGUMENT, and M > 16 with
  * TQ4_ERR_UNSUPPORTED. The first call on a device looks up the array's device address (make it

@@ -19,7 +19,7 @@ void set_error(const char* fmt, ...) {
   t_last_error = buf;
 }
 
-static void clear_error() { t_last_error.clear(); }
+void clear_error() { t_last_error.clear(); }
 
 void free_workspaces(Weight& w);
 
@@ -172,6 +172,7 @@ tq4_status tq4_weight_create(const tq4_weight_desc* d, const void* b, int64_t b_
   if (st == TQ4_OK && d->zp_kind != TQ4_ZP_NONE) st = w->zps.alloc(w->n_pad * w->blocks_pad * tsz);
   if (st == TQ4_OK) st = prepare_weight(*w, b, scales, zp);
   if (st == TQ4_OK) st = make_weight_maps(*w);
+  if (st == TQ4_OK) st = make_gemv_maps(*w);
   cudaSetDevice(prev);
   if (st != TQ4_OK) {
     tq4_weight_destroy(w);
@@ -208,17 +209,6 @@ tq4_status tq4_weight_info(const tq4_weight* w, tq4_weight_desc* d, int64_t* dev
 }
 
 // RAII switch to the handle's device for the duration of a call.
-struct DeviceGuard {
-  int prev = -1;
-  explicit DeviceGuard(int dev) {
-    if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) cudaSetDevice(dev);
-    else if (prev == dev) prev = -1;
-  }
-  ~DeviceGuard() {
-    if (prev >= 0) cudaSetDevice(prev);
-  }
-};
-
 tq4_status tq4_matmul(const tq4_weight* w, const void* a, int64_t m, tq4_dtype a_t,
                       const void* bias, tq4_dtype bias_t, void* y, tq4_dtype y_t, void* stream) {
   clear_error();

@@ -25,8 +25,8 @@ enum DeviceCode : int32_t {
   kDevBadArgument = 0x200,
 };
 
-// Defined here (libtq4 is one translation unit, csrc/tq4_all.cu).
-__device__ int32_t g_device_status = 0;
+// Defined in weight.cu (the library is built with relocatable device code).
+extern __device__ int32_t g_device_status;
 
 __device__ __forceinline__ void report(int32_t code) { atomicCAS(&g_device_status, 0, code); }
 
@@ -54,6 +54,14 @@ __device__ __forceinline__ float load_as_f32(const void* p, int64_t i, tq4_dtype
     case TQ4_BF16: return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
     default: return static_cast<const float*>(p)[i];
   }
+}
+
+// Element i of a scale / zero-point array stored in T (4-byte f32, or 2-byte bf16 / f16).
+__device__ __forceinline__ float scale_to_f32(const void* base, int64_t i, int st_bytes, int bf) {
+  if (st_bytes == 4) return static_cast<const float*>(base)[i];
+  const uint16_t v = static_cast<const uint16_t*>(base)[i];
+  if (bf) return __uint_as_float(((uint32_t)v) << 16);
+  return __half2float(__ushort_as_half(v));
 }
 
 // One typed rounding of an f32 value that holds an exact result: the value of `x` rounded to t,

@@ -17,57 +17,11 @@
 // Every mbarrier wait is bounded by a clock deadline; a wait that runs out writes the device
 // status word, raises the CTA's abort flag and the CTA winds down (no trap, no endless spin).
 #include "internal.cuh"
+#include "sm100.cuh"
 
 namespace tq4 {
 
-// ---- PTX wrappers -------------------------------------------------------------------------------
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// About one second at the B200's clocks; a healthy stage completes in microseconds.
-constexpr long long kWaitCycles = 2000000000LL;
-
-// Waits for the phase `parity` of `bar`, unless the CTA aborted; false on timeout or abort.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          int32_t code) {
-  const long long t0 = clock64();
-  while (!mbar_try(bar, parity)) {
-    if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) {
-      report(code);
-      *abort_flag = 1;
-      return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
-                                            uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
-
+// ---- PTX wrappers (mbarrier / TMA in sm100.cuh) ---------------------------------------------------
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   // K-major, 128-byte swizzle: LBO 16 B (unused inside one atom), SBO 1024 B (8 rows x 128 B),
   // version 1 (sm_100), layout type 2 (SWIZZLE_128B), base offset 0 (1024-aligned atoms).
@@ -180,6 +134,7 @@ struct GemmArgs {
   int stage_bytes;
   int sc_off, zc_off;  // offsets of the staged scales / zero points within a stage
   int st_bytes;
+  int int_zp;      // zero points are integers (packed or absent): the fused dequant path applies
   const void* bias;
   tq4_dtype bias_t;
   void* y;
@@ -309,9 +264,50 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint8_t* sc = st + p.sc_off;
       const uint8_t* zc = st + p.zc_off;
       const int b0 = (kt * 128) >> p.bs_log2;
+      constexpr bool T_SAME = (BF && T == TQ4_BF16) || (!BF && T == TQ4_F16);
       for (int task = tid; task < BN * 4; task += 256) {
         const int r = task >> 2, t = task & 3;
         const uint4 v = *reinterpret_cast<const uint4*>(wp + r * 64 + t * 16);
+        if constexpr (T_SAME) {
+          if (p.int_zp) {
+            // T is the MMA type and the zero points are integers: (O + q) - (O + z) is exact, so
+            // one f16x2/bf16x2 op gives q - z straight from the magic-number value, and one more
+            // multiply gives RN_T((q - z) * s), the reference's weight.
+            const uint16_t* sc16 = reinterpret_cast<const uint16_t*>(sc);
+            const uint16_t* zc16 = reinterpret_cast<const uint16_t*>(zc);
+            uint32_t s2 = 0, oz2 = 0, oz16 = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              if (j == 0 || ((16 * j) & ((1 << p.bs_log2) - 1)) == 0) {  // a new block
+                const int lb = ((kt * 128 + 16 * j) >> p.bs_log2) - b0;
+                const uint32_t sv = sc16[lb * BN + r];
+                s2 = sv | (sv << 16);
+                const float z = p.has_zp ? scale_to_f32(zc16, lb * BN + r, 2, BF) : p.z_const;
+                oz2 = h2_splat((BF ? 128.f : 1024.f) + z, BF);  // O + z (exact)
+                oz16 = h2_splat(64.f + z, BF);                   // for the 16q pair (f16)
+              }
+              const uint32_t x = (j < 2) ? v.x : (j < 4) ? v.y : (j < 6) ? v.z : v.w;
+              const uint32_t src = (j & 1) ? (x >> 8) : x;
+              uint32_t d0, d1;
+              if (!BF) {
+                d0 = h2_sub(lop3_and_or(src, 0x000F000Fu, 0x64006400u), oz2, false);
+                const uint32_t r1 = lop3_and_or(src, 0x00F000F0u, 0x64006400u);  // 1024 + 16 q
+                // r1/16 - (64 + z) = q - z, one rounding of an exact value
+                asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d1) : "r"(r1), "r"(0x2C002C00u), "r"(oz16 ^ 0x80008000u));
+              } else {
+                d0 = h2_sub(lop3_and_or(src, 0x000F000Fu, 0x43004300u), oz2, true);
+                d1 = h2_sub(lop3_and_or(src >> 4, 0x000F000Fu, 0x43004300u), oz2, true);
+              }
+              uint2 out;
+              out.x = h2_mul(d0, s2, BF);
+              out.y = h2_mul(d1, s2, BF);
+              const int chunk = 2 * (j & 3) + (t >> 1);
+              uint8_t* dst = w16 + (j >> 2) * (BN * 128) + r * 128 + ((chunk ^ (r & 7)) << 4) + ((t & 1) << 3);
+              *reinterpret_cast<uint2*>(dst) = out;
+            }
+            continue;
+          }
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint32_t x = (j < 2) ? v.x : (j < 4) ? v.y : (j < 6) ? v.z : v.w;
@@ -422,9 +418,9 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-static tq4_status make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, uint64_t inner,
-                           uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
-                           uint32_t box_outer, CUtensorMapSwizzle sw) {
+tq4_status make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, uint64_t inner,
+                    uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                    uint32_t box_outer, CUtensorMapSwizzle sw) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     set_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -565,6 +561,7 @@ tq4_status run_gemm_tc(const Weight& w, const void* a, int64_t m, tq4_dtype a_t,
   args.K = (int)w.desc.K;
   args.ktiles = (int)w.groups;
   args.st_bytes = dtype_size(w.desc.dequant_dtype);
+  args.int_zp = w.desc.zp_kind != TQ4_ZP_FLOAT;
   args.bias = bias;
   args.bias_t = bias_t;
   args.y = y;

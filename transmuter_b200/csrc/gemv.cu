@@ -3,8 +3,8 @@
 // Math (the MatMulNBits clause, quantized.ex:30-46 with dequantize_weight/4 at :234-240):
 //   Y[m][n] = sum_k A[m][k] * (q[n][k] - z[n][b(k)]) * s[n][b(k)]
 // is evaluated per "segment" (a run of seg = min(block_size, group, 128) weights of one block).
-// The weights enter the tensor cores as magic-number floats O + q*c(k)^-1 straight out of one
-// LOP3 (O = 1024 for f16, 128 for bf16; c(k) is 1/16, 1/4, ... for the nibbles the mask leaves
+// The weights enter the tensor cores as magic-number floats O + q/c(k) straight out of one LOP3
+// (O = 1024 for f16, 128 for bf16; c(k) is 1/16, 1/4, ... for the nibbles the mask leaves
 // shifted, and the staged activation at k is multiplied by c(k) to match). With the staged
 // activations v(k) = RN(A[m][k] / E * c(k)) (E an exact power of two per segment chosen so that
 // v cannot overflow f16),
@@ -13,43 +13,60 @@
 // so zero points, scales and the magic offset cost a few FMAs per segment and each pair of
 // weights costs one LOP3 (plus one shift per 32-bit word).
 //
-// Work split: a tile is 16*WN weight rows x a K range of whole 64-byte groups; persistent CTAs
-// of 8 warps walk the tiles. Each warp owns 16 rows of the tile (mma.sync m16n8k16, weights as
-// the A operand) and every WK-th group of the range (WK = 8/WN). Activations and per-segment
-// factors are staged in shared memory once per K range; each tile's scales / zero points arrive
-// by cp.async (block-major, so each block's rows are one contiguous run) while its first weights
-// are in flight; the packed weights stream from HBM with 128-bit non-allocating loads, two
-// groups ahead. Warps that share rows reduce through shared memory; tiles that share rows
-// (split-K) reduce through a float workspace, the last CTA of a row tile doing the sum in a
-// fixed order (deterministic) and resetting its counter.
+// Structure: persistent CTAs of one TMA producer warp and 8 consumer warps walk "items" (128
+// weight rows x a K range). The producer streams each item's packed rows (one 128-row x 64-byte
+// box per group, so consumer reads of rows 64 bytes apart are bank-conflict free) and the
+// block-major scales / zero points of the same K range into a ring of mbarrier stages; it runs
+// ahead into the next item while the consumers finish the current one. Each consumer warp owns 16
+// rows (mma.sync m16n8k16, weights as the A operand). Activations are staged in shared memory once
+// per K range.
+//   M = 1: the MMA's 8 activation columns hold 8 different segments of the one activation row
+//          (column c takes segment c of the stage, the others see zero), so scales and zero points
+//          are applied once per stage (up to 8 segments) instead of once per segment.
+//   M > 1: the columns are activation rows; the correction runs at the end of each segment.
+// Items that share rows (split-K) reduce through a float workspace: the last CTA of a row tile
+// sums the partials in a fixed order (deterministic) and resets its counter.
 #include <map>
 #include <memory>
 #include <mutex>
 
 #include "internal.cuh"
+#include "sm100.cuh"
 
 namespace tq4 {
 
+constexpr int kRows = 128;            // weight rows per item (8 consumer warps x 16)
+constexpr int kScaleRows = 136;       // scale box height: 128 rows + 8 of padding (bank spread)
+constexpr int kConsumers = 256;
+constexpr int kGemvThreads = kConsumers + 32;
+constexpr int kMaxStages = 4;
+constexpr int kSmemBudget = 110 * 1024;  // two CTAs per SM
+
+enum GemvMode { kCols = 0, kSegMT1 = 1, kSegMT2 = 2 };
+
 struct GemvArgs {
-  const uint8_t* q;
-  int64_t row_bytes;
-  const void* scales;  // [blocks_pad][n_pad] in T
-  const void* zps;     // same, or null
-  float z_const;
-  int st_bf16;         // 2-byte scale storage is bf16 (else f16)
-  int K, N, M;
-  int bs_log2, seg_log2;
   const void* a;
   const void* bias;
   tq4_dtype bias_t;
   void* y;
   tq4_dtype y_t;
   int64_t ldy;
+  float z_const;
+  int has_zp;
+  int st_bytes, st_bf16;
+  int K, N, M;
+  int bs_log2, seg_log2;
   int groups;            // groups per row
-  int groups_per_split;  // CTA K range in groups
-  int wn;                // warps along N: 1, 2, 4 or 8
+  int groups_per_split;  // item K range in groups
+  int gps;               // groups per stage
+  int nbs;               // scale blocks per stage (box height)
+  int stages;
+  int stage_bytes, sc_off, zc_off;  // within a stage
+  int act_off, seg_off, bar_off;    // within the CTA's shared memory
+  int sk;                // staged activation row stride (elements)
+  int ctas_n;            // row tiles of 128
   int ksplit;
-  int ctas_n;            // row tiles; the persistent grid walks ctas_n * ksplit tiles
+  int items;
   int64_t n_pad;
   float* ws;
   int* counters;
@@ -118,7 +135,7 @@ __device__ __forceinline__ void weight_pairs(uint32_t x, int j, uint32_t& p0, ui
 }
 
 // The offset O of the magic-number weights and the activation factor c(k) that matches the
-// weight at position k (k is the position within the 64-byte group's elements).
+// weight at position k (k counted from the start of a 64-byte group).
 template <int BITS, bool BF, bool PRECISE>
 __device__ __forceinline__ float magic_offset() {
   if constexpr (BITS == 8 && BF) return 0.f;
@@ -156,33 +173,12 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
   }
 }
 
-__device__ __forceinline__ uint4 ld_stream(const uint8_t* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
-}
-
-__device__ __forceinline__ float scale_to_f32(const void* base, int64_t i, int st_bytes, int bf) {
-  if (st_bytes == 4) return static_cast<const float*>(base)[i];
-  const uint16_t v = static_cast<const uint16_t*>(base)[i];
-  if (bf) return __uint_as_float(((uint32_t)v) << 16);
-  return __half2float(__ushort_as_half(v));
-}
-
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int w) {
   return w == 0 ? v.x : (w == 1 ? v.y : (w == 2 ? v.z : v.w));
 }
 
-constexpr int kGemvThreads = 256;
-constexpr int kPrefetch = 2;  // groups per load batch (two batches in flight)
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
 }
 
 // Four consecutive activations A[m][k..k+3] as f32 (zeros past K). `vec` when a 4-wide load is
@@ -209,27 +205,28 @@ __device__ __forceinline__ void load_act4(const void* a, int64_t m, int64_t k, i
 }
 
 // Stages A[0:M][k0 : k0+kr] into shared memory as v(k) = RN(A / E * c(k)) in the MMA type, with
-// the per-segment factors {E, E*O*SV - (no zero points ? z*E*SA : 0), E*SA} as float4 [seg][m].
+// the per-segment factors {E, E*O*SV + (no zero points ? z*E*SA : 0), E*SA} as float4 [seg][mp].
 // Rows >= M are left as they are: their outputs are never stored, and an MMA output element
-// depends only on its own activation row.
+// depends only on its own activation row. Run by the 256 consumer threads.
 template <int BITS, tq4_dtype AT>
-__device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int kr, int sk, int mp,
+__device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int kr, int mp,
                                                   uint16_t* act, float4* segf) {
   constexpr bool BF = (AT == TQ4_BF16);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr bool PRECISE = (AT == TQ4_F32);
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
   const int vec_per_row = kr / 4;
   const int total = p.M * vec_per_row;
   const int total_pad = (total + 31) & ~31;  // whole warps take part in the shuffles
   const int L = (1 << p.seg_log2) >> 2;      // lanes per segment (<= 32)
   const bool vec = (p.K & 3) == 0;
-  constexpr bool PRECISE = (AT == TQ4_F32);
   const float O = magic_offset<BITS, BF, PRECISE>();
-  const bool fold_z = p.zps == nullptr;
-  for (int base = 0; base < total_pad; base += 4 * kGemvThreads) {
+  const bool fold_z = !p.has_zp;
+  for (int base = 0; base < total_pad; base += 4 * kConsumers) {
     float a4[4][4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {  // issue all loads first
-      const int v = base + u * kGemvThreads + threadIdx.x;
+      const int v = base + u * kConsumers + tid;
       if (v < total) {
         load_act4<AT>(p.a, v / vec_per_row, (int64_t)k0 + (v % vec_per_row) * 4, p.K, vec, a4[u]);
       } else {
@@ -239,8 +236,8 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      if (base + u * kGemvThreads + warp * 32 >= total_pad) continue;  // warp-uniform
-      const int v = base + u * kGemvThreads + threadIdx.x;
+      if (base + u * kConsumers + warp * 32 >= total_pad) continue;  // warp-uniform
+      const int v = base + u * kConsumers + tid;
       const int m = v / vec_per_row, kk = (v % vec_per_row) * 4;
       float mx = fmaxf(fmaxf(fabsf(a4[u][0]), fabsf(a4[u][1])), fmaxf(fabsf(a4[u][2]), fabsf(a4[u][3])));
       for (int off = 1; off < L; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -278,7 +275,7 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int
         uint2 packed;
         packed.x = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
         packed.y = (uint32_t)h[2] | ((uint32_t)h[3] << 16);
-        *reinterpret_cast<uint2*>(act + m * sk + kk) = packed;
+        *reinterpret_cast<uint2*>(act + m * p.sk + kk) = packed;
         if ((lane & (L - 1)) == 0) {
           const int s_idx = kk >> p.seg_log2;
           const float za = e_scale * sa;
@@ -290,325 +287,377 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int
   }
 }
 
-// Shared-memory plan of one CTA (identical on host and device).
-struct GemvSmem {
-  int sk, nseg, nblk_max;
-  int act_off, seg_off, sc_off, zc_off, red_off, total;
+// The item's K range.
+struct ItemRange {
+  int rt, split, g_begin, g_end, k0, kr;
 };
-
-__host__ __device__ inline GemvSmem gemv_smem_plan(int mt, int kr_max, int seg, int bs, int rows_cta,
-                                                   int st_bytes, bool zp) {
-  GemvSmem s{};
-  const int mp = 8 * mt;
-  s.sk = kr_max + 16;
-  s.nseg = kr_max / seg;
-  s.nblk_max = (kr_max + bs - 1) / bs + 1;
-  s.act_off = 0;
-  s.seg_off = (s.act_off + mp * s.sk * 2 + 15) / 16 * 16;
-  s.sc_off = s.seg_off + s.nseg * mp * 16;
-  s.zc_off = s.sc_off + (s.nblk_max * rows_cta * st_bytes + 15) / 16 * 16;
-  s.red_off = s.zc_off + (zp ? (s.nblk_max * rows_cta * st_bytes + 15) / 16 * 16 : 0);
-  s.total = s.red_off + 8 * 32 * mt * 4 * 4;
-  return s;
+__device__ __forceinline__ ItemRange item_range(const GemvArgs& p, int item, int G) {
+  ItemRange r;
+  r.split = item / p.ctas_n;
+  r.rt = item % p.ctas_n;
+  r.g_begin = r.split * p.groups_per_split;
+  r.g_end = min(p.groups, r.g_begin + p.groups_per_split);
+  r.k0 = r.g_begin * G;
+  r.kr = (r.g_end - r.g_begin) * G;
+  return r;
 }
 
-template <int BITS, tq4_dtype AT, int ST_BYTES, int MT>
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs p) {
+// Y (or a split-K partial) of one output.
+__device__ __forceinline__ void write_out(const GemvArgs& p, int split, int64_t n, int m, float v) {
+  if (p.ksplit == 1) {
+    if (n < p.N && m < p.M) {
+      if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
+      store_from_f32(p.y, (int64_t)m * p.ldy + n, p.y_t, v);
+    }
+  } else if (m < p.M) {
+    p.ws[((int64_t)split * p.M + m) * p.n_pad + n] = v;
+  }
+}
+
+template <int BITS, tq4_dtype AT, int MODE>
+__global__ void __launch_bounds__(kGemvThreads, 2)
+    gemv_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_s,
+                const __grid_constant__ CUtensorMap map_z, const GemvArgs p) {
   constexpr bool BF = (AT == TQ4_BF16);
+  constexpr bool PRECISE = (AT == TQ4_F32);
   constexpr int G = 512 / BITS;  // elements per 64-byte group
   constexpr int STEPS = G / 16;
   constexpr int STEPS_PER_WORD = 32 / BITS / 4;  // 2 (4-bit), 4 (2-bit), 1 (8-bit)
-  constexpr int MP = 8 * MT;
-  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int MT = (MODE == kSegMT2) ? 2 : 1;
+  constexpr int MP = (MODE == kCols) ? 1 : 8 * MT;  // staged activation rows
+  extern __shared__ uint8_t smem_raw[];
   __shared__ int s_last;
+  // stages start 1024-byte aligned (TMA destinations)
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t sbase = (raw_addr + 1023) & ~1023u;
+  uint8_t* smem = smem_raw + (sbase - raw_addr);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t bars = sbase + p.bar_off;
+  const int S = p.stages;
+  auto full = [&](int s) { return bars + 8 * s; };
+  auto empty = [&](int s) { return bars + 8 * (kMaxStages + s); };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + p.bar_off + 8 * 2 * kMaxStages);
+
+  // this CTA's items: a contiguous range, so consecutive items mostly share their K range
+  const int it0 = (int)((int64_t)blockIdx.x * p.items / gridDim.x);
+  const int it1 = (int)((int64_t)(blockIdx.x + 1) * p.items / gridDim.x);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 8);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == 8) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int gs = 0;  // global stage counter (same sequence as the consumers)
+      bool ok = true;
+      for (int item = it0; item < it1 && ok; ++item) {
+        const ItemRange r = item_range(p, item, G);
+        const int row0 = r.rt * kRows;
+        for (int c0 = r.g_begin; c0 < r.g_end; c0 += p.gps, ++gs) {
+          const int s = gs % S;
+          if (!mbar_wait(empty(s), ((gs / S) & 1) ^ 1, abort_flag, kDevTimeoutStageEmpty)) {
+            ok = false;
+            break;
+          }
+          const int ng = min(p.gps, r.g_end - c0);
+          const int b0 = (c0 * G) >> p.bs_log2;
+          const uint32_t st = sbase + s * p.stage_bytes;
+          const uint32_t sc_bytes = kScaleRows * p.nbs * p.st_bytes;
+          mbar_expect_tx(full(s), ng * kRows * 64 + sc_bytes * (p.has_zp ? 2 : 1));
+          for (int gi = 0; gi < ng; ++gi) tma_load_2d(st + gi * kRows * 64, &map_w, (c0 + gi) * 64, row0, full(s));
+          tma_load_2d(st + p.sc_off, &map_s, row0, b0, full(s));
+          if (p.has_zp) tma_load_2d(st + p.zc_off, &map_z, row0, b0, full(s));
+        }
+      }
+      // the copies still in flight land before the CTA exits (bounded)
+      for (int g = max(0, gs - S); g < gs; ++g) mbar_drain(full(g % S), (g / S) & 1);
+    }
+    return;  // the producer takes part in no consumer barrier
+  }
+
+  // ---------------- consumers ----------------
   const int g = lane >> 2, t = lane & 3;
-  const int wn = p.wn, wk = 8 / wn;
-  const int warp_n = warp % wn, warp_k = warp / wn;
-  const int rows_cta = 16 * wn;
+  const int rl = warp * 16 + g;  // this thread's first row within the item
+  uint16_t* act = reinterpret_cast<uint16_t*>(smem + p.act_off);
+  float4* segf = reinterpret_cast<float4*>(smem + p.seg_off);
   const int seg_log2 = p.seg_log2;
   const int seg = 1 << seg_log2;
-  const bool has_zp = p.zps != nullptr;
-  const GemvSmem L = gemv_smem_plan(MT, p.groups_per_split * G, seg, 1 << p.bs_log2, rows_cta,
-                                    ST_BYTES, has_zp);
-  uint16_t* act = reinterpret_cast<uint16_t*>(smem + L.act_off);
-  float4* segf = reinterpret_cast<float4*>(smem + L.seg_off);
-  uint8_t* sc = smem + L.sc_off;
-  uint8_t* zc = smem + L.zc_off;
-  float* red = reinterpret_cast<float*>(smem + L.red_off);
-  const int sk = L.sk;
-
-  const int tiles = p.ctas_n * p.ksplit;
+  int gs = 0;
   int staged_split = -1;
-  for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-    const int split = tile / p.ctas_n, rt = tile % p.ctas_n;
-    const int64_t cta_row0 = (int64_t)rt * rows_cta;
-    const int64_t row0 = cta_row0 + warp_n * 16;
-    const int g_begin = split * p.groups_per_split;
-    const int g_end = min(p.groups, g_begin + p.groups_per_split);
-    const int kr = (g_end - g_begin) * G;
-    const int k0 = g_begin * G;
-    const int b_first = k0 >> p.bs_log2;
-    const int nblk = ((k0 + kr - 1) >> p.bs_log2) - b_first + 1;
+  bool ok = true;
 
-    // -- scales / zero points of this tile: per block, the tile's rows are one contiguous run
-    const int c16 = rows_cta * ST_BYTES / 16;  // 16-byte chunks per block
-    for (int i = threadIdx.x; i < nblk * c16; i += kGemvThreads) {
-      const int bb = i / c16, c = i % c16;
-      const int64_t src = ((int64_t)(b_first + bb) * p.n_pad + cta_row0) * ST_BYTES + c * 16;
-      cp_async16(sc + (bb * rows_cta) * ST_BYTES + c * 16, static_cast<const uint8_t*>(p.scales) + src);
-      if (has_zp) cp_async16(zc + (bb * rows_cta) * ST_BYTES + c * 16, static_cast<const uint8_t*>(p.zps) + src);
+  for (int item = it0; item < it1; ++item) {
+    const ItemRange r = item_range(p, item, G);
+    if (r.split != staged_split) {  // activations for this K range
+      consumer_sync();              // everyone is done with the previous range
+      stage_activations<BITS, AT>(p, r.k0, r.kr, MP, act, segf);
+      staged_split = r.split;
+      consumer_sync();
     }
 
-    // -- the first weight batch
-    const uint8_t* rowg = p.q + (row0 + g) * p.row_bytes + t * 16;
-    const uint8_t* rowg8 = rowg + 8 * p.row_bytes;
-    uint4 xa[kPrefetch], xb[kPrefetch];  // the batch being computed
-    uint4 na[kPrefetch], nb[kPrefetch];  // the next batch, in flight
-    const int c_first = g_begin + warp_k;
-#pragma unroll
-    for (int d = 0; d < kPrefetch; ++d) {
-      const int c = c_first + d * wk;
-      xa[d] = xb[d] = make_uint4(0, 0, 0, 0);
-      if (c < g_end) {
-        xa[d] = ld_stream(rowg + (int64_t)c * 64);
-        xb[d] = ld_stream(rowg8 + (int64_t)c * 64);
-      }
-    }
-
-    // -- activations, once per K range
-    if (split != staged_split) {
-      stage_activations<BITS, AT>(p, k0, kr, sk, MP, act, segf);
-      staged_split = split;
-    }
-    cp_async_wait_all();
-    __syncthreads();
-
-    // -- main loop over this warp's groups
-    float acc[MT][4], blk[MT][4];
+    float acc[MT][4];   // kSeg*: finished outputs; kCols: per-thread partial sums of 2 rows
+    float blk[MT][4];   // MMA accumulators
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[mt][i] = blk[mt][i] = 0.f;
-    const int rl_g = warp_n * 16 + g;
 
-    for (int cb = c_first; cb < g_end; cb += kPrefetch * wk) {
-      const int cn = cb + kPrefetch * wk;
+    for (int c0 = r.g_begin; c0 < r.g_end; c0 += p.gps, ++gs) {
+      const int s = gs % S;
+      if (ok) ok = mbar_wait(full(s), (gs / S) & 1, abort_flag, kDevTimeoutTmaFull);
+      if (ok) {
+        const int ng = min(p.gps, r.g_end - c0);
+        const uint8_t* st = smem + s * p.stage_bytes;
+        const uint8_t* sc = st + p.sc_off;
+        const uint8_t* zc = st + p.zc_off;
+        const int b0 = (c0 * G) >> p.bs_log2;
+        const int ks = (c0 - r.g_begin) * G;  // stage start within the staged activations
+        for (int gi = 0; gi < ng; ++gi) {
+          const uint4 xa = *reinterpret_cast<const uint4*>(st + gi * kRows * 64 + rl * 64 + t * 16);
+          const uint4 xb = *reinterpret_cast<const uint4*>(st + gi * kRows * 64 + (rl + 8) * 64 + t * 16);
 #pragma unroll
-      for (int d = 0; d < kPrefetch; ++d) {
-        const int c = cn + d * wk;
-        na[d] = nb[d] = make_uint4(0, 0, 0, 0);
-        if (c < g_end) {
-          na[d] = ld_stream(rowg + (int64_t)c * 64);
-          nb[d] = ld_stream(rowg8 + (int64_t)c * 64);
-        }
-      }
+          for (int j = 0; j < STEPS; ++j) {
+            const int w = j / STEPS_PER_WORD;
+            uint32_t a0, a1, a2, a3;
+            weight_pairs<BITS, BF, PRECISE>(word_of(xa, w), j, a0, a2);
+            weight_pairs<BITS, BF, PRECISE>(word_of(xb, w), j, a1, a3);
+            const int kk = ks + gi * G + 16 * j + 4 * t;
+            if constexpr (MODE == kCols) {
+              // column g takes segment g of the stage; the other columns see zero
+              const int col = (gi * G + 16 * j) >> seg_log2;
+              const uint2 bv = *reinterpret_cast<const uint2*>(act + kk);
+              const bool mine = (g == col);
+              mma16816<BF>(blk[0], a0, a1, a2, a3, mine ? bv.x : 0u, mine ? bv.y : 0u);
+            } else {
 #pragma unroll
-      for (int d = 0; d < kPrefetch; ++d) {
-        const int c = cb + d * wk;
-        if (c >= g_end) break;
-        const int kc = (c - g_begin) * G;
+              for (int mt = 0; mt < MT; ++mt) {
+                const uint2 bv = *reinterpret_cast<const uint2*>(act + (mt * 8 + g) * p.sk + kk);
+                mma16816<BF>(blk[mt], a0, a1, a2, a3, bv.x, bv.y);
+              }
+              if ((((j + 1) * 16) & (seg - 1)) == 0) {  // end of a segment
+                const int kseg = ks + gi * G + (j + 1) * 16 - seg;  // within the staged range
+                const int s_idx = kseg >> seg_log2;
+                const int lb = ((r.k0 + kseg) >> p.bs_log2) - b0;
+                const float s_g = scale_to_f32(sc, lb * kScaleRows + rl, p.st_bytes, p.st_bf16);
+                const float s_g8 = scale_to_f32(sc, lb * kScaleRows + rl + 8, p.st_bytes, p.st_bf16);
+                const float z_g = p.has_zp ? scale_to_f32(zc, lb * kScaleRows + rl, p.st_bytes, p.st_bf16) : 0.f;
+                const float z_g8 = p.has_zp ? scale_to_f32(zc, lb * kScaleRows + rl + 8, p.st_bytes, p.st_bf16) : 0.f;
 #pragma unroll
-        for (int j = 0; j < STEPS; ++j) {
-          const int w = j / STEPS_PER_WORD;
-          uint32_t a0, a1, a2, a3;
-          weight_pairs<BITS, BF, AT == TQ4_F32>(word_of(xa[d], w), j, a0, a2);
-          weight_pairs<BITS, BF, AT == TQ4_F32>(word_of(xb[d], w), j, a1, a3);
-          const int kk = kc + 16 * j + 4 * t;
+                for (int mt = 0; mt < MT; ++mt) {
+                  const int m0 = mt * 8 + 2 * t;
+                  const float4 F0 = segf[s_idx * MP + m0], F1 = segf[s_idx * MP + m0 + 1];
+                  acc[mt][0] = fmaf(s_g, fmaf(-z_g, F0.z, fmaf(F0.x, blk[mt][0], -F0.y)), acc[mt][0]);
+                  acc[mt][1] = fmaf(s_g, fmaf(-z_g, F1.z, fmaf(F1.x, blk[mt][1], -F1.y)), acc[mt][1]);
+                  acc[mt][2] = fmaf(s_g8, fmaf(-z_g8, F0.z, fmaf(F0.x, blk[mt][2], -F0.y)), acc[mt][2]);
+                  acc[mt][3] = fmaf(s_g8, fmaf(-z_g8, F1.z, fmaf(F1.x, blk[mt][3], -F1.y)), acc[mt][3]);
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-            const uint2 bv = *reinterpret_cast<const uint2*>(act + (mt * 8 + g) * sk + kk);
-            mma16816<BF>(blk[mt], a0, a1, a2, a3, bv.x, bv.y);
-          }
-          if ((((j + 1) * 16) & (seg - 1)) == 0) {  // end of a segment
-            const int s_idx = (kc + (j + 1) * 16 - seg) >> seg_log2;
-            const int bb = ((k0 + s_idx * seg) >> p.bs_log2) - b_first;
-            const float s_g = scale_to_f32(sc, bb * rows_cta + rl_g, ST_BYTES, p.st_bf16);
-            const float s_g8 = scale_to_f32(sc, bb * rows_cta + rl_g + 8, ST_BYTES, p.st_bf16);
-            const float z_g = has_zp ? scale_to_f32(zc, bb * rows_cta + rl_g, ST_BYTES, p.st_bf16) : 0.f;
-            const float z_g8 = has_zp ? scale_to_f32(zc, bb * rows_cta + rl_g + 8, ST_BYTES, p.st_bf16) : 0.f;
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-              const int m0 = mt * 8 + 2 * t;
-              const float4 F0 = segf[s_idx * MP + m0], F1 = segf[s_idx * MP + m0 + 1];
-              // s * (E*P - X - z*ZA); without zero points X already holds z_const*ZA
-              acc[mt][0] = fmaf(s_g, fmaf(-z_g, F0.z, fmaf(F0.x, blk[mt][0], -F0.y)), acc[mt][0]);
-              acc[mt][1] = fmaf(s_g, fmaf(-z_g, F1.z, fmaf(F1.x, blk[mt][1], -F1.y)), acc[mt][1]);
-              acc[mt][2] = fmaf(s_g8, fmaf(-z_g8, F0.z, fmaf(F0.x, blk[mt][2], -F0.y)), acc[mt][2]);
-              acc[mt][3] = fmaf(s_g8, fmaf(-z_g8, F1.z, fmaf(F1.x, blk[mt][3], -F1.y)), acc[mt][3]);
-#pragma unroll
-              for (int i = 0; i < 4; ++i) blk[mt][i] = 0.f;
+                  for (int i = 0; i < 4; ++i) blk[mt][i] = 0.f;
+                }
+              }
             }
           }
         }
-      }
+        if constexpr (MODE == kCols) {
+          // columns 2t and 2t+1 hold segments 2t and 2t+1 of this stage
+          const int nseg_stage = (ng * G) >> seg_log2;
 #pragma unroll
-      for (int d = 0; d < kPrefetch; ++d) {
-        xa[d] = na[d];
-        xb[d] = nb[d];
-      }
-    }
-
-    // -- reduce the warps that share rows (fixed order)
-    if (wk > 1) {
-      if (warp_k > 0) {
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) red[(warp * 32 + lane) * (MT * 4) + mt * 4 + i] = acc[mt][i];
-      }
-      __syncthreads();
-      if (warp_k == 0) {
-        for (int kk = 1; kk < wk; ++kk) {
-          const int src = (kk * wn + warp_n) * 32 + lane;
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[mt][i] += red[src * (MT * 4) + mt * 4 + i];
-        }
-      }
-    }
-
-    const int64_t n_g = row0 + g, n_g8 = row0 + g + 8;
-    if (p.ksplit == 1) {
-      if (warp_k == 0) {
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int m = mt * 8 + 2 * t + (i & 1);
-            const int64_t n = (i < 2) ? n_g : n_g8;
-            if (m < p.M && n < p.N) {
-              float v = acc[mt][i];
-              if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
-              store_from_f32(p.y, (int64_t)m * p.ldy + n, p.y_t, v);
+          for (int h = 0; h < 2; ++h) {
+            const int sg = 2 * t + h;
+            if (sg < nseg_stage) {
+              const int kseg = ks + (sg << seg_log2);
+              const int lb = ((r.k0 + kseg) >> p.bs_log2) - b0;
+              const float4 F = segf[kseg >> seg_log2];
+              const float s_g = scale_to_f32(sc, lb * kScaleRows + rl, p.st_bytes, p.st_bf16);
+              const float s_g8 = scale_to_f32(sc, lb * kScaleRows + rl + 8, p.st_bytes, p.st_bf16);
+              float z_g = 0.f, z_g8 = 0.f;
+              if (p.has_zp) {
+                z_g = scale_to_f32(zc, lb * kScaleRows + rl, p.st_bytes, p.st_bf16);
+                z_g8 = scale_to_f32(zc, lb * kScaleRows + rl + 8, p.st_bytes, p.st_bf16);
+              }
+              acc[0][0] = fmaf(s_g, fmaf(-z_g, F.z, fmaf(F.x, blk[0][h], -F.y)), acc[0][0]);
+              acc[0][2] = fmaf(s_g8, fmaf(-z_g8, F.z, fmaf(F.x, blk[0][2 + h], -F.y)), acc[0][2]);
             }
           }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) blk[0][i] = 0.f;
         }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty(s));  // this warp is done with the stage
+    }
+
+    // ---- outputs of the item: rows row0 + rl (and + 8)
+    const int64_t n_g = (int64_t)r.rt * kRows + rl, n_g8 = n_g + 8;
+    if constexpr (MODE == kCols) {
+      float y0 = acc[0][0], y8 = acc[0][2];
+      y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+      y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+      y8 += __shfl_xor_sync(0xffffffffu, y8, 1);
+      y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
+      if (t == 0) {
+        write_out(p, r.split, n_g, 0, y0);
+        write_out(p, r.split, n_g8, 0, y8);
       }
     } else {
-      // split-K: write this tile's partial; the last CTA of the row tile sums them in order
-      if (warp_k == 0) {
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
+      for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int m = mt * 8 + 2 * t + (i & 1);
-            const int64_t n = (i < 2) ? n_g : n_g8;
-            if (m < p.M) p.ws[((int64_t)split * p.M + m) * p.n_pad + n] = acc[mt][i];
-          }
-      }
+        for (int i = 0; i < 4; ++i)
+          write_out(p, r.split, (i < 2) ? n_g : n_g8, mt * 8 + 2 * t + (i & 1), acc[mt][i]);
+    }
+    if (p.ksplit > 1) {
+      // the last item of a row tile sums the partials in split order
       __threadfence();
-      __syncthreads();
+      consumer_sync();
       if (threadIdx.x == 0) {
-        const int prev = atomicAdd(&p.counters[rt], 1);
+        const int prev = atomicAdd(&p.counters[r.rt], 1);
         s_last = (prev == p.ksplit - 1);
         if (prev >= p.ksplit) report(kDevTimeoutSplitK);  // a counter left non-zero earlier
       }
-      __syncthreads();
+      consumer_sync();
       if (s_last) {
         __threadfence();
-        const int outputs = rows_cta * p.M;
-        for (int i = threadIdx.x; i < outputs; i += kGemvThreads) {
-          const int m = i / rows_cta;
-          const int64_t n = cta_row0 + (i % rows_cta);
+        for (int i = threadIdx.x; i < kRows * p.M; i += kConsumers) {
+          const int m = i / kRows;
+          const int64_t n = (int64_t)r.rt * kRows + (i % kRows);
           if (n >= p.N) continue;
           float v = 0.f;
-          for (int s = 0; s < p.ksplit; ++s) v += __ldcg(&p.ws[((int64_t)s * p.M + m) * p.n_pad + n]);
+          for (int sp = 0; sp < p.ksplit; ++sp) v += __ldcg(&p.ws[((int64_t)sp * p.M + m) * p.n_pad + n]);
           if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
           store_from_f32(p.y, (int64_t)m * p.ldy + n, p.y_t, v);
         }
-        if (threadIdx.x == 0) p.counters[rt] = 0;
+        if (threadIdx.x == 0) p.counters[r.rt] = 0;
       }
+      consumer_sync();
     }
-    __syncthreads();  // the tile's shared data (scales, reduction) is free again
   }
 }
 
 // ---- host side --------------------------------------------------------------------------------
 struct GemvPlan {
-  int wn, ksplit, groups_per_split, mt, ctas_n;
-  size_t smem;
+  int mode, ksplit, groups_per_split, ctas_n, stages, stage_bytes, sc_off, zc_off, act_off,
+      seg_off, bar_off, sk, smem, items;
 };
+
+static int seg_of(const Weight& w) {
+  const int G = 512 / w.desc.bits;
+  return std::min<int>(std::min(w.desc.block_size, G), 128);
+}
+
+// Groups per stage and scale blocks per stage of a handle (fixed at creation: the TMA boxes).
+void gemv_stage_shape(const Weight& w, int* gps, int* nbs) {
+  const int G = 512 / w.desc.bits;
+  const int spg = G / seg_of(w);  // segments per group
+  *gps = std::max(1, std::min(4, 8 / spg));
+  const int span = *gps * G;
+  *nbs = w.desc.block_size <= span ? span / w.desc.block_size : 1;
+}
 
 static GemvPlan plan_gemv(const Weight& w, int64_t m) {
   GemvPlan pl{};
-  const int bits = w.desc.bits;
-  const int G = 512 / bits;
-  const int seg = std::min<int>(std::min(w.desc.block_size, G), 128);
-  pl.mt = m <= 8 ? 1 : 2;
-  const int sms = w.num_sms;
-  const int target = 2 * sms;
+  const int G = 512 / w.desc.bits;
+  const int seg = seg_of(w);
+  const int spg = G / seg;
+  const int gps = w.gv_gps;
+  pl.mode = (m == 1 && spg * gps <= 8) ? kCols : (m <= 8 ? kSegMT1 : kSegMT2);
+  const int mp = pl.mode == kCols ? 1 : (pl.mode == kSegMT1 ? 8 : 16);
+  pl.ctas_n = (int)(w.n_pad / kRows);
   const int64_t groups = w.groups;
-  pl.wn = 1;
-  for (int wn = 8; wn >= 1; wn >>= 1) {
-    const int64_t ctas = (w.n_pad + 16 * wn - 1) / (16 * wn);
-    if (ctas >= target || wn == 1) {
-      pl.wn = wn;
-      break;
-    }
-  }
-  pl.ctas_n = (int)((w.n_pad + 16 * pl.wn - 1) / (16 * pl.wn));
-  const int wk = 8 / pl.wn;
+  const int target = 2 * w.num_sms;
+  // split K for parallelism (enough items for every CTA) and for the activation staging to fit
   int ksplit = 1;
-  if (pl.ctas_n < target) ksplit = (int)std::min<int64_t>((target + pl.ctas_n - 1) / pl.ctas_n,
-                                                         std::max<int64_t>(1, groups / wk));
-  const size_t budget = 100 * 1024;
-  const bool zp = w.zps.ptr != nullptr;
-  const int st_bytes = w.desc.dequant_dtype == TQ4_F32 ? 4 : 2;
-  const int rows_cta = 16 * pl.wn;
+  if (pl.ctas_n < target) ksplit = (int)std::min<int64_t>((target + pl.ctas_n - 1) / pl.ctas_n, groups);
+  const int st = dtype_size(w.desc.dequant_dtype);
+  const int w_bytes = gps * kRows * 64;
+  const int sc_bytes = (kScaleRows * w.gv_nbs * st + 127) / 128 * 128;
+  pl.sc_off = w_bytes;
+  pl.zc_off = pl.sc_off + sc_bytes;
+  pl.stage_bytes = (pl.zc_off + (w.zps.ptr ? sc_bytes : 0) + 1023) / 1024 * 1024;
   for (;;) {
-    const int gps = (int)((groups + ksplit - 1) / ksplit);
-    const GemvSmem s = gemv_smem_plan(pl.mt, gps * G, seg, w.desc.block_size, rows_cta, st_bytes, zp);
-    if ((size_t)s.total <= budget || gps == 1) {
-      pl.groups_per_split = gps;
-      pl.smem = s.total;
+    // whole stages per item: a stage then never straddles the blocks of its scale box
+    const int gps_split = (int)(((groups + ksplit - 1) / ksplit + gps - 1) / gps * gps);
+    const int kr = gps_split * G;
+    pl.sk = kr + 16;
+    const int act_bytes = ((mp == 1 ? kr : mp * pl.sk) * 2 + 15) / 16 * 16;
+    const int seg_bytes = (kr / seg) * mp * 16;
+    const int fixed = act_bytes + seg_bytes + 8 * 2 * kMaxStages + 16;
+    const int stages = std::min(kMaxStages, (kSmemBudget - fixed) / pl.stage_bytes);
+    if (stages >= 2 || gps_split <= gps) {
+      pl.groups_per_split = gps_split;
+      pl.stages = std::max(2, stages);
+      pl.act_off = pl.stages * pl.stage_bytes;
+      pl.seg_off = pl.act_off + act_bytes;
+      pl.bar_off = pl.seg_off + seg_bytes;
+      pl.smem = pl.bar_off + 8 * 2 * kMaxStages + 16;
       break;
     }
     ++ksplit;
   }
   pl.ksplit = (int)((groups + pl.groups_per_split - 1) / pl.groups_per_split);
+  pl.items = pl.ctas_n * pl.ksplit;
   return pl;
 }
 
-template <int BITS, tq4_dtype AT, int ST, int MT>
-static cudaError_t launch_gemv_t(const GemvArgs& args, int tiles, int sms, size_t smem, cudaStream_t st) {
-  auto kern = gemv_kernel<BITS, AT, ST, MT>;
-  // attribute and occupancy once per instantiation (the shared-memory budget is fixed)
-  static int per_sm = 0;
-  if (per_sm == 0) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024 + 1024);
+template <int BITS, tq4_dtype AT, int MODE>
+static cudaError_t launch_gemv_t(const Weight& w, const GemvArgs& args, int smem, cudaStream_t st) {
+  auto kern = gemv_kernel<BITS, AT, MODE>;
+  static bool attr_set = false;  // once per instantiation
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 1024);
     if (e != cudaSuccess) return e;
-    int n = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kGemvThreads, 100 * 1024);
-    if (e != cudaSuccess) return e;
-    per_sm = std::max(1, n);
+    attr_set = true;
   }
-  const int grid = std::min(tiles, per_sm * sms);
-  kern<<<grid, kGemvThreads, smem, st>>>(args);
+  const int grid = std::min(args.items, 2 * w.num_sms);
+  kern<<<grid, kGemvThreads, smem + 1024, st>>>(w.gv_wmap, w.gv_smap, w.gv_zmap, args);
   return cudaGetLastError();
 }
 
 template <int BITS, tq4_dtype AT>
-static cudaError_t launch_gemv_st(const GemvArgs& args, int st_bytes, int mt, int tiles, int sms,
-                                  size_t smem, cudaStream_t st) {
-  if (st_bytes == 4) {
-    return mt == 1 ? launch_gemv_t<BITS, AT, 4, 1>(args, tiles, sms, smem, st)
-                   : launch_gemv_t<BITS, AT, 4, 2>(args, tiles, sms, smem, st);
+static cudaError_t launch_gemv_mode(const Weight& w, const GemvArgs& args, int mode, int smem,
+                                    cudaStream_t st) {
+  switch (mode) {
+    case kCols: return launch_gemv_t<BITS, AT, kCols>(w, args, smem, st);
+    case kSegMT1: return launch_gemv_t<BITS, AT, kSegMT1>(w, args, smem, st);
+    default: return launch_gemv_t<BITS, AT, kSegMT2>(w, args, smem, st);
   }
-  return mt == 1 ? launch_gemv_t<BITS, AT, 2, 1>(args, tiles, sms, smem, st)
-                 : launch_gemv_t<BITS, AT, 2, 2>(args, tiles, sms, smem, st);
 }
 
 template <int BITS>
-static cudaError_t launch_gemv_bits(const GemvArgs& args, tq4_dtype a_t, int st_bytes, int mt,
-                                    int tiles, int sms, size_t smem, cudaStream_t st) {
+static cudaError_t launch_gemv_bits(const Weight& w, const GemvArgs& args, tq4_dtype a_t, int mode,
+                                    int smem, cudaStream_t st) {
   switch (a_t) {
-    case TQ4_F16: return launch_gemv_st<BITS, TQ4_F16>(args, st_bytes, mt, tiles, sms, smem, st);
-    case TQ4_BF16: return launch_gemv_st<BITS, TQ4_BF16>(args, st_bytes, mt, tiles, sms, smem, st);
-    default: return launch_gemv_st<BITS, TQ4_F32>(args, st_bytes, mt, tiles, sms, smem, st);
+    case TQ4_F16: return launch_gemv_mode<BITS, TQ4_F16>(w, args, mode, smem, st);
+    case TQ4_BF16: return launch_gemv_mode<BITS, TQ4_BF16>(w, args, mode, smem, st);
+    default: return launch_gemv_mode<BITS, TQ4_F32>(w, args, mode, smem, st);
   }
+}
+
+// The GEMV's TMA descriptors of a new handle: one 128-row x 64-byte box of packed rows, and
+// 136-row x (blocks of a stage) boxes of the block-major scales / zero points.
+tq4_status make_gemv_maps(Weight& w) {
+  w.gv_maps_ok = false;
+  gemv_stage_shape(w, &w.gv_gps, &w.gv_nbs);
+  const int st = dtype_size(w.desc.dequant_dtype);
+  const CUtensorMapDataType sdt = st == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  TQ4_TRY(make_map(&w.gv_wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.q.ptr, w.row_bytes, w.n_pad,
+                   w.row_bytes, 64, kRows, CU_TENSOR_MAP_SWIZZLE_NONE));
+  TQ4_TRY(make_map(&w.gv_smap, sdt, w.scales.ptr, w.n_pad, w.blocks_pad, w.n_pad * st, kScaleRows,
+                   w.gv_nbs, CU_TENSOR_MAP_SWIZZLE_NONE));
+  if (w.zps.ptr)
+    TQ4_TRY(make_map(&w.gv_zmap, sdt, w.zps.ptr, w.n_pad, w.blocks_pad, w.n_pad * st, kScaleRows,
+                     w.gv_nbs, CU_TENSOR_MAP_SWIZZLE_NONE));
+  else
+    w.gv_zmap = w.gv_smap;  // never loaded
+  w.gv_maps_ok = true;
+  return TQ4_OK;
 }
 
 // Per-stream split-K workspaces of a handle: calls on different streams may overlap on the GPU,
@@ -654,34 +703,44 @@ tq4_status gemv_workspace(const Weight& w, cudaStream_t st, int64_t ws_bytes, in
 tq4_status run_gemv_with(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,
                          tq4_dtype bias_t, void* y, tq4_dtype y_t, int64_t ldy, cudaStream_t st,
                          float* ws, int* counters, int64_t ws_capacity_floats, int64_t ctr_capacity) {
+  if (!w.gv_maps_ok) {
+    set_error("GEMV: the handle has no TMA descriptors");
+    return TQ4_ERR_CUDA;
+  }
   const GemvPlan pl = plan_gemv(w, m);
   GemvArgs args{};
-  args.q = static_cast<const uint8_t*>(w.q.ptr);
-  args.row_bytes = w.row_bytes;
-  args.scales = w.scales.ptr;
-  args.zps = w.zps.ptr;
-  args.z_const = w.z_const;
-  args.st_bf16 = w.desc.dequant_dtype == TQ4_BF16;
-  args.K = (int)w.desc.K;
-  args.N = (int)w.desc.N;
-  args.M = (int)m;
-  args.bs_log2 = w.bs_log2;
-  const int G = 512 / w.desc.bits;
-  const int seg = std::min<int>(std::min(w.desc.block_size, G), 128);
-  int seg_log2 = 0;
-  while ((1 << seg_log2) < seg) ++seg_log2;
-  args.seg_log2 = seg_log2;
   args.a = a;
   args.bias = bias;
   args.bias_t = bias_t;
   args.y = y;
   args.y_t = y_t;
   args.ldy = ldy;
+  args.z_const = w.z_const;
+  args.has_zp = w.zps.ptr != nullptr;
+  args.st_bytes = dtype_size(w.desc.dequant_dtype);
+  args.st_bf16 = w.desc.dequant_dtype == TQ4_BF16;
+  args.K = (int)w.desc.K;
+  args.N = (int)w.desc.N;
+  args.M = (int)m;
+  args.bs_log2 = w.bs_log2;
+  int seg_log2 = 0;
+  while ((1 << seg_log2) < seg_of(w)) ++seg_log2;
+  args.seg_log2 = seg_log2;
   args.groups = (int)w.groups;
   args.groups_per_split = pl.groups_per_split;
-  args.wn = pl.wn;
-  args.ksplit = pl.ksplit;
+  args.gps = w.gv_gps;
+  args.nbs = w.gv_nbs;
+  args.stages = pl.stages;
+  args.stage_bytes = pl.stage_bytes;
+  args.sc_off = pl.sc_off;
+  args.zc_off = pl.zc_off;
+  args.act_off = pl.act_off;
+  args.seg_off = pl.seg_off;
+  args.bar_off = pl.bar_off;
+  args.sk = pl.sk;
   args.ctas_n = pl.ctas_n;
+  args.ksplit = pl.ksplit;
+  args.items = pl.items;
   args.n_pad = w.n_pad;
   if (pl.ksplit > 1) {
     const int64_t need = (int64_t)pl.ksplit * m * w.n_pad;
@@ -693,12 +752,10 @@ tq4_status run_gemv_with(const Weight& w, const void* a, int64_t m, tq4_dtype a_
     args.ws = ws;
     args.counters = counters;
   }
-  const int tiles = pl.ctas_n * pl.ksplit;
-  const int st_bytes = w.desc.dequant_dtype == TQ4_F32 ? 4 : 2;
   cudaError_t e;
-  if (w.desc.bits == 4) e = launch_gemv_bits<4>(args, a_t, st_bytes, pl.mt, tiles, w.num_sms, pl.smem, st);
-  else if (w.desc.bits == 2) e = launch_gemv_bits<2>(args, a_t, st_bytes, pl.mt, tiles, w.num_sms, pl.smem, st);
-  else e = launch_gemv_bits<8>(args, a_t, st_bytes, pl.mt, tiles, w.num_sms, pl.smem, st);
+  if (w.desc.bits == 4) e = launch_gemv_bits<4>(w, args, a_t, pl.mode, pl.smem, st);
+  else if (w.desc.bits == 2) e = launch_gemv_bits<2>(w, args, a_t, pl.mode, pl.smem, st);
+  else e = launch_gemv_bits<8>(w, args, a_t, pl.mode, pl.smem, st);
   if (e != cudaSuccess) {
     set_error("GEMV launch failed: %s", cudaGetErrorString(e));
     return TQ4_ERR_CUDA;

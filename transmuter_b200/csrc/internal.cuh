@@ -14,6 +14,19 @@ namespace tq4 {
 
 // Thread-local last error message (tq4_last_error).
 void set_error(const char* fmt, ...);
+void clear_error();
+
+// Switches to `dev` for the duration of a call (RAII).
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) cudaSetDevice(dev);
+    else if (prev == dev) prev = -1;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
 
 inline int dtype_size(tq4_dtype t) {
   switch (t) {
@@ -105,6 +118,13 @@ struct tq4_weight {
   alignas(64) CUtensorMap smaps[3];
   alignas(64) CUtensorMap zmaps[3];
   bool wmaps_ok = false;
+  // TMA descriptors of the GEMV: 128 packed rows x 64 bytes, and 136 rows x gv_nbs blocks of the
+  // scales / zero points; gv_gps groups per pipeline stage
+  alignas(64) CUtensorMap gv_wmap;
+  alignas(64) CUtensorMap gv_smap;
+  alignas(64) CUtensorMap gv_zmap;
+  bool gv_maps_ok = false;
+  int gv_gps = 1, gv_nbs = 1;
 };
 
 namespace tq4 {
@@ -112,6 +132,11 @@ using Weight = tq4_weight;
 
 tq4_status prepare_weight(Weight& w, const void* b, const void* scales, const void* zp);
 tq4_status make_weight_maps(Weight& w);
+tq4_status make_gemv_maps(Weight& w);
+// A 2-D tiled TMA descriptor (cuTensorMapEncodeTiled through the runtime's driver entry point).
+tq4_status make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, uint64_t inner,
+                    uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                    CUtensorMapSwizzle sw);
 tq4_status run_dequant(const Weight& w, const int64_t* rows, int64_t n_out, void* out, cudaStream_t st);
 // Y rows have a stride of `ldy` elements (N for a dense Y; the shard width for a sharded call).
 tq4_status run_gemv(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,

@@ -21,9 +21,9 @@
 
 namespace tq4 {
 
-// 2 MiB of split-K partial sums and 64 KiB of counters: room for the Llama-3-8B-shaped
-// projections at M = 16 (the largest, K=4096 x N=14336, needs 1.75 MiB).
-constexpr int64_t kNoAllocScratchFloats = (int64_t)1 << 19;
+// 4 MiB of split-K partial sums and 64 KiB of counters: room for the Llama-3-8B-shaped
+// projections at M = 16 (the largest needs 3.5 MiB).
+constexpr int64_t kNoAllocScratchFloats = (int64_t)1 << 20;
 constexpr int64_t kNoAllocCounters = 16384;
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];

@@ -8,6 +8,8 @@
 
 namespace tq4 {
 
+__device__ int32_t g_device_status = 0;
+
 // One thread per output 32-bit word of the packed layout: gathers its 32/BITS elements from
 // the raw rows (element k of row n = bits [(k%per)*BITS, ...) of byte k/per, packed.ex:11-23).
 template <int BITS>
