@@ -41,6 +41,7 @@ constexpr int kConsumers = 256;
 constexpr int kGemvThreads = kConsumers + 32;
 constexpr int kMaxStages = 4;
 constexpr int kSmemBudget = 110 * 1024;  // two CTAs per SM
+constexpr int kSmemBudget3 = 0;          // three CTAs per SM (M = 1 kernel): measured slower, off
 
 enum GemvMode { kCols = 0, kSegMT1 = 1, kSegMT2 = 2 };
 
@@ -67,6 +68,9 @@ struct GemvArgs {
   int ctas_n;            // row tiles of 128
   int ksplit;
   int items;
+  int units;             // M = 1 stream-K: (row tile, stage) units, stages per row tile, max pieces
+  int spr;
+  int maxp;
   int64_t n_pad;
   float* ws;
   int* counters;
@@ -207,12 +211,13 @@ __device__ __forceinline__ void load_act4(const void* a, int64_t m, int64_t k, i
 // Stages A[0:M][k0 : k0+kr] into shared memory as v(k) = RN(A / E * c(k)) in the MMA type, with
 // the per-segment factors {E, E*O*SV + (no zero points ? z*E*SA : 0), E*SA} as float4 [seg][mp].
 // Rows >= M are left as they are: their outputs are never stored, and an MMA output element
-// depends only on its own activation row. Run by the 256 consumer threads.
-template <int BITS, tq4_dtype AT>
+// depends only on its own activation row. Run by the 256 consumer threads. `act` and `segf`
+// point at position k0 (element k0 - kk is at act[kk]). PRECISE must match the weight_pairs
+// variant the consumers use.
+template <int BITS, tq4_dtype AT, bool PRECISE = (AT == TQ4_F32)>
 __device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int kr, int mp,
                                                   uint16_t* act, float4* segf) {
   constexpr bool BF = (AT == TQ4_BF16);
-  constexpr bool PRECISE = (AT == TQ4_F32);
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const int vec_per_row = kr / 4;
@@ -300,6 +305,19 @@ __device__ __forceinline__ ItemRange item_range(const GemvArgs& p, int item, int
   r.k0 = r.g_begin * G;
   r.kr = (r.g_end - r.g_begin) * G;
   return r;
+}
+
+// sum_{i < n} src[i * stride] in index order, with the loads issued 16 at a time.
+__device__ __forceinline__ float sum_partials(const float* src, int64_t stride, int n) {
+  float total = 0.f;
+  for (int base = 0; base < n; base += 16) {
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = (base + i < n) ? __ldcg(src + (base + i) * stride) : 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) total += v[i];
+  }
+  return total;
 }
 
 // Y (or a split-K partial) of one output.
@@ -529,8 +547,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
           const int m = i / kRows;
           const int64_t n = (int64_t)r.rt * kRows + (i % kRows);
           if (n >= p.N) continue;
-          float v = 0.f;
-          for (int sp = 0; sp < p.ksplit; ++sp) v += __ldcg(&p.ws[((int64_t)sp * p.M + m) * p.n_pad + n]);
+          float v = sum_partials(p.ws + (int64_t)m * p.n_pad + n, (int64_t)p.M * p.n_pad, p.ksplit);
           if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
           store_from_f32(p.y, (int64_t)m * p.ldy + n, p.y_t, v);
         }
@@ -541,11 +558,285 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
   }
 }
 
+// ---- M = 1, 4-bit: compile-time segment layout, stream-K balance -----------------------------------
+// SPS = MMA steps (16 weights each) per segment = seg / 16. A stage holds GPS = min(4, SPS) groups
+// of 128 weights, i.e. NSEG = GPS * 8 / SPS <= 8 segments; MMA column c takes segment c of the
+// stage. Every step's column is a compile-time constant, so a thread's B fragment is the staged
+// activation times a 0/1 f16x2 mask (one FMA-pipe multiply) and the block of each segment is its
+// index (block_size <= 128, so blocks start on group boundaries). The (row tile, group) units are
+// split evenly over the CTAs (stream-K): each CTA stages the whole activation row once and walks
+// its units in stages of up to GPS groups that never cross a row tile; a row tile that spans
+// several CTAs is finished by the last of them, which sums the partials in CTA order.
+__device__ __forceinline__ int unit_owner(int u, int units, int grid) {
+  return (int)((((int64_t)u + 1) * grid - 1) / units);
+}
+__device__ __forceinline__ int unit_first(int b, int units, int grid) {
+  return (int)((int64_t)b * units / grid);
+}
+
+template <tq4_dtype AT, int SPS>
+__global__ void __launch_bounds__(kGemvThreads, 3)
+    gemv_m1_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_s,
+                   const __grid_constant__ CUtensorMap map_z, const GemvArgs p) {
+  constexpr bool BF = (AT == TQ4_BF16);
+  // A column accumulates one segment between corrections, so the 1024 offset of the plain magic
+  // numbers only costs precision on long segments: f32 activations take the precise weights from
+  // 64-wide segments up.
+  constexpr bool PRECISE = (AT == TQ4_F32) && SPS > 2;
+  constexpr int G = 128;
+  constexpr int GPS = SPS < 4 ? SPS : 4;
+  constexpr int SEG = 16 * SPS;
+  constexpr int NSEG = GPS * 8 / SPS;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int s_last;
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t sbase = (raw_addr + 1023) & ~1023u;
+  uint8_t* smem = smem_raw + (sbase - raw_addr);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t bars = sbase + p.bar_off;
+  const int S = p.stages;
+  auto full = [&](int s) { return bars + 8 * s; };
+  auto empty = [&](int s) { return bars + 8 * (kMaxStages + s); };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + p.bar_off + 8 * 2 * kMaxStages);
+  const int u0 = unit_first(blockIdx.x, p.units, gridDim.x);
+  const int u1 = unit_first(blockIdx.x + 1, p.units, gridDim.x);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 8);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == 8) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      const uint32_t sc_bytes = kScaleRows * p.nbs * p.st_bytes;
+      int gs = 0;
+      for (int u = u0; u < u1; ++gs) {
+        const int s = gs % S;
+        if (!mbar_wait(empty(s), ((gs / S) & 1) ^ 1, abort_flag, kDevTimeoutStageEmpty)) break;
+        const int rt = u / p.groups, c0 = u % p.groups;
+        const int ng = min(min(GPS, p.groups - c0), u1 - u);  // a chunk never crosses a row tile
+        u += ng;
+        const int row0 = rt * kRows;
+        const uint32_t st = sbase + s * p.stage_bytes;
+        mbar_expect_tx(full(s), ng * kRows * 64 + sc_bytes * (p.has_zp ? 2 : 1));
+        for (int gi = 0; gi < ng; ++gi) tma_load_2d(st + gi * kRows * 64, &map_w, (c0 + gi) * 64, row0, full(s));
+        const int b0 = (c0 * G) >> p.bs_log2;
+        tma_load_2d(st + p.sc_off, &map_s, row0, b0, full(s));
+        if (p.has_zp) tma_load_2d(st + p.zc_off, &map_z, row0, b0, full(s));
+      }
+      for (int g = max(0, gs - S); g < gs; ++g) mbar_drain(full(g % S), (g / S) & 1);
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int g = lane >> 2, t = lane & 3;
+  const int rl = warp * 16 + g;
+  uint16_t* act = reinterpret_cast<uint16_t*>(smem + p.act_off);
+  float4* segf = reinterpret_cast<float4*>(smem + p.seg_off);
+  {
+    // the activations of the groups this CTA's units touch (one or two runs, or the whole row)
+    const int c_a = u0 % p.groups, c_b = (u1 - 1) % p.groups;
+    if (u1 - u0 >= p.groups) {
+      stage_activations<4, AT, PRECISE>(p, 0, p.groups * G, 1, act, segf);
+    } else if (c_a <= c_b) {
+      stage_activations<4, AT, PRECISE>(p, c_a * G, (c_b - c_a + 1) * G, 1, act + c_a * G,
+                                        segf + (c_a * G) / SEG);
+    } else {
+      stage_activations<4, AT, PRECISE>(p, c_a * G, (p.groups - c_a) * G, 1, act + c_a * G,
+                                        segf + (c_a * G) / SEG);
+      stage_activations<4, AT, PRECISE>(p, 0, (c_b + 1) * G, 1, act, segf);
+    }
+  }
+  consumer_sync();
+
+  // 0/1 multipliers of this thread's B column for each stage column
+  const uint32_t one2 = BF ? 0x3F803F80u : 0x3C003C00u;
+  uint32_t mask[NSEG];
+#pragma unroll
+  for (int c = 0; c < NSEG; ++c) mask[c] = (g == c) ? one2 : 0u;
+
+  int gs = 0;
+  bool ok = true;
+  float acc0 = 0.f, acc8 = 0.f;
+  for (int u = u0; u < u1; ++gs) {
+    const int rt = u / p.groups, c0 = u % p.groups;
+    const int ng = min(min(GPS, p.groups - c0), u1 - u);
+    u += ng;
+    const int s = gs % S;
+    if (ok) ok = mbar_wait(full(s), (gs / S) & 1, abort_flag, kDevTimeoutTmaFull);
+    if (ok) {
+      const uint8_t* st = smem + s * p.stage_bytes;
+      const uint8_t* sc = st + p.sc_off;
+      const uint8_t* zc = st + p.zc_off;
+      const uint16_t* actk = act + c0 * G + 4 * t;
+      float blk2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // even / odd steps
+#pragma unroll
+      for (int gi = 0; gi < GPS; ++gi) {
+        if (gi < ng) {
+          const uint4 xa = *reinterpret_cast<const uint4*>(st + gi * kRows * 64 + rl * 64 + t * 16);
+          const uint4 xb = *reinterpret_cast<const uint4*>(st + gi * kRows * 64 + (rl + 8) * 64 + t * 16);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint32_t a0, a1, a2, a3;
+            weight_pairs<4, BF, PRECISE>(word_of(xa, j / 2), j, a0, a2);
+            weight_pairs<4, BF, PRECISE>(word_of(xb, j / 2), j, a1, a3);
+            const uint2 bv = *reinterpret_cast<const uint2*>(actk + gi * G + 16 * j);
+            const uint32_t m = mask[(gi * 8 + j) / SPS];
+            uint32_t b0, b1;
+            if (BF) {
+              asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(b0) : "r"(bv.x), "r"(m));
+              asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(b1) : "r"(bv.y), "r"(m));
+            } else {
+              asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(b0) : "r"(bv.x), "r"(m));
+              asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(b1) : "r"(bv.y), "r"(m));
+            }
+            mma16816<BF>(blk2[j & 1], a0, a1, a2, a3, b0, b1);  // two independent MMA chains
+          }
+        }
+      }
+      float blk[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) blk[i] = blk2[0][i] + blk2[1][i];
+      // columns 2t, 2t+1 = segments 2t, 2t+1 of the stage
+      const int nseg = ng * 8 / SPS;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int sg = 2 * t + h;
+        if (sg < nseg) {
+          const int lb = (sg * SEG) >> p.bs_log2;  // the stage starts on a block boundary
+          const float4 F = segf[(c0 * G) / SEG + sg];
+          const float s_g = scale_to_f32(sc, lb * kScaleRows + rl, p.st_bytes, p.st_bf16);
+          const float s_g8 = scale_to_f32(sc, lb * kScaleRows + rl + 8, p.st_bytes, p.st_bf16);
+          float z_g = 0.f, z_g8 = 0.f;
+          if (p.has_zp) {
+            z_g = scale_to_f32(zc, lb * kScaleRows + rl, p.st_bytes, p.st_bf16);
+            z_g8 = scale_to_f32(zc, lb * kScaleRows + rl + 8, p.st_bytes, p.st_bf16);
+          }
+          acc0 = fmaf(s_g, fmaf(-z_g, F.z, fmaf(F.x, blk[h], -F.y)), acc0);
+          acc8 = fmaf(s_g8, fmaf(-z_g8, F.z, fmaf(F.x, blk[2 + h], -F.y)), acc8);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty(s));
+
+    // end of this CTA's piece of row tile rt
+    if (c0 + ng == p.groups || u == u1) {
+      float y0 = acc0, y8 = acc8;
+      y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+      y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+      y8 += __shfl_xor_sync(0xffffffffu, y8, 1);
+      y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
+      acc0 = acc8 = 0.f;
+      const int64_t n_g = (int64_t)rt * kRows + rl;
+      const int b_first = unit_owner(rt * p.groups, p.units, gridDim.x);
+      const int b_last = unit_owner(rt * p.groups + p.groups - 1, p.units, gridDim.x);
+      if (b_first == b_last) {  // the whole row tile is this CTA's
+        if (t == 0) {
+          write_out(p, 0, n_g, 0, y0);
+          write_out(p, 0, n_g + 8, 0, y8);
+        }
+      } else {
+        const int piece = blockIdx.x - b_first;
+        float* part = p.ws + ((int64_t)rt * p.maxp + piece) * kRows;
+        if (t == 0) {
+          part[rl] = y0;
+          part[rl + 8] = y8;
+        }
+        __threadfence();
+        consumer_sync();
+        if (threadIdx.x == 0) {
+          const int prev = atomicAdd(&p.counters[rt], 1);
+          s_last = (prev == b_last - b_first);
+          if (prev > b_last - b_first) report(kDevTimeoutSplitK);
+        }
+        consumer_sync();
+        if (s_last) {
+          __threadfence();
+          if (threadIdx.x < kRows) {
+            const int64_t n = (int64_t)rt * kRows + threadIdx.x;
+            float v = sum_partials(p.ws + (int64_t)rt * p.maxp * kRows + threadIdx.x, kRows,
+                                   b_last - b_first + 1);
+            if (n < p.N) {
+              if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
+              store_from_f32(p.y, n, p.y_t, v);
+            }
+          }
+          if (threadIdx.x == 0) p.counters[rt] = 0;
+        }
+      }
+    }
+  }
+}
+
 // ---- host side --------------------------------------------------------------------------------
 struct GemvPlan {
   int mode, ksplit, groups_per_split, ctas_n, stages, stage_bytes, sc_off, zc_off, act_off,
       seg_off, bar_off, sk, smem, items;
+  // M = 1 stream-K (mode kM1)
+  int units, spr, maxp, grid, ctas_per_sm;
+  int64_t ws_floats;  // split-K / stream-K partials (0: none)
 };
+
+constexpr int kM1 = 3;
+
+// CTA that owns unit u when `units` units are split evenly over `grid` CTAs (host copy).
+static int owner_of(int64_t u, int64_t units, int64_t grid) { return (int)(((u + 1) * grid - 1) / units); }
+
+// The M = 1 stream-K plan, when the whole activation row fits the shared-memory budget.
+static bool plan_m1(const Weight& w, GemvPlan& pl) {
+  if (w.desc.bits != 4 || w.desc.block_size > 128) return false;
+  const int G = 128, seg = w.desc.block_size;
+  const int gps = w.gv_gps;
+  if (gps != std::min(4, seg / 16)) return false;  // the handle's boxes follow the same rule
+  const int st = dtype_size(w.desc.dequant_dtype);
+  const int sc_bytes = (kScaleRows * w.gv_nbs * st + 127) / 128 * 128;
+  pl.sc_off = gps * kRows * 64;
+  pl.zc_off = pl.sc_off + sc_bytes;
+  pl.stage_bytes = (pl.zc_off + (w.zps.ptr ? sc_bytes : 0) + 1023) / 1024 * 1024;
+  const int kr = (int)w.groups * G;
+  const int act_bytes = (kr * 2 + 15) / 16 * 16;
+  const int seg_bytes = (kr / seg) * 16;
+  const int fixed = act_bytes + seg_bytes + 8 * 2 * kMaxStages + 16;
+  // three CTAs per SM when three stages fit in a third of the shared memory, else two
+  int stages = std::min(kMaxStages, (kSmemBudget3 - fixed) / pl.stage_bytes);
+  pl.ctas_per_sm = 3;
+  if (stages < 3) {
+    stages = std::min(kMaxStages, (kSmemBudget - fixed) / pl.stage_bytes);
+    pl.ctas_per_sm = 2;
+  }
+  if (stages < 2) return false;
+  pl.mode = kM1;
+  pl.stages = stages;
+  pl.act_off = stages * pl.stage_bytes;
+  pl.seg_off = pl.act_off + act_bytes;
+  pl.bar_off = pl.seg_off + seg_bytes;
+  pl.smem = pl.bar_off + 8 * 2 * kMaxStages + 16;
+  pl.sk = kr + 16;
+  pl.ctas_n = (int)(w.n_pad / kRows);
+  pl.spr = (int)w.groups;
+  pl.units = pl.ctas_n * pl.spr;  // one unit = 128 rows x one 64-byte group
+  pl.grid = std::min(pl.units, pl.ctas_per_sm * w.num_sms);
+  pl.ksplit = 1;
+  pl.groups_per_split = (int)w.groups;
+  pl.items = pl.ctas_n;
+  pl.maxp = 1;
+  for (int rt = 0; rt < pl.ctas_n; ++rt) {
+    const int pieces = owner_of((int64_t)rt * pl.spr + pl.spr - 1, pl.units, pl.grid) -
+                       owner_of((int64_t)rt * pl.spr, pl.units, pl.grid) + 1;
+    pl.maxp = std::max(pl.maxp, pieces);
+  }
+  pl.ws_floats = pl.maxp > 1 ? (int64_t)pl.ctas_n * pl.maxp * kRows : 0;
+  return true;
+}
 
 static int seg_of(const Weight& w) {
   const int G = 512 / w.desc.bits;
@@ -563,6 +854,8 @@ void gemv_stage_shape(const Weight& w, int* gps, int* nbs) {
 
 static GemvPlan plan_gemv(const Weight& w, int64_t m) {
   GemvPlan pl{};
+  if (m == 1 && plan_m1(w, pl)) return pl;
+  pl = GemvPlan{};
   const int G = 512 / w.desc.bits;
   const int seg = seg_of(w);
   const int spg = G / seg;
@@ -603,7 +896,32 @@ static GemvPlan plan_gemv(const Weight& w, int64_t m) {
   }
   pl.ksplit = (int)((groups + pl.groups_per_split - 1) / pl.groups_per_split);
   pl.items = pl.ctas_n * pl.ksplit;
+  pl.grid = std::min(pl.items, 2 * w.num_sms);
+  pl.ws_floats = pl.ksplit > 1 ? (int64_t)pl.ksplit * m * w.n_pad : 0;
   return pl;
+}
+
+template <tq4_dtype AT, int SPS>
+static cudaError_t launch_m1_t(const Weight& w, const GemvArgs& args, int grid, int smem, cudaStream_t st) {
+  auto kern = gemv_m1_kernel<AT, SPS>;
+  static bool attr_set = false;  // once per instantiation
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 1024);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  kern<<<grid, kGemvThreads, smem + 1024, st>>>(w.gv_wmap, w.gv_smap, w.gv_zmap, args);
+  return cudaGetLastError();
+}
+
+template <tq4_dtype AT>
+static cudaError_t launch_m1_sps(const Weight& w, const GemvArgs& args, int grid, int smem, cudaStream_t st) {
+  switch (std::min<int>(w.desc.block_size, 128) / 16) {
+    case 1: return launch_m1_t<AT, 1>(w, args, grid, smem, st);
+    case 2: return launch_m1_t<AT, 2>(w, args, grid, smem, st);
+    case 4: return launch_m1_t<AT, 4>(w, args, grid, smem, st);
+    default: return launch_m1_t<AT, 8>(w, args, grid, smem, st);
+  }
 }
 
 template <int BITS, tq4_dtype AT, int MODE>
@@ -741,19 +1059,27 @@ tq4_status run_gemv_with(const Weight& w, const void* a, int64_t m, tq4_dtype a_
   args.ctas_n = pl.ctas_n;
   args.ksplit = pl.ksplit;
   args.items = pl.items;
+  args.units = pl.units;
+  args.spr = pl.spr;
+  args.maxp = pl.maxp;
   args.n_pad = w.n_pad;
-  if (pl.ksplit > 1) {
-    const int64_t need = (int64_t)pl.ksplit * m * w.n_pad;
-    if (ws == nullptr || need > ws_capacity_floats || pl.ctas_n > ctr_capacity) {
+  if (pl.ws_floats > 0) {
+    if (ws == nullptr || pl.ws_floats > ws_capacity_floats || pl.ctas_n > ctr_capacity) {
       set_error("split-K workspace too small: need %lld floats and %d counters",
-                (long long)need, pl.ctas_n);
+                (long long)pl.ws_floats, pl.ctas_n);
       return TQ4_ERR_INVALID_ARGUMENT;
     }
     args.ws = ws;
     args.counters = counters;
   }
   cudaError_t e;
-  if (w.desc.bits == 4) e = launch_gemv_bits<4>(w, args, a_t, pl.mode, pl.smem, st);
+  if (pl.mode == kM1) {
+    switch (a_t) {
+      case TQ4_F16: e = launch_m1_sps<TQ4_F16>(w, args, pl.grid, pl.smem, st); break;
+      case TQ4_BF16: e = launch_m1_sps<TQ4_BF16>(w, args, pl.grid, pl.smem, st); break;
+      default: e = launch_m1_sps<TQ4_F32>(w, args, pl.grid, pl.smem, st); break;
+    }
+  } else if (w.desc.bits == 4) e = launch_gemv_bits<4>(w, args, a_t, pl.mode, pl.smem, st);
   else if (w.desc.bits == 2) e = launch_gemv_bits<2>(w, args, a_t, pl.mode, pl.smem, st);
   else e = launch_gemv_bits<8>(w, args, a_t, pl.mode, pl.smem, st);
   if (e != cudaSuccess) {
@@ -763,10 +1089,7 @@ tq4_status run_gemv_with(const Weight& w, const void* a, int64_t m, tq4_dtype a_
   return TQ4_OK;
 }
 
-int64_t gemv_workspace_floats(const Weight& w, int64_t m) {
-  const GemvPlan pl = plan_gemv(w, m);
-  return pl.ksplit > 1 ? (int64_t)pl.ksplit * m * w.n_pad : 0;
-}
+int64_t gemv_workspace_floats(const Weight& w, int64_t m) { return plan_gemv(w, m).ws_floats; }
 
 int64_t gemv_counter_count(const Weight& w, int64_t m) { return plan_gemv(w, m).ctas_n; }
 

@@ -28,14 +28,29 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As mbar_try, but the thread may sleep in hardware up to `ns` nanoseconds for the phase instead
+// of spinning (waiting warps then take no issue slots).
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // About one second at the B200's clocks; a healthy stage completes in microseconds.
 constexpr long long kWaitCycles = 2000000000LL;
 
 // Waits for the phase `parity` of `bar`, unless the CTA aborted; false on timeout or abort.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int32_t code) {
+  if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try(bar, parity)) {
+  while (!mbar_try_sleep(bar, parity, 1000000u)) {
     if (*abort_flag) return false;
     if (clock64() - t0 > kWaitCycles) {
       report(code);
