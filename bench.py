@@ -164,6 +164,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
 
+    if args.workload == "c4":
+        return decoder_bench(args, rank, world, local_rank)
     from transmuter_b200 import workloads
     if args.workload not in workloads.CONFIGS:
         raise SystemExit(f"unknown workload {args.workload}; one of {sorted(workloads.CONFIGS)}")
@@ -367,6 +369,176 @@ def main():
         w.close()
     if comm is not None:
         comm.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# ---- C4: the q4 decoder ----------------------------------------------------------------------
+DECODE_PROMPT = 128
+
+
+def decoder_bytes_per_token(cfg, pos):
+    """Algorithmic HBM bytes of one decode step at position `pos`: every MatMulNBits weight once
+    (packed nibbles + f32 scales; the embedding row gather is one lm_head row) plus the KV cache
+    read up to pos and written at pos (f32)."""
+    qkv_n = (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim
+    per_layer = cfg.hidden * qkv_n + cfg.heads * cfg.head_dim * cfg.hidden + cfg.hidden * 2 * cfg.inter \
+        + cfg.inter * cfg.hidden
+    weights = cfg.layers * per_layer + cfg.vocab * cfg.hidden
+    packed = weights // 2 + weights // cfg.block_size * 4
+    kv = cfg.layers * 2 * cfg.kv_heads * cfg.head_dim * 4 * (pos + 1)
+    return packed + kv
+
+
+def decoder_cpu(cfg, seed, steps, budget_s):
+    """Moved-weight CPU path (oracle decoder in float32: dense weights, BLAS matrix-vector products)
+    for a bounded number of decode steps at positions 127.. with the cache rows before them
+    filled with seeded values (the attention work of a 128-token prefill, without running it)."""
+    from oracle.decoder import OracleDecoder
+    from transmuter_b200.decoder import random_weights, rope_tables
+    weights = random_weights(cfg, seed)
+    cos, sin = rope_tables(cfg)
+    ref = OracleDecoder(cfg, weights, cos, sin, dtype=np.float32)
+    del weights
+    r = np.random.default_rng(seed)
+    fill = (cfg.layers, cfg.kv_heads, DECODE_PROMPT - 1, cfg.head_dim)
+    ref.k_cache[:, :, :DECODE_PROMPT - 1] = r.standard_normal(fill, dtype=np.float32)
+    ref.v_cache[:, :, :DECODE_PROMPT - 1] = r.standard_normal(fill, dtype=np.float32)
+    tok = int(r.integers(0, cfg.vocab))
+    ref.step(tok, DECODE_PROMPT - 1)  # warm-up (overwrites its own position)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    for i in range(steps):
+        t0 = time.perf_counter()
+        tok = int(np.argmax(ref.step(tok, DECODE_PROMPT - 1 + i)))
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end:
+            break
+    sample = (f"oracle decoder in f32 with dense dequantized weights (numpy/BLAS), {len(times)} greedy decode "
+              f"steps from position {DECODE_PROMPT - 1} (cache rows before it seeded, not prefilled)")
+    return len(times) / sum(times), len(times), sample
+
+
+def decoder_bench(args, rank, world, local_rank):
+    """Decode tok/s of the Qwen3-0.6B-shaped q4 decoder: a 128-token prompt (forced steps, timed
+    separately as prefill), then K greedy decode steps, each one CUDA graph replay of a whole
+    token (28 layers, lm_head, argmax) with the position and token in device memory. N > 1 runs
+    independent replicas (the decoder does not shard)."""
+    import zlib
+    from transmuter_b200.decoder import QWEN3_0_6B, Q4Decoder
+    cfg = QWEN3_0_6B
+    seed = zlib.crc32(b"c4")
+    config = {"workload": "c4 Qwen3-0.6B-shaped q4 decoder, batch 1, f32 KV cache",
+              "layers": cfg.layers, "hidden": cfg.hidden, "inter": cfg.inter, "heads": cfg.heads,
+              "kv_heads": cfg.kv_heads, "head_dim": cfg.head_dim, "vocab": cfg.vocab, "block_size": cfg.block_size,
+              "scales": "f32", "prompt_tokens": DECODE_PROMPT}
+    steps = args.steps or 128
+    if steps > cfg.max_len - DECODE_PROMPT:
+        raise SystemExit(f"--steps at most {cfg.max_len - DECODE_PROMPT} for c4 (cache of {cfg.max_len})")
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        value, n_timed, sample = decoder_cpu(cfg, seed, steps, budget_s=120.0)
+        config["parallelism"] = "host cores"
+        line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+                "steps": steps, "warmup": args.warmup, "ms_per_step": 1e3 / value, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (random-init weights of the architecture, seeded prompt)", "config": config,
+                "cpu_baseline": {"value": value, "unit": "tok/s", "cores": blas_threads(), "kind": "port",
+                                 "sample": sample + f" ({n_timed} of {steps} steps timed)"},
+                "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    config["parallelism"] = "single GPU" if world == 1 else f"{world} independent replicas"
+    dec = Q4Decoder(cfg, seed=seed, device=dev)
+    prompt = np.random.default_rng(seed + rank).integers(0, cfg.vocab, DECODE_PROMPT)
+    dec.reset(prompt)
+    dec.capture()
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(ms):
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        return ms
+
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    for _ in range(max(3, args.warmup)):  # warm-up: whole sequences
+        dec.reset(prompt)
+        dec.run(DECODE_PROMPT - 1 + steps)
+    torch.cuda.synchronize()
+    dec.reset(prompt)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    dec.run(DECODE_PROMPT - 1)  # prefill: forced prompt tokens
+    e1.record(stream)
+    dec.run(steps)              # timed decode steps
+    e2.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms_prefill = max_over_ranks(e0.elapsed_time(e1))
+    ms = max_over_ranks(e1.elapsed_time(e2))
+    tokens = dec.log[DECODE_PROMPT:DECODE_PROMPT + steps].cpu().numpy()
+    value = steps / (ms / 1e3) * world
+
+    # e2e through the public API: generate() copies the prompt in and the tokens out
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    t0.record(stream)
+    out = dec.generate(prompt, steps)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = max_over_ranks(t0.elapsed_time(t1))
+    assert np.array_equal(out, tokens), "generate() and the timed decode disagree"
+
+    pk, pk_kind = peaks()
+    step_bytes = np.mean([decoder_bytes_per_token(cfg, DECODE_PROMPT - 1 + i) for i in range(steps)])
+    achieved = step_bytes / (ms / 1e3 / steps) / 1e9
+    launches = cfg.layers * 9 + 4
+    if rank == 0:
+        config["l2"] = "inputs larger than L2 (about 372 MB of weights read per token, L2 126 MB)"
+        config["prefill"] = {"tok_per_s": (DECODE_PROMPT - 1) / (ms_prefill / 1e3) * world,
+                             "note": "prompt run as forced decode steps (M=1), one graph replay per token"}
+        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
+                "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (random-init weights of the architecture, seeded prompt)", "config": config,
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                             "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                             "scope": "whole decode step (all launches of one token); bytes = weights + KV",
+                             "peak_source": f"{pk_kind} (copy)"},
+                "e2e": {"value": steps / (ms_e2e / 1e3) * world, "unit": "tok/s",
+                        "h2d_bytes_per_step": int(DECODE_PROMPT * 8 // steps),
+                        "d2h_bytes_per_step": 8,
+                        "note": "generate(): prompt in, prefill, decode, tokens out; tok/s counts decode tokens"},
+                "gpu_launches": steps * launches, "clocks": clocks}
+        if world == 1 and not args.no_cpu_baseline:
+            del dec
+            torch.cuda.empty_cache()
+            v, n_timed, sample = decoder_cpu(cfg, seed, steps, budget_s=20.0)
+            line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": blas_threads(), "kind": "port",
+                                    "sample": sample}
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 

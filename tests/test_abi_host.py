@@ -16,8 +16,12 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def header_symbols():
-    text = open(os.path.join(ROOT, "include", "tq4.h")).read()
-    return sorted(set(re.findall(r"\b(tq4_[a-z_]+)\s*\(", text)))
+    names = set()
+    inc = os.path.join(ROOT, "include")
+    for header in sorted(os.listdir(inc)):
+        if header.endswith(".h"):
+            names |= set(re.findall(r"\b(tq4_[a-z_]+)\s*\(", open(os.path.join(inc, header)).read()))
+    return sorted(names)
 
 
 def test_header_and_binding_agree():
