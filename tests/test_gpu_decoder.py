@@ -82,6 +82,41 @@ def test_position_past_cache_sets_device_status(tiny):
     assert torch.equal(dec.k_cache, k_before)
 
 
+@pytest.mark.parametrize("pos", [0, 1, 31, 32, 33, 100, 255, 256])
+@pytest.mark.parametrize("heads,kv_heads,head_dim", [(16, 8, 128), (8, 2, 64), (4, 4, 256)])
+def test_attention_decode_against_torch(pos, heads, kv_heads, head_dim):
+    """tq4_attention_decode over positions that end inside, on and past 32-position chunks (the
+    chunk-combine path) against an fp64 softmax over the same cache; the new row lands in the cache."""
+    lib = _lib.load()
+    max_len = 257
+    g = torch.Generator().manual_seed(pos * 7 + heads)
+    dev = torch.device("cuda:0")
+    q = torch.randn(heads, head_dim, generator=g)
+    k_new = torch.randn(kv_heads, head_dim, generator=g)
+    v_new = torch.randn(kv_heads, head_dim, generator=g)
+    k_cache = torch.randn(kv_heads, max_len, head_dim, generator=g)
+    v_cache = torch.randn(kv_heads, max_len, head_dim, generator=g)
+    k_ref, v_ref = k_cache.double().clone(), v_cache.double().clone()
+    k_ref[:, pos], v_ref[:, pos] = k_new.double(), v_new.double()
+    grp = heads // kv_heads
+    ref = torch.empty(heads, head_dim, dtype=torch.float64)
+    for h in range(heads):
+        s = k_ref[h // grp, :pos + 1] @ q[h].double() / head_dim ** 0.5
+        ref[h] = torch.softmax(s, 0) @ v_ref[h // grp, :pos + 1]
+    d = [t.to(dev).contiguous() for t in (q, k_new, v_new, k_cache, v_cache)]
+    p = torch.tensor([pos], dtype=torch.int32, device=dev)
+    out = torch.empty(heads, head_dim, device=dev)
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+    fn = lib.tq4_attention_decode
+    fn.argtypes = [ctypes.c_void_p] * 7 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    for _ in range(2):  # twice: the arrival counters must be back at zero after a call
+        _lib.check(fn(*[vp(t) for t in d], vp(p), vp(out), heads, kv_heads, head_dim, max_len,
+                      ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+        torch.cuda.synchronize()
+        assert o.rel_l2(out.double().cpu().numpy(), ref.numpy()) < 1e-5
+    assert torch.equal(d[3][:, pos].cpu(), k_new) and torch.equal(d[4][:, pos].cpu(), v_new)
+
+
 def torch_reference_logits(dec, cfg, prompt, steps):
     """fp32 restatement on the GPU over the dequantized weights (bit-exact to the handles')."""
     w = {name: pw.dequantize().float() for name, pw in dec.weights.items()}

@@ -2,6 +2,7 @@
 // the kernels. Errors become status codes plus a thread-local message, in the spirit of the
 // reference's ArgumentError raises (quantized.ex:33-34) that run_nodes wraps with the op name
 // and shapes (lib/transmuter.ex:661-679).
+#include <cstdlib>
 #include <cstdarg>
 
 #include "internal.cuh"
@@ -20,6 +21,14 @@ void set_error(const char* fmt, ...) {
 }
 
 void clear_error() { t_last_error.clear(); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("TQ4_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 void free_workspaces(Weight& w);
 

@@ -30,6 +30,15 @@ extern __device__ int32_t g_device_status;
 
 __device__ __forceinline__ void report(int32_t code) { atomicCAS(&g_device_status, 0, code); }
 
+// Programmatic dependent launch. A kernel launched with launch_pdl may start while the kernel
+// before it on the stream is still running: everything it does before pdl_wait() must touch only
+// memory no earlier kernel writes (weights, its own shared memory). pdl_wait() returns once the
+// previous grid has completed and its writes are visible; every CTA of such a kernel passes it
+// (or exits without touching global memory) so that completion stays transitive along the stream.
+// pdl_trigger() lets the next kernel be scheduled; without a PDL launch both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- float types ------------------------------------------------------------------------------
 template <tq4_dtype T> struct FloatOf;
 template <> struct FloatOf<TQ4_F32> { using type = float; };

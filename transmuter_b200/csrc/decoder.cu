@@ -4,6 +4,10 @@
 #include "../../include/tq4_decoder.h"
 #include "internal.cuh"
 
+#include <map>
+#include <memory>
+#include <mutex>
+
 namespace tq4 {
 
 // Deterministic block sum (fixed shuffle tree, then warp order).
@@ -35,6 +39,8 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta,
                                                           const float* __restrict__ w, float* __restrict__ y,
                                                           int64_t n, float eps) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[8];
   float* xr = x + blockIdx.x * n;
   float* yr = y + blockIdx.x * n;
@@ -59,6 +65,8 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(float* __restrict__ q
                                                            const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                                            const int32_t* __restrict__ pos, int heads, int head_dim,
                                                            int max_pos, float eps) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[4];
   __shared__ float buf[512];
   const int h = blockIdx.x;
@@ -87,69 +95,183 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(float* __restrict__ q
   }
 }
 
-// One query row per head; the CTA of the first query head of each KV group also writes the new
-// key / value into the cache (the other heads read the new ones from k_new / v_new).
-__global__ void __launch_bounds__(128) attention_decode_kernel(const float* __restrict__ q, const float* __restrict__ k_new,
-                                                               const float* __restrict__ v_new, float* __restrict__ k_cache,
-                                                               float* __restrict__ v_cache, const int32_t* __restrict__ pos,
-                                                               float* __restrict__ out, int heads, int kv_heads,
-                                                               int head_dim, int max_len, float scale) {
-  extern __shared__ float sm[];  // q [head_dim], scores [max_len]
-  __shared__ float red[4];
-  float* qs = sm;
-  float* sc = sm + head_dim;
-  const int h = blockIdx.x;
-  const int group = heads / kv_heads;
-  const int kvh = h / group;
+// One-token GroupQueryAttention, split over positions (flash-decoding). CTA (chunk c, KV head kvh)
+// takes positions [32c, 32c + 32) for all G = heads / kv_heads query heads of that KV head, so each
+// K/V row is read once per token. A chunk keeps its max m, sum l and unnormalised output
+// o = sum_p exp(s_p - m) v_p; the last chunk CTA of a KV head (atomic arrival count) combines them
+// in chunk order, so the result does not depend on scheduling. The CTA whose chunk holds the new
+// position writes k_new / v_new into the cache; the other chunks never read that row.
+constexpr int kAttnChunk = 32;
+constexpr int kAttnThreads = 128;
+constexpr int kAttnMaxGroup = 8;
+constexpr int kAttnMaxDim = 256;
+
+__global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
+    const float* __restrict__ q, const float* __restrict__ k_new, const float* __restrict__ v_new,
+    float* __restrict__ k_cache, float* __restrict__ v_cache, const int32_t* __restrict__ pos,
+    float* __restrict__ out, int heads, int kv_heads, int head_dim, int max_len, float scale,
+    float* __restrict__ part, int* __restrict__ counters, int chunks_max) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float qs[kAttnMaxGroup * kAttnMaxDim];
+  __shared__ float sc[kAttnMaxGroup][kAttnChunk];
+  __shared__ float ml[kAttnMaxGroup][2];
+  __shared__ int s_last;
+  const int G = heads / kv_heads;
+  const int c = blockIdx.x, kvh = blockIdx.y;
   const int L = *pos + 1;
   if (L < 1 || L > max_len) {  // position past the cache
-    if (threadIdx.x == 0) report(kDevBadArgument);
+    if (threadIdx.x == 0 && c == 0) report(kDevBadArgument);
     return;
   }
-  const float* kn = k_new + (int64_t)kvh * head_dim;
-  const float* vn = v_new + (int64_t)kvh * head_dim;
-  float* kc = k_cache + (int64_t)kvh * max_len * head_dim;
-  float* vc = v_cache + (int64_t)kvh * max_len * head_dim;
-  for (int d = threadIdx.x; d < head_dim; d += 128) {
-    qs[d] = q[(int64_t)h * head_dim + d];
-    if (h % group == 0) {
-      kc[(int64_t)(L - 1) * head_dim + d] = kn[d];
-      vc[(int64_t)(L - 1) * head_dim + d] = vn[d];
+  const int nch = (L + kAttnChunk - 1) / kAttnChunk;
+  const int p0 = c * kAttnChunk;
+  if (p0 >= L) return;
+  const int np = min(kAttnChunk, L - p0);
+  const int64_t D = head_dim;
+  const float* kn = k_new + kvh * D;
+  const float* vn = v_new + kvh * D;
+  float* kc = k_cache + (int64_t)kvh * max_len * D;
+  float* vc = v_cache + (int64_t)kvh * max_len * D;
+  const bool has_new = (p0 + np == L);  // this chunk holds position L - 1
+  for (int i = threadIdx.x; i < G * head_dim; i += kAttnThreads) qs[i] = q[(int64_t)kvh * G * D + i];
+  if (has_new)
+    for (int d = threadIdx.x; d < head_dim; d += kAttnThreads) {
+      kc[(int64_t)(L - 1) * D + d] = kn[d];
+      vc[(int64_t)(L - 1) * D + d] = vn[d];
     }
-  }
   __syncthreads();
+
+  // scores: warp w takes positions w, w + 4, ...; lanes split head_dim
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int p = warp; p < L; p += 4) {
-    const float* kp = (p == L - 1) ? kn : kc + (int64_t)p * head_dim;
-    float dot = 0.f;
-    for (int d = lane; d < head_dim; d += 32) dot = fmaf(qs[d], kp[d], dot);
-    for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-    if (lane == 0) sc[p] = dot * scale;
+  for (int i = warp; i < np; i += kAttnThreads / 32) {
+    const int p = p0 + i;
+    const float* kp = (p == L - 1) ? kn : kc + (int64_t)p * D;
+    float dot[kAttnMaxGroup];
+#pragma unroll
+    for (int g = 0; g < kAttnMaxGroup; ++g) dot[g] = 0.f;
+    for (int d = lane; d < head_dim; d += 32) {
+      const float kv = kp[d];
+#pragma unroll
+      for (int g = 0; g < kAttnMaxGroup; ++g)
+        if (g < G) dot[g] = fmaf(qs[g * head_dim + d], kv, dot[g]);
+    }
+#pragma unroll
+    for (int g = 0; g < kAttnMaxGroup; ++g) {
+      if (g >= G) break;
+      float v = dot[g];
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == 0) sc[g][i] = v * scale;
+    }
   }
   __syncthreads();
-  float mx = -INFINITY;
-  for (int p = threadIdx.x; p < L; p += 128) mx = fmaxf(mx, sc[p]);
-  mx = block_max<128>(mx, red);
-  float sum = 0.f;
-  for (int p = threadIdx.x; p < L; p += 128) {
-    const float e = expf(sc[p] - mx);
-    sc[p] = e;
-    sum += e;
-  }
-  sum = block_sum<128>(sum, red);
-  const float inv = 1.f / sum;
-  for (int d = threadIdx.x; d < head_dim; d += 128) {
-    float o = 0.f;
-    for (int p = 0; p < L; ++p) {
-      const float vv = (p == L - 1) ? vn[d] : vc[(int64_t)p * head_dim + d];
-      o = fmaf(sc[p], vv, o);
+  // chunk softmax statistics: warp w takes heads w, w + 4, ...
+  for (int g = warp; g < G; g += kAttnThreads / 32) {
+    const float v = lane < np ? sc[g][lane] : -INFINITY;
+    float m = v;
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    const float e = lane < np ? expf(v - m) : 0.f;
+    float l = e;
+    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+    if (lane < np) sc[g][lane] = e;
+    if (lane == 0) {
+      ml[g][0] = m;
+      ml[g][1] = l;
     }
-    out[(int64_t)h * head_dim + d] = o * inv;
   }
+  __syncthreads();
+  // o[g][d] = sum_p e[g][p] v[p][d]
+  const int64_t stride_c = (int64_t)G * (D + 2);
+  float* my = part + ((int64_t)kvh * chunks_max + c) * stride_c;
+  for (int d = threadIdx.x; d < head_dim; d += kAttnThreads) {
+    float o[kAttnMaxGroup];
+#pragma unroll
+    for (int g = 0; g < kAttnMaxGroup; ++g) o[g] = 0.f;
+    for (int i = 0; i < np; ++i) {
+      const int p = p0 + i;
+      const float vv = (p == L - 1) ? vn[d] : vc[(int64_t)p * D + d];
+#pragma unroll
+      for (int g = 0; g < kAttnMaxGroup; ++g)
+        if (g < G) o[g] = fmaf(sc[g][i], vv, o[g]);
+    }
+#pragma unroll
+    for (int g = 0; g < kAttnMaxGroup; ++g) {
+      if (g >= G) break;
+      if (nch == 1)
+        out[((int64_t)kvh * G + g) * D + d] = o[g] / ml[g][1];
+      else
+        my[g * (D + 2) + d] = o[g];
+    }
+  }
+  if (nch == 1) return;
+  if (threadIdx.x < G) {
+    my[threadIdx.x * (D + 2) + D] = ml[threadIdx.x][0];
+    my[threadIdx.x * (D + 2) + D + 1] = ml[threadIdx.x][1];
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(&counters[kvh], 1);
+    s_last = (prev == nch - 1);
+    if (prev >= nch) report(kDevTimeoutSplitK);  // a counter left non-zero earlier
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const float* base = part + (int64_t)kvh * chunks_max * stride_c;
+  for (int i = threadIdx.x; i < G * head_dim; i += kAttnThreads) {
+    const int g = i / head_dim, d = i % head_dim;
+    float M = -INFINITY;
+    for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, base[cc * stride_c + g * (D + 2) + D]);
+    float num = 0.f, den = 0.f;
+    for (int cc = 0; cc < nch; ++cc) {
+      const float* pc = base + cc * stride_c + g * (D + 2);
+      const float w = expf(pc[D] - M);
+      num = fmaf(w, pc[d], num);
+      den = fmaf(w, pc[D + 1], den);
+    }
+    out[((int64_t)kvh * G + g) * D + d] = num / den;
+  }
+  if (threadIdx.x == 0) counters[kvh] = 0;
+}
+
+// Per-(device, stream) scratch of the attention partials and arrival counters.
+struct AttnScratch {
+  DeviceBuffer part, counters;
+};
+static std::mutex g_attn_mu;
+static std::map<std::pair<int, cudaStream_t>, std::unique_ptr<AttnScratch>> g_attn_scratch;
+
+static tq4_status attn_scratch(cudaStream_t st, int64_t part_bytes, int64_t counters, float** part, int** ctr) {
+  int dev = 0;
+  TQ4_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_attn_mu);
+  auto& slot = g_attn_scratch[{dev, st}];
+  if (!slot) slot.reset(new AttnScratch());
+  if (slot->part.bytes < part_bytes || slot->counters.bytes < counters * 4) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    TQ4_CUDA(cudaStreamIsCapturing(st, &cs));
+    if (cs != cudaStreamCaptureStatusNone) {
+      set_error("tq4_attention_decode: first call on a stream (or a larger cache) during stream capture; "
+                "call it once before capturing");
+      return TQ4_ERR_INVALID_ARGUMENT;
+    }
+    TQ4_CUDA(cudaStreamSynchronize(st));
+    if (slot->part.bytes < part_bytes) TQ4_TRY(slot->part.alloc(part_bytes));
+    if (slot->counters.bytes < counters * 4) {
+      TQ4_TRY(slot->counters.alloc(counters * 4));
+      TQ4_CUDA(cudaMemsetAsync(slot->counters.ptr, 0, counters * 4, st));
+    }
+  }
+  *part = static_cast<float*>(slot->part.ptr);
+  *ctr = static_cast<int*>(slot->counters.ptr);
+  return TQ4_OK;
 }
 
 __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ out,
                                 int64_t n) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float x = g[i];
     out[i] = x / (1.f + expf(-x)) * u[i];
@@ -161,6 +283,8 @@ __global__ void __launch_bounds__(1024) argmax_advance_kernel(const float* __res
                                                               const int64_t* __restrict__ forced, int forced_len,
                                                               int32_t* __restrict__ pos, int64_t* __restrict__ token,
                                                               int64_t* __restrict__ log, int log_len) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float bv[32];
   __shared__ int64_t bi[32];
   float best = -INFINITY;
@@ -215,8 +339,8 @@ tq4_status tq4_add_rmsnorm(float* x, const float* delta, const float* w, float* 
     return TQ4_ERR_INVALID_ARGUMENT;
   }
   if (rows == 0) return TQ4_OK;
-  add_rmsnorm_kernel<<<(unsigned)rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, delta, w, y, n, eps);
-  TQ4_CUDA(cudaGetLastError());
+  TQ4_CUDA(launch_pdl(add_rmsnorm_kernel, dim3((unsigned)rows), dim3(256), 0, static_cast<cudaStream_t>(stream), x,
+                      delta, w, y, n, eps));
   return TQ4_OK;
 }
 
@@ -229,9 +353,8 @@ tq4_status tq4_qk_norm_rope(float* q, float* k, const float* q_w, const float* k
     set_error("tq4_qk_norm_rope: bad arguments (head_dim must be even and <= 512)");
     return TQ4_ERR_INVALID_ARGUMENT;
   }
-  qk_norm_rope_kernel<<<heads + kv_heads, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      q, k, q_w, k_w, cos_table, sin_table, pos, heads, head_dim, max_pos, eps);
-  TQ4_CUDA(cudaGetLastError());
+  TQ4_CUDA(launch_pdl(qk_norm_rope_kernel, dim3(heads + kv_heads), dim3(128), 0, static_cast<cudaStream_t>(stream),
+                      q, k, q_w, k_w, cos_table, sin_table, pos, heads, head_dim, max_pos, eps));
   return TQ4_OK;
 }
 
@@ -240,16 +363,21 @@ tq4_status tq4_attention_decode(const float* q, const float* k_new, const float*
                                 int heads, int kv_heads, int head_dim, int max_len, void* stream) {
   clear_error();
   if (!q || !k_new || !v_new || !k_cache || !v_cache || !pos || !out || heads <= 0 || kv_heads <= 0 ||
-      heads % kv_heads || head_dim <= 0 || max_len <= 0 || (size_t)(head_dim + max_len) * 4 > 200 * 1024) {
-    set_error("tq4_attention_decode: bad arguments");
+      heads % kv_heads || heads / kv_heads > kAttnMaxGroup || head_dim <= 0 || head_dim > kAttnMaxDim ||
+      max_len <= 0 || kv_heads > 65535) {
+    set_error("tq4_attention_decode: bad arguments (heads a multiple of kv_heads, at most %d query heads per "
+              "KV head, head_dim <= %d)", kAttnMaxGroup, kAttnMaxDim);
     return TQ4_ERR_INVALID_ARGUMENT;
   }
-  const size_t smem = (size_t)(head_dim + max_len) * sizeof(float);
-  if (smem > 48 * 1024) TQ4_CUDA(cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  attention_decode_kernel<<<heads, 128, smem, static_cast<cudaStream_t>(stream)>>>(
-      q, k_new, v_new, k_cache, v_cache, pos, out, heads, kv_heads, head_dim, max_len,
-      1.f / sqrtf((float)head_dim));
-  TQ4_CUDA(cudaGetLastError());
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int G = heads / kv_heads;
+  const int chunks = (max_len + kAttnChunk - 1) / kAttnChunk;
+  float* part = nullptr;
+  int* ctr = nullptr;
+  TQ4_TRY(attn_scratch(st, (int64_t)kv_heads * chunks * G * (head_dim + 2) * 4, kv_heads, &part, &ctr));
+  TQ4_CUDA(launch_pdl(attention_decode_kernel, dim3(chunks, kv_heads), dim3(kAttnThreads), 0, st, q, k_new, v_new,
+                      k_cache, v_cache, pos, out, heads, kv_heads, head_dim, max_len, 1.f / sqrtf((float)head_dim),
+                      part, ctr, chunks));
   return TQ4_OK;
 }
 
@@ -261,8 +389,7 @@ tq4_status tq4_silu_mul(const float* gate, const float* up, float* out, int64_t 
   }
   if (n == 0) return TQ4_OK;
   const int grid = (int)std::min<int64_t>((n + 255) / 256, 1024);
-  silu_mul_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(gate, up, out, n);
-  TQ4_CUDA(cudaGetLastError());
+  TQ4_CUDA(launch_pdl(silu_mul_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), gate, up, out, n));
   return TQ4_OK;
 }
 
@@ -274,9 +401,8 @@ tq4_status tq4_argmax_advance(const float* logits, int64_t n, const int64_t* for
     set_error("tq4_argmax_advance: bad arguments");
     return TQ4_ERR_INVALID_ARGUMENT;
   }
-  argmax_advance_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(logits, n, forced, forced_len,
-                                                                          pos, token, log, log_len);
-  TQ4_CUDA(cudaGetLastError());
+  TQ4_CUDA(launch_pdl(argmax_advance_kernel, dim3(1), dim3(1024), 0, static_cast<cudaStream_t>(stream), logits, n,
+                      forced, forced_len, pos, token, log, log_len));
   return TQ4_OK;
 }
 

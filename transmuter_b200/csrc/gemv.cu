@@ -602,6 +602,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
   const int u0 = unit_first(blockIdx.x, p.units, gridDim.x);
   const int u1 = unit_first(blockIdx.x + 1, p.units, gridDim.x);
 
+  pdl_trigger();
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full(s), 1);
@@ -614,6 +615,8 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
 
   if (warp == 8) {
     // ---------------- TMA producer ----------------
+    // The packed weights, scales and zero points are constant: the ring starts filling before the
+    // previous kernel on the stream has finished (programmatic dependent launch).
     if (lane == 0) {
       const uint32_t sc_bytes = kScaleRows * p.nbs * p.st_bytes;
       int gs = 0;
@@ -641,6 +644,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
   const int rl = warp * 16 + g;
   uint16_t* act = reinterpret_cast<uint16_t*>(smem + p.act_off);
   float4* segf = reinterpret_cast<float4*>(smem + p.seg_off);
+  pdl_wait();  // activations, outputs and partials belong to the stream's order from here on
   {
     // the activations of the groups this CTA's units touch (one or two runs, or the whole row)
     const int c_a = u0 % p.groups, c_b = (u1 - 1) % p.groups;
@@ -910,8 +914,8 @@ static cudaError_t launch_m1_t(const Weight& w, const GemvArgs& args, int grid, 
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  kern<<<grid, kGemvThreads, smem + 1024, st>>>(w.gv_wmap, w.gv_smap, w.gv_zmap, args);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(kGemvThreads), smem + 1024, st, w.gv_wmap, w.gv_smap, w.gv_zmap,
+                    args);
 }
 
 template <tq4_dtype AT>

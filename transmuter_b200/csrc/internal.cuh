@@ -7,6 +7,7 @@
 #include <cstring>
 #include <string>
 #include <type_traits>
+#include <utility>
 
 #include "common.cuh"
 
@@ -63,6 +64,25 @@ inline const char* dtype_name(tq4_dtype t) {
       return _e == cudaErrorMemoryAllocation ? TQ4_ERR_OUT_OF_MEMORY : TQ4_ERR_CUDA;        \
     }                                                                                       \
   } while (0)
+
+// Launch with the programmatic-stream-serialization attribute (see pdl_wait in common.cuh), unless
+// the environment sets TQ4_PDL=0, in which case it is an ordinary launch.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // A device allocation owned by a handle (freed on destruction).
 struct DeviceBuffer {

@@ -119,6 +119,8 @@ __global__ void dequant_kernel(const uint8_t* __restrict__ q, int64_t row_bytes,
                                float z_const, int64_t n_pad, int bs_log2, int64_t n,
                                int64_t k, const int64_t* __restrict__ rows, int64_t n_rows,
                                T* __restrict__ out) {
+  pdl_wait();  // row indices may come from the previous kernel
+  pdl_trigger();
   const int64_t total = n * k;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -217,10 +219,10 @@ template <int BITS, typename T>
 static void launch_dequant(const Weight& w, const int64_t* rows, int64_t n_out, void* out,
                            cudaStream_t st) {
   const int64_t total = n_out * w.desc.K;
-  dequant_kernel<BITS, T><<<grid_for(total, 256), 256, 0, st>>>(
-      static_cast<const uint8_t*>(w.q.ptr), w.row_bytes, static_cast<const T*>(w.scales.ptr),
-      static_cast<const T*>(w.zps.ptr), w.z_const, w.n_pad, w.bs_log2, n_out, w.desc.K, rows,
-      w.desc.N, static_cast<T*>(out));
+  launch_pdl(dequant_kernel<BITS, T>, dim3(grid_for(total, 256)), dim3(256), 0, st,
+             static_cast<const uint8_t*>(w.q.ptr), w.row_bytes, static_cast<const T*>(w.scales.ptr),
+             static_cast<const T*>(w.zps.ptr), w.z_const, w.n_pad, w.bs_log2, n_out, (int64_t)w.desc.K, rows,
+             (int64_t)w.desc.N, static_cast<T*>(out));
 }
 
 template <typename T>
