@@ -1,0 +1,52 @@
+"""GPU tests of the N-sharded MatMulNBits path (tq4_comm_* / tq4_sharded_*): a one-rank
+communicator in this process, and two ranks (one process per GPU, NCCL all-gather over NVLink)
+through tests/sharded_worker.py when the box has two GPUs. The sharded Y must equal the
+unsharded handle's Y on the same GPU to within the split-K summation order."""
+
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import matmul_nbits as o
+from transmuter_b200 import sharded, workloads
+from transmuter_b200.quantized import PackedWeight
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.mark.parametrize("m", [1, 4, 40])
+def test_one_rank_sharded_equals_unsharded(m):
+    dev = torch.device("cuda:0")
+    cfg = workloads.Config(f"shard-one-{m}", 1024, 3000, m, zp="packed", a_type="f16", scale_type="f16")
+    p = workloads.make(cfg)
+    b, s = torch.from_numpy(p["B"]).to(dev), torch.from_numpy(p["scales"]).to(dev)
+    z = torch.from_numpy(p["zp"]).to(dev)
+    a = torch.from_numpy(p["A"]).to(dev)
+    comm = sharded.Comm(sharded.Comm.unique_id(), 1, 0, 0, timeout_ms=30000)
+    sw = sharded.ShardedWeight(comm, (1024, 3000, 4, 32), b, s, z, dtype=torch.float16)
+    pw = PackedWeight((1024, 3000, 4, 32), b, s, z, dtype=torch.float16, device=dev)
+    assert (sw.first, sw.count) == (0, 3000)
+    y_sh, y_ref = sw.matmul(a), pw.matmul(a)
+    torch.cuda.synchronize()
+    assert torch.equal(y_sh, y_ref)  # one rank: the same kernel over the same rows
+    ref, _ = o.matmul_nbits(p["attrs"], p["A"], p["B"], p["scales"], p["zp"])
+    assert o.rel_l2(y_sh.double().cpu().numpy(), ref) < 5e-3
+    sw.close()
+    pw.close()
+    comm.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_sharded_equals_unsharded():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29517",
+           os.path.join(ROOT, "tests", "sharded_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    assert '"ok": true' in r.stdout
