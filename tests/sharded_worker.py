@@ -5,7 +5,8 @@ Every rank builds the same seeded weights, takes its rows through tq4_sharded_cr
 tq4_sharded_matmul (its GEMV / GEMM, then the NCCL all-gather and, for M > 1, the unshard
 kernel) and compares the full Y with the unsharded handle on its own GPU. The columns come from
 the same kernels over the same rows, so they agree to within the split-K summation order
-(rel-L2 1e-6); the unsharded result is itself pinned to the oracle by the parity tests.
+(rel-L2 1e-6 for f32 outputs; 1e-4 for f16 outputs, where that order can move a value by one
+f16 ulp); the unsharded result is itself pinned to the oracle by the parity tests.
 Exit status 0 when every case agrees on every rank.
 """
 
@@ -57,11 +58,11 @@ def main():
         y_ref = pw.matmul(a)
         torch.cuda.synchronize()
         err = o.rel_l2(y_sh.double().cpu().numpy(), y_ref.double().cpu().numpy())
-        worst.append((cfg.name, err))
+        worst.append((cfg.name, err, 1e-6 if at == "f32" else 1e-4))
         sw.close()
         pw.close()
     comm.close()
-    ok = all(e < 1e-6 for _, e in worst)
+    ok = all(e < tol for _, e, tol in worst)
     flags = torch.tensor([int(ok)])
     dist.all_reduce(flags, op=dist.ReduceOp.MIN)
     if rank == 0:
