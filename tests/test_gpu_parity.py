@@ -203,6 +203,25 @@ def test_large_m_parity(k, n, m, bits, bs, zp, st, at, t, bias):
     assert o.rel_l2(got, want) < TOL[at], o.rel_l2(got, want)
 
 
+# f32 activations at M > 16 take the tensor cores as row-scaled f16 (and f32 weights as
+# row-scaled f16); the rel-L2 1e-3 bar of f32 activations still holds, for ordinary, wide and
+# tiny scales (the latter would sit in f16's subnormal range without the row exponent).
+F32_PREFILL = [
+    (1024, 384, 48, 32, "none", (0.005, 0.02)),
+    (1000, 333, 40, 16, "float", (0.005, 0.02)),
+    (2048, 500, 100, 64, "packed", (0.001, 2.0)),
+    (72, 16, 20, 32, "none", (0.005, 0.02)),
+    (1024, 256, 64, 32, "packed", (1e-6, 1e-5)),
+    (4096, 640, 300, 128, "packed", (0.002, 0.01)),
+]
+
+
+@pytest.mark.parametrize("k,n,m,bs,zp,scale_range", F32_PREFILL)
+def test_f32_prefill_parity(k, n, m, bs, zp, scale_range):
+    got, want, _ = run_case(k, n, m, 4, bs, zp, "f32", "f32", "f32", True, scale_range=scale_range)
+    assert o.rel_l2(got, want) < TOL["f32"], o.rel_l2(got, want)
+
+
 def test_c1_full_size():
     cfg = workloads.CONFIGS["c1"]
     got, want, _ = run_case(cfg.k, cfg.n, cfg.m, 4, 32, "none", "f32", "f32", "f32", False)
@@ -278,3 +297,22 @@ def test_concurrent_streams_do_not_share_workspace():
 
 def test_device_status_clean():
     assert device_status() == 0
+
+
+def test_lm_head_row_tiles_handed_out_in_arrival_order():
+    """The 151936-row lm_head at M = 1 hands whole row tiles to CTAs through an arrival counter
+    that the last CTA resets: back-to-back calls on one handle (the next call's prefetch overlaps
+    the previous call) must each see a fresh hand-out, and the result has no partial sums, so
+    every call gives the same bits whatever CTA took which tile."""
+    cfg = workloads.CONFIGS["c3m1"]
+    p = workloads.make(cfg)
+    w = weight_for(cfg, p, "f32")
+    a = to_dev(p["A"])
+    a2 = torch.flip(a, dims=[1]).contiguous()
+    ys = [w.matmul(x) for x in (a, a2, a, a2, a)]  # no synchronisation between the calls
+    torch.cuda.synchronize()
+    assert torch.equal(ys[0], ys[2]) and torch.equal(ys[0], ys[4]) and torch.equal(ys[1], ys[3])
+    wd = w.dequantize().double()
+    for x, y in ((a, ys[0]), (a2, ys[1])):
+        want = x.double() @ wd.T
+        assert ((y.double() - want).norm() / want.norm()).item() < 1e-3

@@ -46,7 +46,7 @@ def make_weight(cfg):
 
 
 @pytest.mark.parametrize("name,m", [("c5-4096x1024-m16", 16), ("c5-4096x1024-m1", 1), ("c5-14336x4096-m16", 16),
-                                    ("c1", 1), ("c5-4096x14336-m16", 9)])
+                                    ("c1", 1), ("c5-4096x14336-m16", 9), ("c3m1", 1)])
 def test_noalloc_matches_matmul_on_two_calls(name, m):
     cfg = workloads.CONFIGS[name]
     w, p = make_weight(cfg)

@@ -46,6 +46,29 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ x,
   float* yr = y + blockIdx.x * n;
   const float* dr = delta ? delta + blockIdx.x * n : nullptr;
   float ss = 0.f;
+  if (n <= 8 * 256) {  // the row stays in registers: one memory round trip
+    float v[8], wv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t i = threadIdx.x + 256 * j;
+      v[j] = i < n ? xr[i] : 0.f;
+      wv[j] = i < n ? w[i] : 0.f;
+      if (dr && i < n) v[j] += dr[i];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t i = threadIdx.x + 256 * j;
+      if (dr && i < n) xr[i] = v[j];
+      ss = fmaf(v[j], v[j], ss);
+    }
+    const float inv = 1.f / sqrtf(block_sum<256>(ss, red) / (float)n + eps);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t i = threadIdx.x + 256 * j;
+      if (i < n) yr[i] = v[j] * inv * wv[j];
+    }
+    return;
+  }
   for (int64_t i = threadIdx.x; i < n; i += 256) {
     float v = xr[i];
     if (dr) {
@@ -100,7 +123,9 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(float* __restrict__ q
 // K/V row is read once per token. A chunk keeps its max m, sum l and unnormalised output
 // o = sum_p exp(s_p - m) v_p; the last chunk CTA of a KV head (atomic arrival count) combines them
 // in chunk order, so the result does not depend on scheduling. The CTA whose chunk holds the new
-// position writes k_new / v_new into the cache; the other chunks never read that row.
+// position writes k_new / v_new into the cache; the other chunks never read that row. A CTA first
+// copies its chunk of K and V into shared memory with 16-byte loads all in flight together (one
+// memory round trip), then works from there.
 constexpr int kAttnChunk = 32;
 constexpr int kAttnThreads = 128;
 constexpr int kAttnMaxGroup = 8;
@@ -134,6 +159,19 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
   float* kc = k_cache + (int64_t)kvh * max_len * D;
   float* vc = v_cache + (int64_t)kvh * max_len * D;
   const bool has_new = (p0 + np == L);  // this chunk holds position L - 1
+  extern __shared__ float4 kv_chunk[];  // K rows [kAttnChunk][D], then V rows
+  float* ks = reinterpret_cast<float*>(kv_chunk);
+  float* vs = ks + kAttnChunk * D;
+  const int D4 = head_dim / 4;
+#pragma unroll 8
+  for (int i = threadIdx.x; i < np * D4; i += kAttnThreads) {
+    const int pi = i / D4, d4 = i - pi * D4;
+    const bool nw = (p0 + pi == L - 1);
+    const float4* kr = reinterpret_cast<const float4*>(nw ? kn : kc + (int64_t)(p0 + pi) * D);
+    const float4* vr = reinterpret_cast<const float4*>(nw ? vn : vc + (int64_t)(p0 + pi) * D);
+    reinterpret_cast<float4*>(ks)[i] = kr[d4];
+    reinterpret_cast<float4*>(vs)[i] = vr[d4];
+  }
   for (int i = threadIdx.x; i < G * head_dim; i += kAttnThreads) qs[i] = q[(int64_t)kvh * G * D + i];
   if (has_new)
     for (int d = threadIdx.x; d < head_dim; d += kAttnThreads) {
@@ -145,8 +183,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
   // scores: warp w takes positions w, w + 4, ...; lanes split head_dim
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = warp; i < np; i += kAttnThreads / 32) {
-    const int p = p0 + i;
-    const float* kp = (p == L - 1) ? kn : kc + (int64_t)p * D;
+    const float* kp = ks + i * D;
     float dot[kAttnMaxGroup];
 #pragma unroll
     for (int g = 0; g < kAttnMaxGroup; ++g) dot[g] = 0.f;
@@ -188,8 +225,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
 #pragma unroll
     for (int g = 0; g < kAttnMaxGroup; ++g) o[g] = 0.f;
     for (int i = 0; i < np; ++i) {
-      const int p = p0 + i;
-      const float vv = (p == L - 1) ? vn[d] : vc[(int64_t)p * D + d];
+      const float vv = vs[i * D + d];
 #pragma unroll
       for (int g = 0; g < kAttnMaxGroup; ++g)
         if (g < G) o[g] = fmaf(sc[g][i], vv, o[g]);
@@ -364,9 +400,12 @@ tq4_status tq4_attention_decode(const float* q, const float* k_new, const float*
   clear_error();
   if (!q || !k_new || !v_new || !k_cache || !v_cache || !pos || !out || heads <= 0 || kv_heads <= 0 ||
       heads % kv_heads || heads / kv_heads > kAttnMaxGroup || head_dim <= 0 || head_dim > kAttnMaxDim ||
-      max_len <= 0 || kv_heads > 65535) {
+      (head_dim & 3) || max_len <= 0 || kv_heads > 65535 ||
+      ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new) |
+        reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15)) {
     set_error("tq4_attention_decode: bad arguments (heads a multiple of kv_heads, at most %d query heads per "
-              "KV head, head_dim <= %d)", kAttnMaxGroup, kAttnMaxDim);
+              "KV head, head_dim a multiple of 4 and <= %d, K/V pointers 16-byte aligned)",
+              kAttnMaxGroup, kAttnMaxDim);
     return TQ4_ERR_INVALID_ARGUMENT;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -375,7 +414,14 @@ tq4_status tq4_attention_decode(const float* q, const float* k_new, const float*
   float* part = nullptr;
   int* ctr = nullptr;
   TQ4_TRY(attn_scratch(st, (int64_t)kv_heads * chunks * G * (head_dim + 2) * 4, kv_heads, &part, &ctr));
-  TQ4_CUDA(launch_pdl(attention_decode_kernel, dim3(chunks, kv_heads), dim3(kAttnThreads), 0, st, q, k_new, v_new,
+  const size_t dyn = (size_t)2 * kAttnChunk * head_dim * sizeof(float);
+  static bool attr_set = false;
+  if (!attr_set) {
+    TQ4_CUDA(cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  2 * kAttnChunk * kAttnMaxDim * (int)sizeof(float)));
+    attr_set = true;
+  }
+  TQ4_CUDA(launch_pdl(attention_decode_kernel, dim3(chunks, kv_heads), dim3(kAttnThreads), dyn, st, q, k_new, v_new,
                       k_cache, v_cache, pos, out, heads, kv_heads, head_dim, max_len, 1.f / sqrtf((float)head_dim),
                       part, ctr, chunks));
   return TQ4_OK;

@@ -9,21 +9,28 @@
 //   warp 0   TMA producer: the activation tile (two 64-k boxes, 128B swizzle: the K-major B
 //            operand), the packed weight tile (128 rows x 64 bytes) and the stage's block-major
 //            scales / zero points, completing on full[s].
-//   warps 2-9 dequantise in registers: warp w owns TMEM lanes 32*(w%4).. (its 32 weight rows)
-//            and one half of the stage's k; each thread turns its row's 64 weights into
-//            RN_T(RN_T(q - z) * s) (exactly the reference's weight when T is A's type) and
-//            writes them with tcgen05.st into one of 4 TMEM weight slots (64 columns each).
+//   warps 2-17 dequantise in registers: warp w owns TMEM lanes 32*(w%4).. (its 32 weight rows)
+//            and one 16-byte piece of each row (32 weights spread over the stage's k; the packed
+//            tile arrives with the 64-byte swizzle, so these loads are free of bank conflicts);
+//            each thread turns them into RN_T(RN_T(q - z) * s) (exactly the reference's weight
+//            when T is A's type) and writes them with tcgen05.st into one of 4 TMEM weight slots
+//            (64 columns each).
 //   warp 1   TMEM allocation, and one thread that issues tcgen05.mma (M=128, N=TM, K=16, A from
 //            TMEM, B from shared memory) x 8 per stage into the f32 accumulator (TM columns);
 //            tcgen05.commit frees the shared-memory stage and the TMEM slot.
-//   warps 2-9 then run the epilogue: tcgen05.ld of their lanes (one weight row, consecutive
-//            activation rows), bias, conversion, stores (a warp writes 32 consecutive columns).
+//   warps 2-17 then run the epilogue: tcgen05.ld of their lanes (one weight row, consecutive
+//            activation rows), bias, conversion into a [TM][128] tile in the idle stage buffers,
+//            then 16-byte stores of whole Y row segments.
 // The shared-memory ring (2-4 stages) and the TMEM slot ring (4) are independent, so the copies,
 // the dequantisation and the MMAs overlap instead of paying their latencies in sequence.
 // Every mbarrier wait is bounded by a clock deadline; a wait that runs out writes the device
 // status word, raises the CTA's abort flag and the CTA winds down (no trap, no endless spin).
 #include "internal.cuh"
 #include "sm100.cuh"
+
+#include <map>
+#include <memory>
+#include <mutex>
 
 namespace tq4 {
 
@@ -47,16 +54,6 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b, bool bf) {
@@ -140,16 +137,17 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
-// 32 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
-      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
-        "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
-        "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
+// 2 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st2(uint32_t taddr, uint32_t r0, uint32_t r1) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1,%2};" ::"r"(taddr), "r"(r0), "r"(r1) : "memory");
+}
+
+// 8 consecutive 32-bit TMEM columns of this thread's lane (loaded and waited for).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 struct GemmArgs {
@@ -169,11 +167,14 @@ struct GemmArgs {
   void* y;
   tq4_dtype y_t;
   int64_t ldy;
+  const float* row_scale;  // per activation row factor of an f32 A carried as scaled f16, or null
+  const int32_t* wexp;     // per weight row exponent of f32 weights carried as scaled f16 / bf16, or null
 };
 
-constexpr int kGemmThreads = 320;  // producer, MMA, 8 dequant / epilogue warps
+constexpr int kDeqWarps = 16;      // dequantising / epilogue warps: 4 per TMEM lane quarter
+constexpr int kGemmThreads = 64 + 32 * kDeqWarps;  // + the producer and MMA warps
 constexpr int WN = 128;            // weight rows per CTA: the MMA's M and the TMEM lanes
-constexpr int kMaxStages = 4;      // shared-memory stages
+constexpr int kMaxStages = 8;      // shared-memory stages
 constexpr int kASlots = 4;         // dequantised weight stages in TMEM, 64 columns each
 constexpr int kTmemCols = 512;
 
@@ -199,27 +200,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = smem_raw + (base - raw_addr);
   const int S = p.stages;
   const uint32_t bars = base + S * p.stage_bytes;
-  auto full = [&](int s) { return bars + 8 * s; };
+  auto full = [&](int s) { return bars + 8 * s; };                        // activations landed
   auto empty = [&](int s) { return bars + 8 * (kMaxStages + s); };
   auto afull = [&](int a) { return bars + 8 * (2 * kMaxStages + a); };
   auto aempty = [&](int a) { return bars + 8 * (2 * kMaxStages + kASlots + a); };
   const uint32_t accum = bars + 8 * (2 * kMaxStages + 2 * kASlots);
-  uint8_t* tail = smem + S * p.stage_bytes + 8 * (2 * kMaxStages + 2 * kASlots + 1);
+  auto wfull = [&](int s) { return bars + 8 * (2 * kMaxStages + 2 * kASlots + 1 + s); };  // weights landed
+  uint8_t* tail = smem + S * p.stage_bytes + 8 * (3 * kMaxStages + 2 * kASlots + 1);
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(tail);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * WN, m0 = blockIdx.y * TM;
   const int KT = p.ktiles;
-  const uint32_t tx_bytes = L::FIXED + WN * p.nb * p.st_bytes * (p.has_zp ? 2 : 1);
+  const uint32_t tx_a = L::ACT_BYTES;
+  const uint32_t tx_w = L::WP_BYTES + WN * p.nb * p.st_bytes * (p.has_zp ? 2 : 1);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full(s), 1);
-      mbar_init(empty(s), 1 + 8);  // the MMAs' commit + the 8 dequantising warps
+      mbar_init(wfull(s), 1);
+      mbar_init(empty(s), 1 + kDeqWarps);  // the MMAs' commit + the dequantising warps
     }
     for (int a = 0; a < kASlots; ++a) {
-      mbar_init(afull(a), 8);
+      mbar_init(afull(a), kDeqWarps);
       mbar_init(aempty(a), 1);
     }
     mbar_init(accum, 1);
@@ -234,27 +238,54 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = *tmem_slot;
+  // The next kernel on the stream may be scheduled only once this CTA holds its tensor memory:
+  // a dependent CTA that took an SM's TMEM first would block this CTA's allocation while it
+  // waits for this grid (and a GEMM CTA owns its SM's shared memory, see plan_gemm_smem).
+  pdl_trigger();
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      int issued = 0;
-      for (int kt = 0; kt < KT; ++kt) {
+      // The first ring's weights, scales and zero points are constant: they load before the
+      // previous kernel on the stream has finished (programmatic dependent launch); the
+      // activations of those stages follow once it has.
+      const int pre = min(S, KT);
+      for (int kt = 0; kt < pre; ++kt) {
+        const uint32_t st = base + kt * p.stage_bytes;
+        const int b0 = (kt * 128) >> p.bs_log2;
+        mbar_expect_tx(wfull(kt), tx_w);
+        tma_load_2d(st + L::ACT_BYTES, &map_w, kt * 64, n0, wfull(kt));
+        tma_load_2d(st + p.sc_off, &map_s, n0, b0, wfull(kt));
+        if (p.has_zp) tma_load_2d(st + p.zc_off, &map_z, n0, b0, wfull(kt));
+      }
+      pdl_wait();
+      for (int kt = 0; kt < pre; ++kt) {
+        const uint32_t st = base + kt * p.stage_bytes;
+        mbar_expect_tx(full(kt), tx_a);
+        tma_load_2d(st, &map_a, kt * 128, m0, full(kt));
+        tma_load_2d(st + L::ACT_BYTES / 2, &map_a, kt * 128 + 64, m0, full(kt));
+      }
+      int issued = pre;
+      for (int kt = pre; kt < KT; ++kt) {
         const int s = kt % S;
         const uint32_t ph = (kt / S) & 1;
         if (!mbar_wait(empty(s), ph ^ 1, abort_flag, kDevTimeoutStageEmpty)) break;
         const uint32_t st = base + s * p.stage_bytes;
         const int b0 = (kt * 128) >> p.bs_log2;
-        mbar_expect_tx(full(s), tx_bytes);
+        mbar_expect_tx(wfull(s), tx_w);
+        tma_load_2d(st + L::ACT_BYTES, &map_w, kt * 64, n0, wfull(s));
+        tma_load_2d(st + p.sc_off, &map_s, n0, b0, wfull(s));
+        if (p.has_zp) tma_load_2d(st + p.zc_off, &map_z, n0, b0, wfull(s));
+        mbar_expect_tx(full(s), tx_a);
         tma_load_2d(st, &map_a, kt * 128, m0, full(s));
         tma_load_2d(st + L::ACT_BYTES / 2, &map_a, kt * 128 + 64, m0, full(s));
-        tma_load_2d(st + L::ACT_BYTES, &map_w, kt * 64, n0, full(s));
-        tma_load_2d(st + p.sc_off, &map_s, n0, b0, full(s));
-        if (p.has_zp) tma_load_2d(st + p.zc_off, &map_z, n0, b0, full(s));
         issued = kt + 1;
       }
       // the copies still in flight complete before the CTA exits (bounded)
-      for (int kt = max(0, issued - S); kt < issued; ++kt) mbar_drain(full(kt % S), (kt / S) & 1);
+      for (int kt = max(0, issued - S); kt < issued; ++kt) {
+        mbar_drain(full(kt % S), (kt / S) & 1);
+        mbar_drain(wfull(kt % S), (kt / S) & 1);
+      }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -283,66 +314,65 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ---------------- dequantising warps (then epilogue) ----------------
     const int quarter = warp & 3;          // TMEM lanes 32*quarter .. +31
-    const int khalf = (warp - 2) >> 2;     // k 64*khalf .. +63 of each stage
+    const int tp = (warp - 2) >> 2;        // 16-byte piece tp of its row: k = 16j + 4tp + e, j = 0..7
     const int r = quarter * 32 + lane;     // this thread's weight row in the tile
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     constexpr bool T_SAME = (BF && T == TQ4_BF16) || (!BF && T == TQ4_F16);
+    const int we = (T == TQ4_F32 && p.wexp) ? p.wexp[n0 + r] : 0;  // n0 + r < n_pad
     for (int kt = 0; kt < KT; ++kt) {
       const int s = kt % S, a = kt % kASlots;
-      if (!mbar_wait(full(s), (kt / S) & 1, abort_flag, kDevTimeoutTmaFull)) break;
+      if (!mbar_wait(wfull(s), (kt / S) & 1, abort_flag, kDevTimeoutTmaFull)) break;
       if (!mbar_wait(aempty(a), ((kt / kASlots) & 1) ^ 1, abort_flag, kDevTimeoutDequant)) break;
       const uint8_t* st = smem + s * p.stage_bytes;
-      const uint8_t* wp = st + L::ACT_BYTES + r * 64 + khalf * 8;
+      // the 64-byte swizzle puts piece tp of row r at 16 * (tp ^ ((r >> 1) & 3)): the 8 lanes of
+      // each load phase read 8 different bank groups
+      const uint4 v = *reinterpret_cast<const uint4*>(st + L::ACT_BYTES + r * 64 + ((tp ^ ((r >> 1) & 3)) << 4));
       const uint8_t* sc = st + p.sc_off;
       const uint8_t* zc = st + p.zc_off;
-      // words 2*khalf and 2*khalf+1 of the row's four 16-byte pieces: steps 4*khalf .. +3
-      uint2 v[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) v[t] = *reinterpret_cast<const uint2*>(wp + t * 16);
       const int b0 = (kt * 128) >> p.bs_log2;
-      uint32_t out[32];  // column c holds k = 64*khalf + 2c, 2c + 1
+      const uint32_t col0 = lane_addr + TM + a * 64 + 2 * tp;  // column 8j + 2tp holds k = 16j + 4tp, +1
+      uint32_t s2 = 0, oz2 = 0, oz16n = 0;
+      float scv = 0.f, z = 0.f;
 #pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const int j = 4 * khalf + jj;
+      for (int j = 0; j < 8; ++j) {
         const int lb = ((kt * 128 + 16 * j) >> p.bs_log2) - b0;  // staged block row
+        const bool new_block = (j == 0) || (((16 * j) & ((1 << p.bs_log2) - 1)) == 0);
+        const uint32_t x = (j < 2) ? v.x : (j < 4) ? v.y : (j < 6) ? v.z : v.w;
+        uint32_t w0, w1;
         if (T_SAME && p.int_zp) {
           // (O + q) - (O + z) is exact in the MMA type; one more multiply gives RN_T((q - z) * s)
-          const uint16_t* sc16 = reinterpret_cast<const uint16_t*>(sc);
-          const uint32_t sv = sc16[lb * WN + r];
-          const uint32_t s2 = sv | (sv << 16);
-          const float z = p.has_zp ? scale_to_f32(zc, lb * WN + r, 2, BF) : p.z_const;
-          const uint32_t oz2 = h2_splat((BF ? 128.f : 1024.f) + z, BF);
-          const uint32_t oz16n = h2_splat(-(64.f + z), BF);
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const uint32_t x = (jj < 2) ? v[t].x : v[t].y;
-            const uint32_t src = (jj & 1) ? (x >> 8) : x;
-            uint32_t d0, d1;
-            if (!BF) {
-              d0 = h2_sub(lop3_and_or(src, 0x000F000Fu, 0x64006400u), oz2, false);
-              const uint32_t r1 = lop3_and_or(src, 0x00F000F0u, 0x64006400u);  // 1024 + 16 q
-              asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d1) : "r"(r1), "r"(0x2C002C00u), "r"(oz16n));
-            } else {
-              d0 = h2_sub(lop3_and_or(src, 0x000F000Fu, 0x43004300u), oz2, true);
-              d1 = h2_sub(lop3_and_or(src >> 4, 0x000F000Fu, 0x43004300u), oz2, true);
-            }
-            out[8 * jj + 2 * t] = h2_mul(d0, s2, BF);
-            out[8 * jj + 2 * t + 1] = h2_mul(d1, s2, BF);
+          if (new_block) {
+            const uint32_t sv = reinterpret_cast<const uint16_t*>(sc)[lb * WN + r];
+            s2 = sv | (sv << 16);
+            z = p.has_zp ? scale_to_f32(zc, lb * WN + r, 2, BF) : p.z_const;
+            oz2 = h2_splat((BF ? 128.f : 1024.f) + z, BF);
+            oz16n = h2_splat(-(64.f + z), BF);
           }
+          const uint32_t src = (j & 1) ? (x >> 8) : x;
+          uint32_t d0, d1;
+          if (!BF) {
+            d0 = h2_sub(lop3_and_or(src, 0x000F000Fu, 0x64006400u), oz2, false);
+            const uint32_t r1 = lop3_and_or(src, 0x00F000F0u, 0x64006400u);  // 1024 + 16 q
+            asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d1) : "r"(r1), "r"(0x2C002C00u), "r"(oz16n));
+          } else {
+            d0 = h2_sub(lop3_and_or(src, 0x000F000Fu, 0x43004300u), oz2, true);
+            d1 = h2_sub(lop3_and_or(src >> 4, 0x000F000Fu, 0x43004300u), oz2, true);
+          }
+          w0 = h2_mul(d0, s2, BF);
+          w1 = h2_mul(d1, s2, BF);
         } else {
-          const float scv = scale_to_f32(sc, lb * WN + r, p.st_bytes, T == TQ4_BF16);
-          const float z = p.has_zp ? scale_to_f32(zc, lb * WN + r, p.st_bytes, T == TQ4_BF16) : p.z_const;
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const uint32_t x = (jj < 2) ? v[t].x : v[t].y;
-            uint32_t q0, q1;
-            q_pairs4(x, jj, BF, q0, q1);
-            out[8 * jj + 2 * t] = deq_pair<BF, T>(q0, z, scv);
-            out[8 * jj + 2 * t + 1] = deq_pair<BF, T>(q1, z, scv);
+          // f32 weights: (q - z) * s * 2^-we, exact scaling of the f32 product before its rounding
+          if (new_block) {
+            scv = ldexpf(scale_to_f32(sc, lb * WN + r, p.st_bytes, T == TQ4_BF16), -we);
+            z = p.has_zp ? scale_to_f32(zc, lb * WN + r, p.st_bytes, T == TQ4_BF16) : p.z_const;
           }
+          uint32_t q0, q1;
+          q_pairs4(x, j, BF, q0, q1);
+          w0 = deq_pair<BF, T>(q0, z, scv);
+          w1 = deq_pair<BF, T>(q1, z, scv);
         }
+        tmem_st2(col0 + 8 * j, w0, w1);
       }
-      tmem_st32(lane_addr + TM + a * 64 + khalf * 32, out);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;");
       __syncwarp();
@@ -355,7 +385,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ---------------- epilogue ----------------
     const long long t0 = clock64();
     bool ok = true;
-    while (!mbar_try(accum, 0)) {
+    while (!mbar_test(accum, 0)) {
       if (clock64() - t0 > kWaitCycles) {
         report(kDevTimeoutAccum);
         *abort_flag = 1;
@@ -364,25 +394,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     asm volatile("tcgen05.fence::after_thread_sync;");
-    const int chalf = khalf;  // activation rows [chalf*TM/2, (chalf+1)*TM/2) of the tile
+    // D (TMEM lane = weight row, column = activation row) -> the tile [TM][128] in Y's type in the
+    // now idle stage buffers -> coalesced 16-byte stores of Y rows.
+    const int ys = p.y_t == TQ4_F32 ? 4 : 2;
     const int64_t n = (int64_t)n0 + r;
     const bool n_ok = n < p.N;
     const float bias_v = (p.bias && n_ok) ? load_as_f32(p.bias, n, p.bias_t) : 0.f;
-    if (__all_sync(0xffffffffu, ok && !*abort_flag)) {
+    const bool run = __all_sync(0xffffffffu, ok && !*abort_flag);
+    if (run) {
+      constexpr int CPW = TM / 4;  // activation rows (TMEM columns) per warp
 #pragma unroll 1
-      for (int c = chalf * (TM / 2); c < (chalf + 1) * (TM / 2); c += 16) {
-        uint32_t rr[16];
-        tmem_ld16(lane_addr + c, rr);
-        if (n_ok) {
+      for (int c = tp * CPW; c < (tp + 1) * CPW; c += 8) {
+        uint32_t rr[8];
+        tmem_ld8(lane_addr + c, rr);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int64_t m = (int64_t)m0 + c + i;
-            if (m < p.M) {
-              float v = __uint_as_float(rr[i]);
-              if (p.bias) v = round_to(v, p.y_t) + bias_v;
-              store_from_f32(p.y, m * p.ldy + n, p.y_t, v);
-            }
-          }
+        for (int i = 0; i < 8; ++i) {
+          const int ml = c + i;
+          float v = __uint_as_float(rr[i]);
+          if (we) v = ldexpf(v, we);
+          if (p.row_scale && m0 + ml < p.M) v *= p.row_scale[m0 + ml];  // a power of two: exact
+          if (p.bias) v = round_to(v, p.y_t) + bias_v;
+          uint8_t* dst = smem + ((int64_t)ml * WN + r) * ys;
+          if (p.y_t == TQ4_F32) *reinterpret_cast<float*>(dst) = v;
+          else if (p.y_t == TQ4_BF16) *reinterpret_cast<__nv_bfloat16*>(dst) = __float2bfloat16_rn(v);
+          else *reinterpret_cast<__half*>(dst) = __float2half_rn(v);
+        }
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * kDeqWarps) : "memory");
+    if (run) {
+      const int rows = min(TM, p.M - m0);
+      const int cpr = WN * ys / 16;  // 16-byte chunks per tile row
+      const int epc = 16 / ys;       // elements per chunk
+      const int tid = threadIdx.x - 64;
+      for (int i = tid; i < rows * cpr; i += 32 * kDeqWarps) {
+        const int ml = i / cpr, cc = i % cpr;
+        const int64_t nn = (int64_t)n0 + cc * epc;
+        const uint8_t* src = smem + ((int64_t)ml * WN + cc * epc) * ys;
+        uint8_t* dst = static_cast<uint8_t*>(p.y) + ((int64_t)(m0 + ml) * p.ldy + nn) * ys;
+        if (nn + epc <= p.N && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+          *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+        } else {
+          for (int e = 0; e < epc && nn + e < p.N; ++e)
+            for (int b = 0; b < ys; ++b) dst[e * ys + b] = src[e * ys + b];
         }
       }
     }
@@ -394,6 +448,58 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kTmemCols));
   }
+}
+
+// f32 activations for the tensor cores: row m of A becomes f16 values a * 2^-e(m), e(m) the
+// exponent of the row's largest magnitude (so every value is at most 2 and none overflows), and
+// row_scale[m] = 2^e(m) is multiplied back in the epilogue. The rounding to f16 is the only
+// change to A (relative 2^-11, like the GEMV's staged activations).
+__global__ void __launch_bounds__(256) scale_rows_f16_kernel(const float* __restrict__ a, int64_t k,
+                                                             __half* __restrict__ out, float* __restrict__ row_scale) {
+  __shared__ float red[8];
+  const float* row = a + blockIdx.x * k;
+  float mx = 0.f;
+  for (int64_t i = threadIdx.x; i < k; i += 256) mx = fmaxf(mx, fabsf(row[i]));
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+  int e = 0;
+  if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
+  const float down = ldexpf(1.f, -e);
+  for (int64_t i = threadIdx.x; i < k; i += 256) out[blockIdx.x * k + i] = __float2half_rn(row[i] * down);
+  if (threadIdx.x == 0) row_scale[blockIdx.x] = ldexpf(1.f, e);
+}
+
+// Per-(device, stream) scratch of the scaled f16 activations.
+struct RowScratch {
+  DeviceBuffer a16, scale;
+};
+static std::mutex g_row_mu;
+static std::map<std::pair<int, cudaStream_t>, std::unique_ptr<RowScratch>> g_row_scratch;
+
+static tq4_status row_scratch(cudaStream_t st, int64_t a_bytes, int64_t rows, void** a16, float** scale) {
+  int dev = 0;
+  TQ4_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_row_mu);
+  auto& slot = g_row_scratch[{dev, st}];
+  if (!slot) slot.reset(new RowScratch());
+  if (slot->a16.bytes < a_bytes || slot->scale.bytes < rows * 4) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    TQ4_CUDA(cudaStreamIsCapturing(st, &cs));
+    if (cs != cudaStreamCaptureStatusNone) {
+      set_error("MatMulNBits: an f32 prefill call needs scratch first allocated during stream capture; "
+                "make the same call once before capturing");
+      return TQ4_ERR_INVALID_ARGUMENT;
+    }
+    TQ4_CUDA(cudaStreamSynchronize(st));
+    if (slot->a16.bytes < a_bytes) TQ4_TRY(slot->a16.alloc(a_bytes));
+    if (slot->scale.bytes < rows * 4) TQ4_TRY(slot->scale.alloc(rows * 4));
+  }
+  *a16 = slot->a16.ptr;
+  *scale = static_cast<float*>(slot->scale.ptr);
+  return TQ4_OK;
 }
 
 // ---- host side ---------------------------------------------------------------------------------
@@ -449,7 +555,7 @@ tq4_status make_weight_maps(Weight& w) {
   const CUtensorMapDataType sdt = st == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
   const int nb = gemm_scale_blocks(w);
   TQ4_TRY(make_map(&w.wmaps[0], CU_TENSOR_MAP_DATA_TYPE_UINT8, w.q.ptr, w.row_bytes, w.n_pad, w.row_bytes, 64,
-                   WN, CU_TENSOR_MAP_SWIZZLE_NONE));
+                   WN, CU_TENSOR_MAP_SWIZZLE_64B));  // 16-byte piece c of row r at c ^ ((r >> 1) & 3)
   TQ4_TRY(make_map(&w.smaps[0], sdt, w.scales.ptr, w.n_pad, w.blocks_pad, w.n_pad * st, WN, nb,
                    CU_TENSOR_MAP_SWIZZLE_NONE));
   if (w.zps.ptr)
@@ -477,9 +583,13 @@ static GemmPlan plan_gemm_smem(const Weight& w) {
   pl.zc_off = pl.sc_off + (sc_bytes + 127) / 128 * 128;
   const int end = pl.zc_off + (w.zps.ptr ? sc_bytes : 0);
   pl.stage_bytes = (end + 1023) / 1024 * 1024;
-  const int fixed = 1024 + 8 * (2 * kMaxStages + 2 * kASlots + 1) + 16;
+  const int fixed = 1024 + 8 * (3 * kMaxStages + 2 * kASlots + 1) + 16;
   pl.stages = std::min(kMaxStages, (kSmemLimit - fixed) / pl.stage_bytes);
   pl.smem = fixed + pl.stages * pl.stage_bytes;
+  // One GEMM CTA per SM: every CTA allocates all 512 TMEM columns, so a second CTA on the SM
+  // (from the next kernel on the stream, launched early) could only sit blocked in its
+  // allocation. Asking for more than half the SM's shared memory rules that out.
+  pl.smem = std::max(pl.smem, kSmemLimit / 2 + 1024);
   return pl;
 }
 
@@ -501,8 +611,7 @@ static tq4_status launch_gemm_t(const CUtensorMap& ma, const Weight& w, GemmArgs
     attr_set = true;
   }
   const dim3 grid((args.N + WN - 1) / WN, (args.M + TM - 1) / TM);
-  kern<<<grid, kGemmThreads, pl.smem, st>>>(ma, w.wmaps[0], w.smaps[0], w.zmaps[0], args);
-  TQ4_CUDA(cudaGetLastError());
+  TQ4_CUDA(launch_pdl(kern, grid, dim3(kGemmThreads), pl.smem, st, ma, w.wmaps[0], w.smaps[0], w.zmaps[0], args));
   return TQ4_OK;
 }
 
@@ -518,16 +627,18 @@ static tq4_status launch_gemm_tm(const CUtensorMap& ma, const Weight& w, const G
 // Whether the tcgen05 GEMM takes this call (else A goes through the GEMV in 16-row slices).
 static bool gemm_eligible(const Weight& w, const void* a, tq4_dtype a_t) {
   if (w.desc.bits != 4) return false;
-  if (a_t != TQ4_F16 && a_t != TQ4_BF16) return false;
+  if (a_t != TQ4_F16 && a_t != TQ4_BF16 && a_t != TQ4_F32) return false;
   if ((w.desc.K * 2) % 16 != 0) return false;                    // TMA row stride
   if ((reinterpret_cast<uintptr_t>(a) & 15) != 0) return false;  // TMA base address
   return w.wmaps_ok;
 }
 
-// Activation rows per CTA: the largest tile that still gives half the SMs a tile.
+// Activation rows per CTA: no wider than M needs, and the largest tile that still gives half the
+// SMs a tile.
 static int choose_tm(const Weight& w, int64_t m) {
   const int64_t nt = (w.desc.N + WN - 1) / WN;
   for (int tm : {256, 128, 64}) {
+    if (tm / 2 >= m) continue;  // the half-size tile already covers M
     if (((m + tm - 1) / tm) * nt >= w.num_sms / 2) return tm;
   }
   return 32;
@@ -535,6 +646,18 @@ static int choose_tm(const Weight& w, int64_t m) {
 
 tq4_status run_gemm_tc(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,
                        tq4_dtype bias_t, void* y, tq4_dtype y_t, int64_t ldy, cudaStream_t st) {
+  const float* row_scale = nullptr;
+  if (a_t == TQ4_F32) {  // carried as row-scaled f16 (scale_rows_f16_kernel)
+    void* a16 = nullptr;
+    float* rs = nullptr;
+    TQ4_TRY(row_scratch(st, m * w.desc.K * 2, m, &a16, &rs));
+    scale_rows_f16_kernel<<<(unsigned)m, 256, 0, st>>>(static_cast<const float*>(a), w.desc.K,
+                                                       static_cast<__half*>(a16), rs);
+    TQ4_CUDA(cudaGetLastError());
+    a = a16;
+    a_t = TQ4_F16;
+    row_scale = rs;
+  }
   const int tm = choose_tm(w, m);
   CUtensorMap ma;
   const CUtensorMapDataType adt = a_t == TQ4_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -555,6 +678,8 @@ tq4_status run_gemm_tc(const Weight& w, const void* a, int64_t m, tq4_dtype a_t,
   args.y = y;
   args.y_t = y_t;
   args.ldy = ldy;
+  args.row_scale = row_scale;
+  args.wexp = static_cast<const int32_t*>(w.wexp.ptr);
   const bool bf = a_t == TQ4_BF16;
   switch (tm) {
     case 256: return bf ? launch_gemm_tm<256, true>(ma, w, args, st) : launch_gemm_tm<256, false>(ma, w, args, st);

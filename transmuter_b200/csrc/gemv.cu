@@ -71,6 +71,7 @@ struct GemvArgs {
   int units;             // M = 1 stream-K: (row tile, stage) units, stages per row tile, max pieces
   int spr;
   int maxp;
+  int dyn;               // M = 1: whole row tiles handed out by an arrival counter (no partials)
   int64_t n_pad;
   float* ws;
   int* counters;
@@ -588,7 +589,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
   constexpr int SEG = 16 * SPS;
   constexpr int NSEG = GPS * 8 / SPS;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ int s_last;
+  __shared__ int s_lastv[2];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t sbase = (raw_addr + 1023) & ~1023u;
   uint8_t* smem = smem_raw + (sbase - raw_addr);
@@ -599,8 +600,9 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
   auto full = [&](int s) { return bars + 8 * s; };
   auto empty = [&](int s) { return bars + 8 * (kMaxStages + s); };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + p.bar_off + 8 * 2 * kMaxStages);
-  const int u0 = unit_first(blockIdx.x, p.units, gridDim.x);
-  const int u1 = unit_first(blockIdx.x + 1, p.units, gridDim.x);
+  volatile int* sinfo = reinterpret_cast<volatile int*>(smem + p.bar_off + 8 * 2 * kMaxStages + 16);  // dyn
+  const int u0 = p.dyn ? 0 : unit_first(blockIdx.x, p.units, gridDim.x);
+  const int u1 = p.dyn ? p.units : unit_first(blockIdx.x + 1, p.units, gridDim.x);
 
   pdl_trigger();
   if (threadIdx.x == 0) {
@@ -620,12 +622,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
     if (lane == 0) {
       const uint32_t sc_bytes = kScaleRows * p.nbs * p.st_bytes;
       int gs = 0;
-      for (int u = u0; u < u1; ++gs) {
-        const int s = gs % S;
-        if (!mbar_wait(empty(s), ((gs / S) & 1) ^ 1, abort_flag, kDevTimeoutStageEmpty)) break;
-        const int rt = u / p.groups, c0 = u % p.groups;
-        const int ng = min(min(GPS, p.groups - c0), u1 - u);  // a chunk never crosses a row tile
-        u += ng;
+      auto issue = [&](int s, int rt, int c0, int ng) {
         const int row0 = rt * kRows;
         const uint32_t st = sbase + s * p.stage_bytes;
         mbar_expect_tx(full(s), ng * kRows * 64 + sc_bytes * (p.has_zp ? 2 : 1));
@@ -633,6 +630,43 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
         const int b0 = (c0 * G) >> p.bs_log2;
         tma_load_2d(st + p.sc_off, &map_s, row0, b0, full(s));
         if (p.has_zp) tma_load_2d(st + p.zc_off, &map_z, row0, b0, full(s));
+      };
+      if (p.dyn) {
+        // Row tile blockIdx.x first (prefetched before the previous kernel finishes), then the
+        // tiles gridDim.x, gridDim.x + 1, ... in arrival order: CTAs that stream faster take more.
+        int rt = blockIdx.x;
+        bool waited = false, ok = true;
+        while (ok) {
+          if (rt >= p.ctas_n) {  // no work left: a stage that only says so
+            const int s = gs % S;
+            if (!mbar_wait(empty(s), ((gs / S) & 1) ^ 1, abort_flag, kDevTimeoutStageEmpty)) break;
+            sinfo[s] = -1;
+            mbar_arrive(full(s));
+            ++gs;
+            break;
+          }
+          for (int c0 = 0; c0 < p.groups && ok; c0 += GPS, ++gs) {
+            const int s = gs % S;
+            ok = mbar_wait(empty(s), ((gs / S) & 1) ^ 1, abort_flag, kDevTimeoutStageEmpty);
+            if (!ok) break;
+            sinfo[s] = rt * p.groups + c0;
+            issue(s, rt, c0, min(GPS, p.groups - c0));
+          }
+          if (!waited) {
+            pdl_wait();  // the counters belong to the stream's order
+            waited = true;
+          }
+          rt = gridDim.x + atomicAdd(&p.counters[0], 1);
+        }
+      } else {
+        for (int u = u0; u < u1; ++gs) {
+          const int s = gs % S;
+          if (!mbar_wait(empty(s), ((gs / S) & 1) ^ 1, abort_flag, kDevTimeoutStageEmpty)) break;
+          const int rt = u / p.groups, c0 = u % p.groups;
+          const int ng = min(min(GPS, p.groups - c0), u1 - u);  // a chunk never crosses a row tile
+          u += ng;
+          issue(s, rt, c0, ng);
+        }
       }
       for (int g = max(0, gs - S); g < gs; ++g) mbar_drain(full(g % S), (g / S) & 1);
     }
@@ -670,12 +704,24 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
   int gs = 0;
   bool ok = true;
   float acc0 = 0.f, acc8 = 0.f;
+  int npub = 0, pub_rt[2] = {0, 0}, pub_pieces[2] = {0, 0};
   for (int u = u0; u < u1; ++gs) {
-    const int rt = u / p.groups, c0 = u % p.groups;
-    const int ng = min(min(GPS, p.groups - c0), u1 - u);
-    u += ng;
     const int s = gs % S;
-    if (ok) ok = mbar_wait(full(s), (gs / S) & 1, abort_flag, kDevTimeoutTmaFull);
+    int rt, c0, ng;
+    if (p.dyn) {
+      if (!mbar_wait(full(s), (gs / S) & 1, abort_flag, kDevTimeoutTmaFull)) break;
+      const int info = sinfo[s];
+      if (info < 0) break;  // the producer ran out of row tiles
+      rt = info / p.groups;
+      c0 = info % p.groups;
+      ng = min(GPS, p.groups - c0);
+    } else {
+      rt = u / p.groups;
+      c0 = u % p.groups;
+      ng = min(min(GPS, p.groups - c0), u1 - u);
+      u += ng;
+      if (ok) ok = mbar_wait(full(s), (gs / S) & 1, abort_flag, kDevTimeoutTmaFull);
+    }
     if (ok) {
       const uint8_t* st = smem + s * p.stage_bytes;
       const uint8_t* sc = st + p.sc_off;
@@ -741,42 +787,70 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
       y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
       acc0 = acc8 = 0.f;
       const int64_t n_g = (int64_t)rt * kRows + rl;
-      const int b_first = unit_owner(rt * p.groups, p.units, gridDim.x);
-      const int b_last = unit_owner(rt * p.groups + p.groups - 1, p.units, gridDim.x);
+      const int b_first = p.dyn ? 0 : unit_owner(rt * p.groups, p.units, gridDim.x);
+      const int b_last = p.dyn ? 0 : unit_owner(rt * p.groups + p.groups - 1, p.units, gridDim.x);
       if (b_first == b_last) {  // the whole row tile is this CTA's
         if (t == 0) {
           write_out(p, 0, n_g, 0, y0);
           write_out(p, 0, n_g + 8, 0, y8);
         }
-      } else {
+      } else if (npub < 2) {  // only the first and the last piece of a CTA can be shared
         const int piece = blockIdx.x - b_first;
         float* part = p.ws + ((int64_t)rt * p.maxp + piece) * kRows;
         if (t == 0) {
           part[rl] = y0;
           part[rl + 8] = y8;
         }
-        __threadfence();
-        consumer_sync();
-        if (threadIdx.x == 0) {
-          const int prev = atomicAdd(&p.counters[rt], 1);
-          s_last = (prev == b_last - b_first);
-          if (prev > b_last - b_first) report(kDevTimeoutSplitK);
-        }
-        consumer_sync();
-        if (s_last) {
-          __threadfence();
-          if (threadIdx.x < kRows) {
-            const int64_t n = (int64_t)rt * kRows + threadIdx.x;
-            float v = sum_partials(p.ws + (int64_t)rt * p.maxp * kRows + threadIdx.x, kRows,
-                                   b_last - b_first + 1);
-            if (n < p.N) {
-              if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
-              store_from_f32(p.y, n, p.y_t, v);
-            }
-          }
-          if (threadIdx.x == 0) p.counters[rt] = 0;
+        pub_rt[npub] = rt;  // published after the loop: one fence, off the weight stream
+        pub_pieces[npub] = b_last - b_first + 1;
+        ++npub;
+      }
+    }
+  }
+
+  if (p.dyn) {
+    // The producer's last (failed) take preceded the stage that stopped the consumers, so when
+    // every CTA has counted itself here no take is left: the last one resets the counters.
+    consumer_sync();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(&p.counters[1], 1) == (int)gridDim.x - 1) {
+        p.counters[0] = 0;
+        p.counters[1] = 0;
+      }
+    }
+    return;
+  }
+
+  // Publish the shared pieces: after a consumer barrier one thread fences (making every
+  // consumer's partial stores visible) and counts the arrivals; the last CTA of a row tile sums
+  // its partials in CTA order and resets the counter.
+  if (npub > 0) {
+    consumer_sync();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      bool any = false;
+      for (int i = 0; i < npub; ++i) {
+        const int prev = atomicAdd(&p.counters[pub_rt[i]], 1);
+        s_lastv[i] = (prev == pub_pieces[i] - 1);
+        any |= s_lastv[i] != 0;
+        if (prev >= pub_pieces[i]) report(kDevTimeoutSplitK);  // a counter left non-zero earlier
+      }
+      if (any) __threadfence();
+    }
+    consumer_sync();
+    for (int i = 0; i < npub; ++i) {
+      if (!s_lastv[i]) continue;
+      const int rt = pub_rt[i];
+      if (threadIdx.x < kRows) {
+        const int64_t n = (int64_t)rt * kRows + threadIdx.x;
+        float v = sum_partials(p.ws + (int64_t)rt * p.maxp * kRows + threadIdx.x, kRows, pub_pieces[i]);
+        if (n < p.N) {
+          if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
+          store_from_f32(p.y, n, p.y_t, v);
         }
       }
+      if (threadIdx.x == 0) p.counters[rt] = 0;
     }
   }
 }
@@ -786,7 +860,7 @@ struct GemvPlan {
   int mode, ksplit, groups_per_split, ctas_n, stages, stage_bytes, sc_off, zc_off, act_off,
       seg_off, bar_off, sk, smem, items;
   // M = 1 stream-K (mode kM1)
-  int units, spr, maxp, grid, ctas_per_sm;
+  int units, spr, maxp, grid, ctas_per_sm, dyn = 0;
   int64_t ws_floats;  // split-K / stream-K partials (0: none)
 };
 
@@ -809,7 +883,7 @@ static bool plan_m1(const Weight& w, GemvPlan& pl) {
   const int kr = (int)w.groups * G;
   const int act_bytes = (kr * 2 + 15) / 16 * 16;
   const int seg_bytes = (kr / seg) * 16;
-  const int fixed = act_bytes + seg_bytes + 8 * 2 * kMaxStages + 16;
+  const int fixed = act_bytes + seg_bytes + 8 * 2 * kMaxStages + 32;
   // three CTAs per SM when three stages fit in a third of the shared memory, else two
   int stages = std::min(kMaxStages, (kSmemBudget3 - fixed) / pl.stage_bytes);
   pl.ctas_per_sm = 3;
@@ -823,7 +897,7 @@ static bool plan_m1(const Weight& w, GemvPlan& pl) {
   pl.act_off = stages * pl.stage_bytes;
   pl.seg_off = pl.act_off + act_bytes;
   pl.bar_off = pl.seg_off + seg_bytes;
-  pl.smem = pl.bar_off + 8 * 2 * kMaxStages + 16;
+  pl.smem = pl.bar_off + 8 * 2 * kMaxStages + 32;  // barriers, abort flag, stage tags
   pl.sk = kr + 16;
   pl.ctas_n = (int)(w.n_pad / kRows);
   pl.spr = (int)w.groups;
@@ -839,6 +913,14 @@ static bool plan_m1(const Weight& w, GemvPlan& pl) {
     pl.maxp = std::max(pl.maxp, pieces);
   }
   pl.ws_floats = pl.maxp > 1 ? (int64_t)pl.ctas_n * pl.maxp * kRows : 0;
+  // Many row tiles per CTA (the lm_head): whole row tiles in arrival order instead of an even
+  // static split, so the CTAs that get more memory bandwidth take more tiles and the call ends
+  // with its CTAs together; no partial sums. Uses counters[0..1].
+  pl.dyn = pl.ctas_n >= 2 * pl.grid;
+  if (pl.dyn) {
+    pl.maxp = 1;
+    pl.ws_floats = 0;
+  }
   return true;
 }
 
@@ -1066,11 +1148,14 @@ tq4_status run_gemv_with(const Weight& w, const void* a, int64_t m, tq4_dtype a_
   args.units = pl.units;
   args.spr = pl.spr;
   args.maxp = pl.maxp;
+  args.dyn = pl.dyn;
   args.n_pad = w.n_pad;
-  if (pl.ws_floats > 0) {
-    if (ws == nullptr || pl.ws_floats > ws_capacity_floats || pl.ctas_n > ctr_capacity) {
+  const int nctr = pl.dyn ? 2 : (pl.ws_floats > 0 ? pl.ctas_n : 0);
+  if (pl.ws_floats > 0 || nctr > 0) {
+    if ((pl.ws_floats > 0 && (ws == nullptr || pl.ws_floats > ws_capacity_floats)) || counters == nullptr ||
+        nctr > ctr_capacity) {
       set_error("split-K workspace too small: need %lld floats and %d counters",
-                (long long)pl.ws_floats, pl.ctas_n);
+                (long long)pl.ws_floats, nctr);
       return TQ4_ERR_INVALID_ARGUMENT;
     }
     args.ws = ws;
@@ -1095,7 +1180,12 @@ tq4_status run_gemv_with(const Weight& w, const void* a, int64_t m, tq4_dtype a_
 
 int64_t gemv_workspace_floats(const Weight& w, int64_t m) { return plan_gemv(w, m).ws_floats; }
 
-int64_t gemv_counter_count(const Weight& w, int64_t m) { return plan_gemv(w, m).ctas_n; }
+// Counters a call uses (zero-initialised, left at zero by the kernel): one per row tile for split
+// partial sums, two for the M = 1 row-tile hand-out, none otherwise.
+int64_t gemv_counter_count(const Weight& w, int64_t m) {
+  const GemvPlan pl = plan_gemv(w, m);
+  return pl.dyn ? 2 : (pl.ws_floats > 0 ? pl.ctas_n : 0);
+}
 
 tq4_status run_gemv(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,
                     tq4_dtype bias_t, void* y, tq4_dtype y_t, int64_t ldy, cudaStream_t st) {
@@ -1103,7 +1193,7 @@ tq4_status run_gemv(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, co
   int* ctr = nullptr;
   const int64_t need = gemv_workspace_floats(w, m);
   const int64_t nctr = gemv_counter_count(w, m);
-  if (need > 0) TQ4_TRY(gemv_workspace(w, st, need * 4, nctr, &ws, &ctr));
+  if (need > 0 || nctr > 0) TQ4_TRY(gemv_workspace(w, st, need * 4, nctr, &ws, &ctr));
   return run_gemv_with(w, a, m, a_t, bias, bias_t, y, y_t, ldy, st, ws, ctr, need, nctr);
 }
 

@@ -129,6 +129,10 @@ struct tq4_weight {
   tq4::DeviceBuffer q;       // [n_pad][row_bytes]
   tq4::DeviceBuffer scales;  // [blocks_pad][n_pad] in T (block-major)
   tq4::DeviceBuffer zps;     // [blocks_pad][n_pad] in T, or empty
+  // [n_pad] int32, T = f32 with 4-bit weights only: |(q - z) * s| <= 2^wexp[n] over row n. The
+  // tensor-core GEMM carries row n's weights as f16 (q - z) * s * 2^-wexp[n] (kept in the normal
+  // f16 range) and multiplies its outputs back by 2^wexp[n].
+  tq4::DeviceBuffer wexp;
   int num_sms = 148;
   // split-K workspaces of the GEMV, one per CUDA stream (a tq4::WorkspaceMap, made on first use)
   void* ws_mutex = nullptr;

@@ -101,7 +101,7 @@ extern "C" tq4_status tq4_matmul_noalloc(const tq4_weight* w, const void* a, int
   }
   const int64_t need = gemv_workspace_floats(*w, m);
   const int64_t nctr = gemv_counter_count(*w, m);
-  if (need > kNoAllocScratchFloats || (need > 0 && nctr > kNoAllocCounters)) {
+  if (need > kNoAllocScratchFloats || nctr > kNoAllocCounters) {
     set_error("tq4_matmul_noalloc: this call needs %lld bytes of split-K scratch and %lld counters; "
               "the static limit is %lld bytes and %lld counters (use tq4_matmul)",
               (long long)(need * 4), (long long)nctr, (long long)(kNoAllocScratchFloats * 4),
@@ -113,7 +113,7 @@ extern "C" tq4_status tq4_matmul_noalloc(const tq4_weight* w, const void* a, int
   float* scratch = nullptr;
   int* counters = nullptr;
   TQ4_TRY(noalloc_scratch(w->device, &scratch, &counters));
-  if (need > 0) TQ4_CUDA(cudaMemsetAsync(counters, 0, (size_t)nctr * sizeof(int), st));
+  if (nctr > 0) TQ4_CUDA(cudaMemsetAsync(counters, 0, (size_t)nctr * sizeof(int), st));
   return run_gemv_with(*w, a, m, a_t, bias, bias_t, y, y_t, w->desc.N, st, scratch, counters,
                        kNoAllocScratchFloats, kNoAllocCounters);
 }

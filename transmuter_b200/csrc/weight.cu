@@ -163,6 +163,25 @@ static void launch_unpack_zp(const Weight& w, const uint8_t* zp, T* dst, cudaStr
                                                               w.blocks, dst, w.n_pad, w.blocks_pad);
 }
 
+// Per-row bound of the f32 weights: wexp[n] with max_b |s_b| * max(|z_b|, |2^bits - 1 - z_b|) <= 2^wexp[n]
+// (frexp exponent of that maximum; 0 for an all-zero or non-finite row).
+__global__ void row_exponent_kernel(const float* __restrict__ scales, const float* __restrict__ zps, float z_const,
+                                    int64_t blocks, int64_t n, int64_t n_pad, float qmax, int32_t* __restrict__ out) {
+  const int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (r >= n_pad) return;
+  float mx = 0.f;
+  if (r < n) {
+    for (int64_t b = 0; b < blocks; ++b) {
+      const float s = fabsf(scales[b * n_pad + r]);
+      const float z = zps ? zps[b * n_pad + r] : z_const;
+      mx = fmaxf(mx, s * fmaxf(fabsf(z), fabsf(qmax - z)));
+    }
+  }
+  int e = 0;
+  if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);
+  out[r] = e;
+}
+
 tq4_status prepare_weight(Weight& w, const void* b_src, const void* s_src, const void* zp_src) {
   const tq4_weight_desc& d = w.desc;
   cudaStream_t st = w.stream;
@@ -210,6 +229,13 @@ tq4_status prepare_weight(Weight& w, const void* b_src, const void* s_src, const
       break;
   }
   TQ4_CUDA(cudaGetLastError());
+  if (d.dequant_dtype == TQ4_F32 && d.bits == 4) {
+    TQ4_TRY(w.wexp.alloc(w.n_pad * 4));
+    row_exponent_kernel<<<grid_for(w.n_pad, 256), 256, 0, st>>>(
+        static_cast<const float*>(w.scales.ptr), static_cast<const float*>(w.zps.ptr), w.z_const, w.blocks,
+        d.N, w.n_pad, 15.f, static_cast<int32_t*>(w.wexp.ptr));
+    TQ4_CUDA(cudaGetLastError());
+  }
   // The staging buffers are freed when this function returns; finish the kernels first.
   TQ4_CUDA(cudaStreamSynchronize(st));
   return TQ4_OK;
