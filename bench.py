@@ -225,7 +225,8 @@ def main():
         obj = [uid]
         dist.broadcast_object_list(obj, src=0)
         comm = shd.Comm(obj[0], world, rank, local_rank, timeout_ms=120000)
-        config["parallelism"] = f"N-sharded over {world} GPUs + NCCL all-gather"
+        config["parallelism"] = (f"N-sharded over {world} GPUs; Y assembled by NVLink peer loads "
+                                 f"(slices >= 4 MB) or NCCL all-gather")
     else:
         config["parallelism"] = "single GPU" if world == 1 else f"{world} independent replicas (dp{world})"
     weights, acts, outs = [], [], []

@@ -2,8 +2,9 @@
 torch.distributed.run, one process per GPU).
 
 Every rank builds the same seeded weights, takes its rows through tq4_sharded_create, runs
-tq4_sharded_matmul (its GEMV / GEMM, then the NCCL all-gather and, for M > 1, the unshard
-kernel) and compares the full Y with the unsharded handle on its own GPU. The columns come from
+tq4_sharded_matmul twice in a row on different inputs (its GEMV / GEMM, then the assembly of Y:
+NCCL's all-gather for small outputs, the NVLink peer exchange for slices of 4 MB and more) and
+compares the full Y with the unsharded handle on its own GPU. The columns come from
 the same kernels over the same rows, so they agree to within the split-K summation order
 (rel-L2 1e-6 for f32 outputs; 1e-4 for f16 outputs, where that order can move a value by one
 f16 ulp); the unsharded result is itself pinned to the oracle by the parity tests.
@@ -31,6 +32,9 @@ CASES = [  # (K, N, M, zero points, A type, scale type)
     (4096, 14336, 1, "packed", "f16", "f16"),
     (1024, 4000, 64, "packed", "f16", "f16"),
     (4096, 1024, 256, "packed", "f16", "f16"),
+    # slices of 4 MB and more per rank: the NVLink peer exchange instead of NCCL's all-gather
+    (4096, 14336, 512, "packed", "f16", "f16"),
+    (1024, 151936, 16, "none", "f32", "f32"),
 ]
 TT = {"f32": torch.float32, "f16": torch.float16}
 
@@ -54,10 +58,12 @@ def main():
         a = torch.from_numpy(np.ascontiguousarray(p["A"])).to(dev)
         sw = sharded.ShardedWeight(comm, (k, n, 4, bs), b, s, z, dtype=TT[st])
         pw = PackedWeight((k, n, 4, bs), b, s, z, dtype=TT[st], device=dev)
-        y_sh = sw.matmul(a)
-        y_ref = pw.matmul(a)
+        a2 = torch.flip(a, dims=[1]).contiguous()  # a second call in a row, on new inputs
+        y_sh, y_sh2 = sw.matmul(a), sw.matmul(a2)
+        y_ref, y_ref2 = pw.matmul(a), pw.matmul(a2)
         torch.cuda.synchronize()
-        err = o.rel_l2(y_sh.double().cpu().numpy(), y_ref.double().cpu().numpy())
+        err = max(o.rel_l2(y_sh.double().cpu().numpy(), y_ref.double().cpu().numpy()),
+                  o.rel_l2(y_sh2.double().cpu().numpy(), y_ref2.double().cpu().numpy()))
         worst.append((cfg.name, err, 1e-6 if at == "f32" else 1e-4))
         sw.close()
         pw.close()

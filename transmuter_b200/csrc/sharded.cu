@@ -1,7 +1,18 @@
-// N-sharded MatMulNBits over NCCL: each rank holds rows [first, first+count) of B, scales and
-// zero points, computes its columns of Y, and an all-gather over NVLink assembles Y on every
-// rank. The reference has no device collective; this serves the very wide projections (the
-// 151936-column lm_head) named by the north star.
+// N-sharded MatMulNBits: each rank holds rows [first, first+count) of B, scales and zero points,
+// computes its columns of Y, and Y is assembled on every rank over NVLink. The reference has no
+// device collective; this serves the very wide projections (the 151936-column lm_head) named by
+// the north star.
+//
+// Assembly of large outputs (a slice of 4 MB or more): each rank computes its slice into a
+// buffer that every peer has mapped (CUDA IPC handles, exchanged once through NCCL). One exchange
+// kernel then, with e this call's epoch (a device counter, so graph replays advance it): (1)
+// stores e into every rank's "ready" flags (release, system scope); (2) waits, bounded, until all
+// ranks' ready flags carry e; (3) loads every rank's slice over NVLink straight into Y's [M][N]
+// layout; (4) in its last block stores e into every rank's "read" flags and waits until every
+// rank has read this rank's slice, so the next call's compute never overwrites a slice that a
+// peer is still reading. Small outputs, where NCCL's latency measured lower, and hosts where
+// peer mapping is not available on every rank use NCCL's all-gather (plus a reordering kernel
+// for M > 1).
 //
 // NCCL is loaded with dlopen at first use, so the library loads on hosts without NCCL and links
 // to whichever libnccl.so.2 the process already has (torch's, when torch is imported first).
@@ -97,6 +108,96 @@ static ncclDataType_t nccl_type(tq4_dtype t) {
   }
 }
 
+constexpr int kMaxPeers = 8;
+constexpr long long kPeerWaitCycles = 2000000000LL;  // about one second
+
+// Flag words of a rank: ready[kMaxPeers], read[kMaxPeers], then the block counter and the epoch.
+constexpr int kFlagReady = 0, kFlagRead = kMaxPeers, kFlagCounter = 2 * kMaxPeers, kFlagEpoch = 2 * kMaxPeers + 1;
+constexpr int kFlagWords = 2 * kMaxPeers + 2;
+constexpr int64_t kPeerMinSlice = 4 << 20;  // bytes per rank below which NCCL assembles Y
+
+struct PeerArgs {
+  const uint8_t* slice[kMaxPeers];       // rank q's [M][share] slice (own or peer-mapped)
+  unsigned long long* flags[kMaxPeers];  // rank q's flag words (own or peer-mapped)
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until flags[base + q] >= epoch for every rank q; false (and the device status) on
+// timeout.
+__device__ __forceinline__ bool wait_flags(const unsigned long long* flags, int base, int nranks,
+                                           unsigned long long epoch) {
+  const long long t0 = clock64();
+  for (int q = 0; q < nranks; ++q) {
+    while (ld_acquire_sys(flags + base + q) < epoch) {
+      if (clock64() - t0 > kPeerWaitCycles) {
+        report(kDevTimeoutPeer);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// Publish this rank's slice, wait for every rank's, gather Y [M][N] (16-byte chunks where
+// aligned); see the top of this file.
+constexpr int kExThreads = 256;
+
+// See the top of this file.
+__global__ void __launch_bounds__(kExThreads) exchange_kernel(PeerArgs pa, unsigned long long* own, int rank,
+                                                              int nranks, int64_t m, int64_t share, int64_t n, int ys,
+                                                              uint8_t* y) {
+  __shared__ int s_ok;
+  const unsigned long long epoch = *reinterpret_cast<volatile unsigned long long*>(own + kFlagEpoch) + 1;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) {
+      __threadfence_system();  // the slice (written by the previous kernel) before the flag
+      for (int q = 0; q < nranks; ++q) st_release_sys(pa.flags[q] + kFlagReady + rank, epoch);
+    }
+    s_ok = wait_flags(own, kFlagReady, nranks, epoch);
+  }
+  __syncthreads();
+  if (s_ok) {
+    const int64_t row_bytes = share * ys;       // a multiple of 32
+    const int64_t chunks_row = row_bytes / 16;  // per slice row
+    const int64_t total = m * nranks * chunks_row;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t c = i % chunks_row, rq = i / chunks_row;
+      const int q = (int)(rq % nranks);
+      const int64_t row = rq / nranks;
+      const int64_t col0 = q * share + c * (16 / ys);  // first Y column of the chunk
+      if (col0 >= n) continue;
+      const uint8_t* src = pa.slice[q] + row * row_bytes + c * 16;
+      uint8_t* dst = y + (row * n + col0) * ys;
+      if (col0 + 16 / ys <= n && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+      } else {
+        for (int e = 0; e < 16 / ys && col0 + e < n; ++e)
+          for (int b = 0; b < ys; ++b) dst[e * ys + b] = src[e * ys + b];
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    unsigned int* counter = reinterpret_cast<unsigned int*>(own + kFlagCounter);
+    if (atomicAdd(counter, 1u) == gridDim.x - 1) {  // the last block: this rank read every slice
+      *counter = 0;
+      __threadfence_system();
+      for (int q = 0; q < nranks; ++q) st_release_sys(pa.flags[q] + kFlagRead + rank, epoch);
+      wait_flags(own, kFlagRead, nranks, epoch);  // every rank has read this rank's slice
+      *reinterpret_cast<volatile unsigned long long*>(own + kFlagEpoch) = epoch;
+    }
+  }
+}
+
 // [P][M][share] (the all-gather order) -> Y [M][N]
 template <typename T>
 __global__ void unshard_kernel(const T* __restrict__ g, int64_t m, int64_t share, int nranks,
@@ -127,9 +228,118 @@ struct tq4_sharded {
   int64_t share = 0;            // rows per rank (a multiple of 16), the all-gather unit
   int64_t first = 0, count = 0;
   std::mutex mu;
-  DeviceBuffer part;    // this rank's [M][share] output
-  DeviceBuffer gather;  // [P][M][share]
+  DeviceBuffer part;    // this rank's [M][share] output (NCCL path)
+  DeviceBuffer gather;  // [P][M][share] (NCCL path)
+  // peer exchange
+  bool peer_tried = false, peer_ok = false;
+  int64_t peer_cap = 0;              // bytes of the slice buffer
+  DeviceBuffer slice, flags;         // this rank's [M][share] slice and its flag words
+  void* peer_slice[kMaxPeers] = {};  // mapped peer buffers (own entries point at our own)
+  void* peer_flags[kMaxPeers] = {};
 };
+
+namespace tq4 {
+
+static void close_peers(tq4_sharded* s) {
+  for (int q = 0; q < s->comm->nranks && q < kMaxPeers; ++q) {
+    if (q == s->comm->rank) continue;
+    if (s->peer_slice[q]) cudaIpcCloseMemHandle(s->peer_slice[q]);
+    if (s->peer_flags[q]) cudaIpcCloseMemHandle(s->peer_flags[q]);
+  }
+  for (int q = 0; q < kMaxPeers; ++q) s->peer_slice[q] = s->peer_flags[q] = nullptr;
+  s->peer_ok = false;
+}
+
+// Collective (every rank, same call): slice buffers of at least `bytes`, their IPC handles
+// exchanged, the peers' buffers mapped. Sets peer_ok only when every rank mapped every peer.
+static tq4_status peer_setup(tq4_sharded* s, NcclApi* api, int64_t bytes, cudaStream_t st) {
+  const int P = s->comm->nranks, R = s->comm->rank;
+  if (s->peer_tried && (!s->peer_ok || s->peer_cap >= bytes)) return TQ4_OK;
+  if (P > kMaxPeers) {
+    s->peer_tried = true;
+    return TQ4_OK;
+  }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  TQ4_CUDA(cudaStreamIsCapturing(st, &cs));
+  if (cs != cudaStreamCaptureStatusNone) {
+    set_error("tq4_sharded_matmul: the first call with a larger M must come before stream capture");
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  TQ4_CUDA(cudaStreamSynchronize(st));
+  if (s->peer_tried) {  // growing: every rank is here too (the same collective call)
+    close_peers(s);
+    TQ4_CUDA(cudaDeviceSynchronize());
+  }
+  s->peer_tried = true;
+  const int64_t cap = (bytes + (2 << 20) - 1) / (2 << 20) * (2 << 20);
+  TQ4_TRY(s->slice.alloc(cap));
+  if (!s->flags.ptr) {  // the epochs only grow: the flag words outlive a slice regrowth
+    TQ4_TRY(s->flags.alloc(kFlagWords * sizeof(unsigned long long)));
+    TQ4_CUDA(cudaMemset(s->flags.ptr, 0, kFlagWords * sizeof(unsigned long long)));
+  }
+  // handles of the slice and the flag words; then one byte: did every open succeed
+  struct Handles {
+    cudaIpcMemHandle_t h[2];
+  } mine{};
+  bool ok = cudaIpcGetMemHandle(&mine.h[0], s->slice.ptr) == cudaSuccess &&
+            cudaIpcGetMemHandle(&mine.h[1], s->flags.ptr) == cudaSuccess;
+  cudaGetLastError();
+  DeviceBuffer xbuf;
+  TQ4_TRY(xbuf.alloc((int64_t)(P + 1) * sizeof(Handles) + 2 * P));
+  uint8_t* dbuf = static_cast<uint8_t*>(xbuf.ptr);
+  TQ4_CUDA(cudaMemcpy(dbuf + P * sizeof(Handles), &mine, sizeof(Handles), cudaMemcpyHostToDevice));
+  ncclResult_t r = api->AllGather(dbuf + P * sizeof(Handles), dbuf, sizeof(Handles), ncclUint8, s->comm->comm, st);
+  if (r == ncclInProgress) {
+    TQ4_TRY(nccl_wait(api, s->comm->comm, std::chrono::steady_clock::now() + std::chrono::seconds(60), "ncclAllGather"));
+  } else if (r != ncclSuccess) {
+    set_error("ncclAllGather: %s", api->GetErrorString(r));
+    return TQ4_ERR_NCCL;
+  }
+  TQ4_CUDA(cudaStreamSynchronize(st));
+  Handles all[kMaxPeers];
+  TQ4_CUDA(cudaMemcpy(all, dbuf, P * sizeof(Handles), cudaMemcpyDeviceToHost));
+  for (int q = 0; q < P; ++q) {
+    if (q == R) {
+      s->peer_slice[q] = s->slice.ptr;
+      s->peer_flags[q] = s->flags.ptr;
+      continue;
+    }
+    for (int k = 0; k < 2 && ok; ++k) {
+      void* ptr = nullptr;
+      if (cudaIpcOpenMemHandle(&ptr, all[q].h[k], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        ok = false;
+        break;
+      }
+      if (k == 0) s->peer_slice[q] = ptr;
+      else s->peer_flags[q] = ptr;
+    }
+  }
+  // agree: peer exchange only if every rank mapped every peer
+  const uint8_t mine_ok = ok ? 1 : 0;
+  TQ4_CUDA(cudaMemcpy(dbuf + P * sizeof(Handles) + P, &mine_ok, 1, cudaMemcpyHostToDevice));
+  r = api->AllGather(dbuf + P * sizeof(Handles) + P, dbuf + P * sizeof(Handles), 1, ncclUint8, s->comm->comm, st);
+  if (r == ncclInProgress) {
+    TQ4_TRY(nccl_wait(api, s->comm->comm, std::chrono::steady_clock::now() + std::chrono::seconds(60), "ncclAllGather"));
+  } else if (r != ncclSuccess) {
+    set_error("ncclAllGather: %s", api->GetErrorString(r));
+    return TQ4_ERR_NCCL;
+  }
+  TQ4_CUDA(cudaStreamSynchronize(st));
+  uint8_t oks[kMaxPeers];
+  TQ4_CUDA(cudaMemcpy(oks, dbuf + P * sizeof(Handles), P, cudaMemcpyDeviceToHost));
+  bool all_ok = true;
+  for (int q = 0; q < P; ++q) all_ok = all_ok && oks[q];
+  if (!all_ok) {
+    close_peers(s);
+    return TQ4_OK;
+  }
+  s->peer_ok = true;
+  s->peer_cap = cap;
+  return TQ4_OK;
+}
+
+}  // namespace tq4
 
 extern "C" {
 
@@ -268,6 +478,37 @@ tq4_status tq4_sharded_matmul(const tq4_sharded* cs, const void* a, int64_t m, t
   const int ys = dtype_size(y_t);
   std::lock_guard<std::mutex> lock(s->mu);
   TQ4_CUDA(cudaSetDevice(s->comm->device));
+  const bool large = m * s->share * ys >= kPeerMinSlice;
+  if (large) TQ4_TRY(peer_setup(s, api, m * s->share * ys, st));
+  if (large && s->peer_ok) {
+    if (s->local) {
+      const void* lb = bias ? static_cast<const uint8_t*>(bias) + s->first * dtype_size(bias_t) : nullptr;
+      TQ4_TRY(run_matmul(*s->local, a, m, a_t, lb, bias_t, s->slice.ptr, y_t, s->share, st));
+    }
+    PeerArgs pa{};
+    for (int q = 0; q < P; ++q) {
+      pa.slice[q] = static_cast<const uint8_t*>(s->peer_slice[q]);
+      pa.flags[q] = static_cast<unsigned long long*>(s->peer_flags[q]);
+    }
+    const int64_t chunks = m * P * (s->share * ys / 16);
+    // Every block waits for the last one's signal, so the grid must be resident all at once: no
+    // more blocks than the SMs hold together (occupancy of this kernel, looked up once per device).
+    static int resident[64] = {0};
+    int dev = s->comm->device;
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (resident[dev] == 0) {
+      int per_sm = 0, sms = 0;
+      TQ4_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, exchange_kernel, kExThreads, 0));
+      TQ4_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, s->comm->device));
+      resident[dev] = std::max(1, per_sm * sms);
+    }
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((chunks + kExThreads - 1) / kExThreads,
+                                                                  std::min(resident[dev], 4 * 148)));
+    exchange_kernel<<<grid, kExThreads, 0, st>>>(pa, static_cast<unsigned long long*>(s->flags.ptr), s->comm->rank,
+                                                 (int)P, m, s->share, s->desc.N, ys, static_cast<uint8_t*>(y));
+    TQ4_CUDA(cudaGetLastError());
+    return TQ4_OK;
+  }
   // Y itself is the gather target when it already has the [P][1][share] layout.
   const bool direct = (m == 1 && s->share * P == s->desc.N);
   if (s->part.bytes < m * s->share * ys) TQ4_TRY(s->part.alloc(m * s->share * ys));
@@ -307,6 +548,11 @@ tq4_status tq4_sharded_matmul(const tq4_sharded* cs, const void* a, int64_t m, t
 tq4_status tq4_sharded_destroy(tq4_sharded* s) {
   if (!s) return TQ4_OK;
   if (s->local) tq4_weight_destroy(s->local);
+  if (s->peer_tried) {
+    cudaSetDevice(s->comm->device);
+    cudaDeviceSynchronize();
+    close_peers(s);
+  }
   s->part.release();
   s->gather.release();
   delete s;
