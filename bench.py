@@ -5,8 +5,8 @@
 A step is one MatMulNBits call (one pass of the hot path over one batch of activations). The
 default workload is the prefill-shaped config (C2: A f16 [512, 1024], K=1024, N=3072, 4-bit,
 block 32, f16 scales, packed zero points; metric TFLOP/s). Other workloads: c1 (decode, M=1,
-GB/s), c3m1 / c3m64 (151936-column lm_head, GB/s; N-sharded with an NCCL all-gather when run
-on several GPUs), c5-<K>x<N>-m<M> (Llama-3-8B shapes).
+GB/s), c3m1 / c3m64 (151936-column lm_head, GB/s; N-sharded when run on several GPUs, Y
+assembled over NVLink), c5-<K>x<N>-m<M> (Llama-3-8B shapes), c4 (the q4 decoder, tok/s).
 
 Timing: W untimed warm-up steps, then exactly K steps between barriers and synchronizes, timed
 with CUDA events on the launching stream; max over ranks. Consecutive steps rotate over R
@@ -152,9 +152,19 @@ def cpu_reference(cfg, p, steps, warmup, budget_s):
 
 # ---- our path --------------------------------------------------------------------------------
 def launches_per_call(cfg, m, sharded_world=1):
-    n = 1 if m <= 16 else -(-m // 16)
-    if sharded_world > 1 and not (m == 1 and cfg.n % (16 * sharded_world) == 0):
-        n += 1  # the unshard kernel after the all-gather
+    """libtq4 kernels per call (NCCL's own kernels are not counted)."""
+    if m <= 16:
+        n = 1                                   # the GEMV
+    elif cfg.bits == 4:
+        n = 2 if cfg.a_type == "f32" else 1     # (row-scaled f16 copy of A) + the tcgen05 GEMM
+    else:
+        n = -(-m // 16)                         # GEMV slices of 16 rows
+    if sharded_world > 1:
+        share = (-(-cfg.n // sharded_world) + 15) // 16 * 16
+        if m * share * (4 if cfg.a_type == "f32" else 2) >= 4 << 20:
+            n += 1                              # the NVLink exchange kernel
+        elif not (m == 1 and cfg.n % (16 * sharded_world) == 0):
+            n += 1                              # the reordering kernel after NCCL's all-gather
     return n
 
 
@@ -329,12 +339,12 @@ def main():
         ms_e2e = t.item()
     e2e_value = metric_value(cfg, ms_e2e / 1e3 / e2e_steps) * units
 
-    # roofline of the dominant kernel (the MatMulNBits kernel is the whole step)
+    # roofline of the dominant kernel (the MatMulNBits kernel is the whole step; with N-sharding
+    # each GPU's kernel does 1/world of the work within the step)
     pk, pk_kind = peaks()
     launches = launches_per_call(cfg, cfg.m, world if sharded_run else 1)
-    main_launches = 1 if cfg.m <= 16 else -(-cfg.m // 16)
     if cfg.metric == "TFLOP/s":
-        achieved = cfg.flops() / main_launches / (sec_per_call / main_launches) / 1e12
+        achieved = cfg.flops() / (world if sharded_run else 1) / sec_per_call / 1e12
         peak = pk["bf16_tflops"]
         bound, unit = "tensor", "TFLOP/s"
     else:
