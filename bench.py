@@ -525,7 +525,7 @@ def decoder_bench(args, rank, world, local_rank):
     pk, pk_kind = peaks()
     step_bytes = np.mean([decoder_bytes_per_token(cfg, DECODE_PROMPT - 1 + i) for i in range(steps)])
     achieved = step_bytes / (ms / 1e3 / steps) / 1e9
-    launches = cfg.layers * 9 + 4
+    launches = cfg.layers * Q4Decoder.LAUNCHES_PER_LAYER + Q4Decoder.LAUNCHES_PER_STEP_EXTRA
     if rank == 0:
         config["l2"] = "inputs larger than L2 (about 372 MB of weights read per token, L2 126 MB)"
         config["prefill"] = {"tok_per_s": (DECODE_PROMPT - 1) / (ms_prefill / 1e3) * world,

@@ -39,6 +39,28 @@ tq4_status tq4_attention_decode(const float* q, const float* k_new, const float*
                                 float* k_cache, float* v_cache, const int32_t* pos, float* out,
                                 int heads, int kv_heads, int head_dim, int max_len, void* stream);
 
+/* tq4_attention_decode with Qwen3's per-head RMSNorm (weights q_w / k_w over head_dim, eps) and
+ * rotate-half RoPE at *pos (cos/sin tables [max_len][head_dim/2]) applied to q and k_new first,
+ * as tq4_qk_norm_rope would: the normalised, rotated key is the one written into the cache.
+ * q and k_new are read, not modified. */
+tq4_status tq4_attention_decode_rope(const float* q, const float* k_new, const float* v_new,
+                                     const float* q_w, const float* k_w, const float* cos_table,
+                                     const float* sin_table, float eps, float* k_cache,
+                                     float* v_cache, const int32_t* pos, float* out, int heads,
+                                     int kv_heads, int head_dim, int max_len, void* stream);
+
+/* A decode-step projection through a MatMulNBits handle (M = 1, f32 in and out; the handle's
+ * weight 4-bit with block_size <= 128):
+ *   y[n] = residual[n] + (W . a)[n],  a = prologue(x)
+ * prologue 0: a = x; 1: a = RMSNorm(x) = x * rsqrt(mean(x^2) + eps) * norm_w
+ * (SkipSimplifiedLayerNormalization / rms_norm/4, transformer.ex:290-300,1056-1069); 2: SwiGLU,
+ * a = silu(x) * x2 (x and x2 of K values each). residual may be NULL, or equal to y (the
+ * decoder's residual stream updated in place). The prologue runs while the GEMV stages its
+ * activations, so the normalised row is never written to memory. */
+tq4_status tq4_matmul_fused(const tq4_weight* w, const float* x, const float* x2,
+                            const float* norm_w, float eps, int prologue, const float* residual,
+                            float* y, void* stream);
+
 /* SwiGLU: out[i] = silu(gate[i]) * up[i], silu(x) = x / (1 + exp(-x)). */
 tq4_status tq4_silu_mul(const float* gate, const float* up, float* out, int64_t n, void* stream);
 

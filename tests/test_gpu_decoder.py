@@ -176,3 +176,85 @@ def test_full_size_decoder_matches_torch_fp32():
         assert o.rel_l2(got[i], ref_logits[i]) < LOGIT_TOL, i
     n = len(prompt)
     assert np.array_equal(dec.log[n:n + 3].cpu().numpy(), ref_tokens)
+
+
+def _fused(lib):
+    fn = lib.tq4_matmul_fused
+    fn.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_float, ctypes.c_int] + [ctypes.c_void_p] * 3
+    return fn
+
+
+@pytest.mark.parametrize("prologue", [0, 1, 2])
+@pytest.mark.parametrize("residual", [False, True])
+@pytest.mark.parametrize("k,n", [(1024, 4096), (3072, 1024), (1024, 151936)])
+def test_matmul_fused_matches_unfused(prologue, residual, k, n):
+    """tq4_matmul_fused against the same steps done separately (torch fp64 over the handle's
+    bit-exact dequantized weight): RMSNorm / SwiGLU prologue, residual epilogue in place."""
+    lib = _lib.load()
+    dev = torch.device("cuda:0")
+    g = torch.Generator().manual_seed(k + n + 7 * prologue)
+    from transmuter_b200.quantized import PackedWeight
+    blocks = k // 32
+    b = torch.randint(0, 256, (n, blocks, 16), dtype=torch.uint8, generator=g)
+    s = torch.rand(n * blocks, generator=g) * 0.015 + 0.005
+    w = PackedWeight((k, n, 4, 32), b.to(dev), s.to(dev), None, dtype=torch.float32, device=dev)
+    x = torch.randn(k, generator=g).to(dev)
+    x2 = torch.randn(k, generator=g).to(dev)
+    nw = (torch.rand(k, generator=g) + 0.5).to(dev)
+    y = torch.randn(n, generator=g).to(dev)
+    y0 = y.clone()
+    vp = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
+    _lib.check(_fused(lib)(w._handle, vp(x), vp(x2), vp(nw), 1e-6, prologue, vp(y) if residual else None, vp(y),
+                           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    xd = x.double()
+    if prologue == 1:
+        a = xd * torch.rsqrt((xd * xd).mean() + 1e-6) * nw.double()
+    elif prologue == 2:
+        a = xd / (1 + torch.exp(-xd)) * x2.double()
+    else:
+        a = xd
+    want = w.dequantize().double() @ a + (y0.double() if residual else 0)
+    assert ((y.double() - want).norm() / want.norm()).item() < 1e-3
+    w.close()
+
+
+@pytest.mark.parametrize("pos", [0, 5, 31, 32, 200])
+def test_attention_decode_rope_matches_separate_steps(pos):
+    """tq4_attention_decode_rope equals tq4_qk_norm_rope followed by tq4_attention_decode, and
+    leaves q / k_new unmodified."""
+    lib = _lib.load()
+    dev = torch.device("cuda:0")
+    heads, kv_heads, hd, max_len = 16, 8, 128, 257
+    cfg = DecoderConfig(heads=heads, kv_heads=kv_heads, head_dim=hd, max_len=max_len)
+    cos, sin = (torch.from_numpy(t).to(dev) for t in rope_tables(cfg))
+    g = torch.Generator().manual_seed(pos + 3)
+    q = torch.randn(heads, hd, generator=g).to(dev)
+    k = torch.randn(kv_heads, hd, generator=g).to(dev)
+    v = torch.randn(kv_heads, hd, generator=g).to(dev)
+    qw = (torch.rand(hd, generator=g) + 0.5).to(dev)
+    kw = (torch.rand(hd, generator=g) + 0.5).to(dev)
+    kc = torch.randn(kv_heads, max_len, hd, generator=g).to(dev)
+    vc = torch.randn(kv_heads, max_len, hd, generator=g).to(dev)
+    p = torch.tensor([pos], dtype=torch.int32, device=dev)
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    fr = lib.tq4_attention_decode_rope
+    fr.argtypes = [ctypes.c_void_p] * 7 + [ctypes.c_float] + [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    out1, kc1, vc1 = torch.empty(heads, hd, device=dev), kc.clone(), vc.clone()
+    q0, k0 = q.clone(), k.clone()
+    _lib.check(fr(vp(q), vp(k), vp(v), vp(qw), vp(kw), vp(cos), vp(sin), 1e-6, vp(kc1), vp(vc1), vp(p), vp(out1),
+                  heads, kv_heads, hd, max_len, st))
+    torch.cuda.synchronize()
+    assert torch.equal(q, q0) and torch.equal(k, k0)
+    fq = lib.tq4_qk_norm_rope
+    fq.argtypes = [ctypes.c_void_p] * 7 + [ctypes.c_int] * 4 + [ctypes.c_float, ctypes.c_void_p]
+    fa = lib.tq4_attention_decode
+    fa.argtypes = [ctypes.c_void_p] * 7 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    q2, k2, out2, kc2, vc2 = q.clone(), k.clone(), torch.empty(heads, hd, device=dev), kc.clone(), vc.clone()
+    _lib.check(fq(vp(q2), vp(k2), vp(qw), vp(kw), vp(cos), vp(sin), vp(p), max_len, heads, kv_heads, hd, 1e-6, st))
+    _lib.check(fa(vp(q2), vp(k2), vp(v), vp(kc2), vp(vc2), vp(p), vp(out2), heads, kv_heads, hd, max_len, st))
+    torch.cuda.synchronize()
+    assert o.rel_l2(out1.double().cpu().numpy(), out2.double().cpu().numpy()) < 1e-5
+    assert o.rel_l2(kc1[:, pos].double().cpu().numpy(), kc2[:, pos].double().cpu().numpy()) < 1e-6
+    assert torch.equal(vc1, vc2)

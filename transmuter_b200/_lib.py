@@ -26,7 +26,8 @@ EXPORTS = [
     "tq4_status_string", "tq4_comm_unique_id", "tq4_comm_create", "tq4_comm_destroy",
     "tq4_sharded_create", "tq4_sharded_rows", "tq4_sharded_matmul", "tq4_sharded_destroy",
     # include/tq4_decoder.h
-    "tq4_add_rmsnorm", "tq4_qk_norm_rope", "tq4_attention_decode", "tq4_silu_mul", "tq4_argmax_advance",
+    "tq4_add_rmsnorm", "tq4_qk_norm_rope", "tq4_attention_decode", "tq4_attention_decode_rope",
+    "tq4_matmul_fused", "tq4_silu_mul", "tq4_argmax_advance",
 ]
 
 

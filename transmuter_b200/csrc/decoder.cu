@@ -10,6 +10,9 @@
 
 namespace tq4 {
 
+tq4_status run_gemv_fused(const Weight& w, const float* x, const float* x2, const float* norm_w, float eps,
+                          int mode, const float* residual, float* y, cudaStream_t st);
+
 // Deterministic block sum (fixed shuffle tree, then warp order).
 template <int THREADS>
 __device__ __forceinline__ float block_sum(float v, float* red) {
@@ -135,7 +138,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
     const float* __restrict__ q, const float* __restrict__ k_new, const float* __restrict__ v_new,
     float* __restrict__ k_cache, float* __restrict__ v_cache, const int32_t* __restrict__ pos,
     float* __restrict__ out, int heads, int kv_heads, int head_dim, int max_len, float scale,
-    float* __restrict__ part, int* __restrict__ counters, int chunks_max) {
+    float* __restrict__ part, int* __restrict__ counters, int chunks_max, const float* __restrict__ q_w,
+    const float* __restrict__ k_w, const float* __restrict__ cos_t, const float* __restrict__ sin_t, float eps) {
   pdl_wait();
   pdl_trigger();
   __shared__ float qs[kAttnMaxGroup * kAttnMaxDim];
@@ -173,9 +177,40 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
     reinterpret_cast<float4*>(vs)[i] = vr[d4];
   }
   for (int i = threadIdx.x; i < G * head_dim; i += kAttnThreads) qs[i] = q[(int64_t)kvh * G * D + i];
+  __syncthreads();
+  float* knew_s = has_new ? ks + (L - 1 - p0) * D : nullptr;  // the new key's staged row
+  if (q_w) {
+    // Qwen3's per-head RMSNorm then rotate-half RoPE at position L - 1 (rms_norm/4,
+    // transformer.ex:1056-1069; rotate/4, :558-590), on the query heads and the new key.
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rows = G + (has_new ? 1 : 0);
+    for (int r = warp; r < rows; r += kAttnThreads / 32) {
+      float* v = r < G ? qs + r * D : knew_s;
+      const float* w = r < G ? q_w : k_w;
+      float ss = 0.f;
+      for (int d = lane; d < head_dim; d += 32) ss = fmaf(v[d], v[d], ss);
+      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      const float inv = 1.f / sqrtf(ss / (float)head_dim + eps);
+      __syncwarp();
+      for (int d = lane; d < head_dim; d += 32) v[d] = v[d] * inv * w[d];
+    }
+    __syncthreads();
+    const int half = head_dim / 2;
+    const float* cr = cos_t + (int64_t)(L - 1) * half;
+    const float* sr = sin_t + (int64_t)(L - 1) * half;
+    for (int i = threadIdx.x; i < rows * half; i += kAttnThreads) {
+      const int r = i / half, j = i % half;
+      float* v = r < G ? qs + r * D : knew_s;
+      const float c = cr[j], sn = sr[j];
+      const float x1 = v[j], x2 = v[j + half];
+      v[j] = x1 * c - x2 * sn;
+      v[j + half] = x2 * c + x1 * sn;
+    }
+    __syncthreads();
+  }
   if (has_new)
     for (int d = threadIdx.x; d < head_dim; d += kAttnThreads) {
-      kc[(int64_t)(L - 1) * D + d] = kn[d];
+      kc[(int64_t)(L - 1) * D + d] = knew_s[d];
       vc[(int64_t)(L - 1) * D + d] = vn[d];
     }
   __syncthreads();
@@ -394,10 +429,60 @@ tq4_status tq4_qk_norm_rope(float* q, float* k, const float* q_w, const float* k
   return TQ4_OK;
 }
 
+namespace {
+struct RopeArgs {
+  const float* q_w = nullptr;
+  const float* k_w = nullptr;
+  const float* cos_t = nullptr;
+  const float* sin_t = nullptr;
+  float eps = 0.f;
+};
+tq4_status attention_impl(const float* q, const float* k_new, const float* v_new, float* k_cache, float* v_cache,
+                          const int32_t* pos, float* out, int heads, int kv_heads, int head_dim, int max_len,
+                          void* stream, const RopeArgs& rope);
+}  // namespace
+
 tq4_status tq4_attention_decode(const float* q, const float* k_new, const float* v_new,
                                 float* k_cache, float* v_cache, const int32_t* pos, float* out,
                                 int heads, int kv_heads, int head_dim, int max_len, void* stream) {
   clear_error();
+  return attention_impl(q, k_new, v_new, k_cache, v_cache, pos, out, heads, kv_heads, head_dim, max_len, stream,
+                        RopeArgs{});
+}
+
+tq4_status tq4_attention_decode_rope(const float* q, const float* k_new, const float* v_new, const float* q_w,
+                                     const float* k_w, const float* cos_table, const float* sin_table, float eps,
+                                     float* k_cache, float* v_cache, const int32_t* pos, float* out, int heads,
+                                     int kv_heads, int head_dim, int max_len, void* stream) {
+  clear_error();
+  if (!q_w || !k_w || !cos_table || !sin_table || (head_dim & 1)) {
+    set_error("tq4_attention_decode_rope: null norm weight / table, or odd head_dim");
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  RopeArgs r;
+  r.q_w = q_w;
+  r.k_w = k_w;
+  r.cos_t = cos_table;
+  r.sin_t = sin_table;
+  r.eps = eps;
+  return attention_impl(q, k_new, v_new, k_cache, v_cache, pos, out, heads, kv_heads, head_dim, max_len, stream, r);
+}
+
+tq4_status tq4_matmul_fused(const tq4_weight* w, const float* x, const float* x2, const float* norm_w, float eps,
+                            int prologue, const float* residual, float* y, void* stream) {
+  clear_error();
+  if (!w || !x || !y || prologue < 0 || prologue > 2 || (prologue == 1 && !norm_w) || (prologue == 2 && !x2)) {
+    set_error("tq4_matmul_fused: bad arguments (RMSNorm needs norm_w, SwiGLU needs x2)");
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  DeviceGuard guard(w->device);
+  return run_gemv_fused(*w, x, x2, norm_w, eps, prologue, residual, y, static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+tq4_status attention_impl(const float* q, const float* k_new, const float* v_new, float* k_cache, float* v_cache,
+                          const int32_t* pos, float* out, int heads, int kv_heads, int head_dim, int max_len,
+                          void* stream, const RopeArgs& rope) {
   if (!q || !k_new || !v_new || !k_cache || !v_cache || !pos || !out || heads <= 0 || kv_heads <= 0 ||
       heads % kv_heads || heads / kv_heads > kAttnMaxGroup || head_dim <= 0 || head_dim > kAttnMaxDim ||
       (head_dim & 3) || max_len <= 0 || kv_heads > 65535 ||
@@ -423,9 +508,10 @@ tq4_status tq4_attention_decode(const float* q, const float* k_new, const float*
   }
   TQ4_CUDA(launch_pdl(attention_decode_kernel, dim3(chunks, kv_heads), dim3(kAttnThreads), dyn, st, q, k_new, v_new,
                       k_cache, v_cache, pos, out, heads, kv_heads, head_dim, max_len, 1.f / sqrtf((float)head_dim),
-                      part, ctr, chunks));
+                      part, ctr, chunks, rope.q_w, rope.k_w, rope.cos_t, rope.sin_t, rope.eps));
   return TQ4_OK;
 }
+}  // namespace
 
 tq4_status tq4_silu_mul(const float* gate, const float* up, float* out, int64_t n, void* stream) {
   clear_error();

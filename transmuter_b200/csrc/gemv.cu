@@ -72,6 +72,12 @@ struct GemvArgs {
   int spr;
   int maxp;
   int dyn;               // M = 1: whole row tiles handed out by an arrival counter (no partials)
+  // M = 1, f32 activations: a transform applied while staging (decoder fusion). 1: RMSNorm,
+  // a = x * rsqrt(mean(x^2) + eps) * pro_w; 2: SwiGLU, a = silu(x) * pro_b (K values each).
+  int pro;
+  const float* pro_w;
+  const float* pro_b;
+  float pro_eps;
   int64_t n_pad;
   float* ws;
   int* counters;
@@ -217,7 +223,7 @@ __device__ __forceinline__ void load_act4(const void* a, int64_t m, int64_t k, i
 // variant the consumers use.
 template <int BITS, tq4_dtype AT, bool PRECISE = (AT == TQ4_F32)>
 __device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int kr, int mp,
-                                                  uint16_t* act, float4* segf) {
+                                                  uint16_t* act, float4* segf, float pro_rs = 1.f) {
   constexpr bool BF = (AT == TQ4_BF16);
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
@@ -234,7 +240,19 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int
     for (int u = 0; u < 4; ++u) {  // issue all loads first
       const int v = base + u * kConsumers + tid;
       if (v < total) {
-        load_act4<AT>(p.a, v / vec_per_row, (int64_t)k0 + (v % vec_per_row) * 4, p.K, vec, a4[u]);
+        const int64_t k = (int64_t)k0 + (v % vec_per_row) * 4;
+        load_act4<AT>(p.a, v / vec_per_row, k, p.K, vec, a4[u]);
+        if constexpr (AT == TQ4_F32) {
+          if (p.pro == 1) {  // RMSNorm (the row's factor computed by the caller)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) a4[u][e] = (k + e < p.K) ? a4[u][e] * pro_rs * p.pro_w[k + e] : 0.f;
+          } else if (p.pro == 2) {  // SwiGLU
+            float b4[4];
+            load_act4<TQ4_F32>(p.pro_b, 0, k, p.K, vec, b4);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) a4[u][e] = a4[u][e] / (1.f + expf(-a4[u][e])) * b4[e];
+          }
+        }
       } else {
 #pragma unroll
         for (int e = 0; e < 4; ++e) a4[u][e] = 0.f;
@@ -679,18 +697,32 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
   uint16_t* act = reinterpret_cast<uint16_t*>(smem + p.act_off);
   float4* segf = reinterpret_cast<float4*>(smem + p.seg_off);
   pdl_wait();  // activations, outputs and partials belong to the stream's order from here on
+  float pro_rs = 1.f;
+  if (AT == TQ4_F32 && p.pro == 1) {  // RMSNorm prologue: the whole row's mean square
+    __shared__ float red[kConsumers / 32];
+    const float* x = static_cast<const float*>(p.a);
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < p.K; k += kConsumers) ss = fmaf(x[k], x[k], ss);
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (lane == 0) red[warp] = ss;
+    consumer_sync();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kConsumers / 32; ++i) tot += red[i];
+    pro_rs = 1.f / sqrtf(tot / (float)p.K + p.pro_eps);
+  }
   {
     // the activations of the groups this CTA's units touch (one or two runs, or the whole row)
     const int c_a = u0 % p.groups, c_b = (u1 - 1) % p.groups;
     if (u1 - u0 >= p.groups) {
-      stage_activations<4, AT, PRECISE>(p, 0, p.groups * G, 1, act, segf);
+      stage_activations<4, AT, PRECISE>(p, 0, p.groups * G, 1, act, segf, pro_rs);
     } else if (c_a <= c_b) {
       stage_activations<4, AT, PRECISE>(p, c_a * G, (c_b - c_a + 1) * G, 1, act + c_a * G,
-                                        segf + (c_a * G) / SEG);
+                                        segf + (c_a * G) / SEG, pro_rs);
     } else {
       stage_activations<4, AT, PRECISE>(p, c_a * G, (p.groups - c_a) * G, 1, act + c_a * G,
-                                        segf + (c_a * G) / SEG);
-      stage_activations<4, AT, PRECISE>(p, 0, (c_b + 1) * G, 1, act, segf);
+                                        segf + (c_a * G) / SEG, pro_rs);
+      stage_activations<4, AT, PRECISE>(p, 0, (c_b + 1) * G, 1, act, segf, pro_rs);
     }
   }
   consumer_sync();
@@ -1104,9 +1136,30 @@ tq4_status gemv_workspace(const Weight& w, cudaStream_t st, int64_t ws_bytes, in
   return TQ4_OK;
 }
 
+// A staging transform of the decoder's fused projections (GemvArgs::pro).
+struct GemvPrologue {
+  int mode;
+  const float* w;
+  const float* b;
+  float eps;
+};
+
+static tq4_status gemv_launch(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,
+                              tq4_dtype bias_t, void* y, tq4_dtype y_t, int64_t ldy, cudaStream_t st, float* ws,
+                              int* counters, int64_t ws_capacity_floats, int64_t ctr_capacity,
+                              const GemvPrologue* pro);
+
 tq4_status run_gemv_with(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,
                          tq4_dtype bias_t, void* y, tq4_dtype y_t, int64_t ldy, cudaStream_t st,
                          float* ws, int* counters, int64_t ws_capacity_floats, int64_t ctr_capacity) {
+  return gemv_launch(w, a, m, a_t, bias, bias_t, y, y_t, ldy, st, ws, counters, ws_capacity_floats, ctr_capacity,
+                     nullptr);
+}
+
+static tq4_status gemv_launch(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,
+                              tq4_dtype bias_t, void* y, tq4_dtype y_t, int64_t ldy, cudaStream_t st, float* ws,
+                              int* counters, int64_t ws_capacity_floats, int64_t ctr_capacity,
+                              const GemvPrologue* pro) {
   if (!w.gv_maps_ok) {
     set_error("GEMV: the handle has no TMA descriptors");
     return TQ4_ERR_CUDA;
@@ -1149,6 +1202,16 @@ tq4_status run_gemv_with(const Weight& w, const void* a, int64_t m, tq4_dtype a_
   args.spr = pl.spr;
   args.maxp = pl.maxp;
   args.dyn = pl.dyn;
+  if (pro && pro->mode) {
+    if (pl.mode != kM1 || m != 1 || a_t != TQ4_F32) {
+      set_error("fused projection: needs M = 1, f32 activations and a 4-bit weight with block <= 128");
+      return TQ4_ERR_UNSUPPORTED;
+    }
+    args.pro = pro->mode;
+    args.pro_w = pro->w;
+    args.pro_b = pro->b;
+    args.pro_eps = pro->eps;
+  }
   args.n_pad = w.n_pad;
   const int nctr = pl.dyn ? 2 : (pl.ws_floats > 0 ? pl.ctas_n : 0);
   if (pl.ws_floats > 0 || nctr > 0) {
@@ -1179,6 +1242,20 @@ tq4_status run_gemv_with(const Weight& w, const void* a, int64_t m, tq4_dtype a_
 }
 
 int64_t gemv_workspace_floats(const Weight& w, int64_t m) { return plan_gemv(w, m).ws_floats; }
+
+int64_t gemv_counter_count(const Weight& w, int64_t m);
+
+// The decoder's fused projection (include/tq4_decoder.h, tq4_matmul_fused).
+tq4_status run_gemv_fused(const Weight& w, const float* x, const float* x2, const float* norm_w, float eps,
+                          int mode, const float* residual, float* y, cudaStream_t st) {
+  float* ws = nullptr;
+  int* ctr = nullptr;
+  const int64_t need = gemv_workspace_floats(w, 1);
+  const int64_t nctr = gemv_counter_count(w, 1);
+  if (need > 0 || nctr > 0) TQ4_TRY(gemv_workspace(w, st, need * 4, nctr, &ws, &ctr));
+  GemvPrologue pro{mode, norm_w, x2, eps};
+  return gemv_launch(w, x, 1, TQ4_F32, residual, TQ4_F32, y, TQ4_F32, w.desc.N, st, ws, ctr, need, nctr, &pro);
+}
 
 // Counters a call uses (zero-initialised, left at zero by the kernel): one per row tile for split
 // partial sums, two for the M = 1 row-tile hand-out, none otherwise.

@@ -10,7 +10,11 @@ f32 cache (:106-175), SwiGLU. q/k/v and gate/up are merged along N into one MatM
 packed form of the sibling merge in lib/transmuter/fusion.ex:430-540).
 
 A step reads its position and token from device memory; one CUDA graph of a step, replayed,
-runs prompt prefill (forced tokens) and greedy decoding without the host.
+runs prompt prefill (forced tokens) and greedy decoding without the host. A layer is five
+launches: the q/k/v projection with the RMSNorm in its activation staging, attention with the
+QK-norm and RoPE folded in, the o projection adding into the residual stream in place, the
+gate/up projection with the RMSNorm in its staging, and the down projection with SwiGLU in its
+staging, adding into the residual stream (tq4_matmul_fused, tq4_attention_decode_rope).
 """
 
 import ctypes
@@ -95,13 +99,9 @@ class Q4Decoder:
         self.k_cache, self.v_cache = torch.zeros(kv, **f32), torch.zeros(kv, **f32)
         qkv_n = (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim
         self.x = torch.zeros(cfg.hidden, **f32)        # residual stream
-        self.h = torch.zeros(cfg.hidden, **f32)        # normed
         self.qkv = torch.zeros(qkv_n, **f32)
         self.attn = torch.zeros(cfg.heads * cfg.head_dim, **f32)
-        self.o = torch.zeros(cfg.hidden, **f32)
         self.gu = torch.zeros(2 * cfg.inter, **f32)
-        self.act = torch.zeros(cfg.inter, **f32)
-        self.down = torch.zeros(cfg.hidden, **f32)
         self.logits = torch.zeros(cfg.vocab, **f32)
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.token = torch.zeros(1, dtype=torch.int64, device=dev)
@@ -120,6 +120,8 @@ class Q4Decoder:
             "tq4_attention_decode": [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp],
             "tq4_silu_mul": [vp, vp, vp, i64, vp],
             "tq4_argmax_advance": [vp, i64, vp, i32, vp, vp, vp, i32, vp],
+            "tq4_attention_decode_rope": [vp, vp, vp, vp, vp, vp, vp, f, vp, vp, vp, vp, i32, i32, i32, i32, vp],
+            "tq4_matmul_fused": [vp, vp, vp, vp, f, i32, vp, vp, vp],
         }
         for name, args in sigs.items():
             fn = getattr(lib, name)
@@ -132,32 +134,29 @@ class Q4Decoder:
     def step(self):
         """One token: embedding of *token at *pos through every layer, then the greedy step."""
         cfg, lib, st, chk = self.cfg, self._lib, self._stream(), _lib.check
-        p = lambda t: ctypes.c_void_p(t.data_ptr())
+        p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
         qd = cfg.heads * cfg.head_dim
         kd = cfg.kv_heads * cfg.head_dim
         lm = self.weights["lm_head"]
         chk(lib.tq4_gather_rows(lm._handle, p(self.token), 1, p(self.x), st))  # tied embedding
-        delta = None
         for layer in range(cfg.layers):
-            chk(lib.tq4_add_rmsnorm(p(self.x), p(delta) if delta is not None else None, p(self.ones_h),
-                                    p(self.h), 1, cfg.hidden, cfg.eps, st))
-            self.weights[f"{layer}.qkv"].matmul(self.h.view(1, -1), out=self.qkv.view(1, -1))
+            w = lambda name: self.weights[f"{layer}.{name}"]._handle
+            chk(lib.tq4_matmul_fused(w("qkv"), p(self.x), None, p(self.ones_h), cfg.eps, 1, None, p(self.qkv), st))
             q, k, v = self.qkv[:qd], self.qkv[qd:qd + kd], self.qkv[qd + kd:]
-            chk(lib.tq4_qk_norm_rope(p(q), p(k), p(self.ones_d), p(self.ones_d), p(self.cos), p(self.sin),
-                                     p(self.pos), cfg.max_len, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.eps, st))
-            chk(lib.tq4_attention_decode(p(q), p(k), p(v), p(self.k_cache[layer]), p(self.v_cache[layer]),
-                                         p(self.pos), p(self.attn), cfg.heads, cfg.kv_heads, cfg.head_dim,
-                                         cfg.max_len, st))
-            self.weights[f"{layer}.o"].matmul(self.attn.view(1, -1), out=self.o.view(1, -1))
-            chk(lib.tq4_add_rmsnorm(p(self.x), p(self.o), p(self.ones_h), p(self.h), 1, cfg.hidden, cfg.eps, st))
-            self.weights[f"{layer}.gate_up"].matmul(self.h.view(1, -1), out=self.gu.view(1, -1))
-            chk(lib.tq4_silu_mul(p(self.gu[:cfg.inter]), p(self.gu[cfg.inter:]), p(self.act), cfg.inter, st))
-            self.weights[f"{layer}.down"].matmul(self.act.view(1, -1), out=self.down.view(1, -1))
-            delta = self.down
-        chk(lib.tq4_add_rmsnorm(p(self.x), p(delta), p(self.ones_h), p(self.h), 1, cfg.hidden, cfg.eps, st))
-        lm.matmul(self.h.view(1, -1), out=self.logits.view(1, -1))
+            chk(lib.tq4_attention_decode_rope(p(q), p(k), p(v), p(self.ones_d), p(self.ones_d), p(self.cos),
+                                              p(self.sin), cfg.eps, p(self.k_cache[layer]), p(self.v_cache[layer]),
+                                              p(self.pos), p(self.attn), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                              cfg.max_len, st))
+            chk(lib.tq4_matmul_fused(w("o"), p(self.attn), None, None, 0.0, 0, p(self.x), p(self.x), st))
+            chk(lib.tq4_matmul_fused(w("gate_up"), p(self.x), None, p(self.ones_h), cfg.eps, 1, None, p(self.gu), st))
+            chk(lib.tq4_matmul_fused(w("down"), p(self.gu[:cfg.inter]), p(self.gu[cfg.inter:]), None, 0.0, 2,
+                                     p(self.x), p(self.x), st))
+        chk(lib.tq4_matmul_fused(lm._handle, p(self.x), None, p(self.ones_h), cfg.eps, 1, None, p(self.logits), st))
         chk(lib.tq4_argmax_advance(p(self.logits), cfg.vocab, p(self.forced), cfg.max_len, p(self.pos),
                                    p(self.token), p(self.log), cfg.max_len, st))
+
+    LAUNCHES_PER_LAYER = 5
+    LAUNCHES_PER_STEP_EXTRA = 3  # embedding gather, lm_head, argmax
 
     def reset(self, prompt):
         """Starts a sequence: the prompt's tokens are forced, position 0 holds prompt[0]."""
