@@ -72,6 +72,7 @@ struct GemvArgs {
   int spr;
   int maxp;
   int dyn;               // M = 1: whole row tiles handed out by an arrival counter (no partials)
+  int clu, gpc;          // M = 1: a row tile's K split over a cluster of `clu` CTAs, gpc groups each
   // M = 1, f32 activations: a transform applied while staging (decoder fusion). 1: RMSNorm,
   // a = x * rsqrt(mean(x^2) + eps) * pro_w; 2: SwiGLU, a = silu(x) * pro_b (K values each).
   int pro;
@@ -186,6 +187,23 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
 
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int w) {
   return w == 0 ? v.x : (w == 1 ? v.y : (w == 2 ? v.z : v.w));
+}
+
+// Thread-block cluster helpers (distributed shared memory).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_cluster_f32(const float* local, unsigned rank) {
+  uint32_t addr = smem_u32(local), remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(addr), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned cluster_ctarank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
 }
 
 __device__ __forceinline__ void consumer_sync() {
@@ -619,8 +637,18 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
   auto empty = [&](int s) { return bars + 8 * (kMaxStages + s); };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + p.bar_off + 8 * 2 * kMaxStages);
   volatile int* sinfo = reinterpret_cast<volatile int*>(smem + p.bar_off + 8 * 2 * kMaxStages + 16);  // dyn
-  const int u0 = p.dyn ? 0 : unit_first(blockIdx.x, p.units, gridDim.x);
-  const int u1 = p.dyn ? p.units : unit_first(blockIdx.x + 1, p.units, gridDim.x);
+  int u0, u1;
+  if (p.dyn) {
+    u0 = 0;
+    u1 = p.units;
+  } else if (p.clu) {  // row tile blockIdx.x / clu, K share blockIdx.x % clu (its cluster rank)
+    const int rt = blockIdx.x / p.clu, kc = blockIdx.x % p.clu;
+    u0 = rt * p.groups + min(p.groups, kc * p.gpc);
+    u1 = rt * p.groups + min(p.groups, (kc + 1) * p.gpc);
+  } else {
+    u0 = unit_first(blockIdx.x, p.units, gridDim.x);
+    u1 = unit_first(blockIdx.x + 1, p.units, gridDim.x);
+  }
 
   pdl_trigger();
   if (threadIdx.x == 0) {
@@ -711,7 +739,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
     for (int i = 0; i < kConsumers / 32; ++i) tot += red[i];
     pro_rs = 1.f / sqrtf(tot / (float)p.K + p.pro_eps);
   }
-  {
+  if (u1 > u0) {
     // the activations of the groups this CTA's units touch (one or two runs, or the whole row)
     const int c_a = u0 % p.groups, c_b = (u1 - 1) % p.groups;
     if (u1 - u0 >= p.groups) {
@@ -811,7 +839,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
     if (lane == 0) mbar_arrive(empty(s));
 
     // end of this CTA's piece of row tile rt
-    if (c0 + ng == p.groups || u == u1) {
+    if (!p.clu && (c0 + ng == p.groups || u == u1)) {
       float y0 = acc0, y8 = acc8;
       y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
       y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
@@ -838,6 +866,34 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
         ++npub;
       }
     }
+  }
+
+  if (p.clu) {
+    // The cluster's partials of row tile blockIdx.x / clu: each CTA leaves its 128 sums in its
+    // shared memory; the rank-0 CTA adds them in rank order (deterministic) and writes Y; the
+    // second barrier keeps every CTA's shared memory alive until then.
+    __shared__ float red_s[kRows];
+    float y0 = acc0, y8 = acc8;
+    y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+    y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+    y8 += __shfl_xor_sync(0xffffffffu, y8, 1);
+    y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
+    if (t == 0) {
+      red_s[rl] = y0;
+      red_s[rl + 8] = y8;
+    }
+    cluster_sync_all();
+    if (cluster_ctarank() == 0 && threadIdx.x < kRows) {
+      float v = 0.f;
+      for (int r = 0; r < p.clu; ++r) v += ld_cluster_f32(red_s + threadIdx.x, (unsigned)r);
+      const int64_t n = (int64_t)(blockIdx.x / p.clu) * kRows + threadIdx.x;
+      if (n < p.N) {
+        if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
+        store_from_f32(p.y, n, p.y_t, v);
+      }
+    }
+    cluster_sync_all();
+    return;
   }
 
   if (p.dyn) {
@@ -892,7 +948,7 @@ struct GemvPlan {
   int mode, ksplit, groups_per_split, ctas_n, stages, stage_bytes, sc_off, zc_off, act_off,
       seg_off, bar_off, sk, smem, items;
   // M = 1 stream-K (mode kM1)
-  int units, spr, maxp, grid, ctas_per_sm, dyn = 0;
+  int units, spr, maxp, grid, ctas_per_sm, dyn = 0, clu = 0, gpc = 0;
   int64_t ws_floats;  // split-K / stream-K partials (0: none)
 };
 
@@ -950,6 +1006,32 @@ static bool plan_m1(const Weight& w, GemvPlan& pl) {
   // with its CTAs together; no partial sums. Uses counters[0..1].
   pl.dyn = pl.ctas_n >= 2 * pl.grid;
   if (pl.dyn) {
+    pl.maxp = 1;
+    pl.ws_floats = 0;
+    return true;
+  }
+  // Few row tiles (decode-sized calls): a row tile's K split over a cluster of up to 8 CTAs whose
+  // whole shares fit their rings (all copies issued at once, before the previous kernel ends),
+  // partial sums reduced in distributed shared memory. The smallest cluster that gives every SM
+  // a CTA; else the largest that fits.
+  int best = 0;
+  for (int ks = 1; ks <= 8; ks *= 2) {
+    const int gpc = (int)((w.groups + ks - 1) / ks);
+    const int need = (gpc + gps - 1) / gps;
+    if (need > kMaxStages || need * pl.stage_bytes + fixed > kSmemBudget) continue;
+    if ((int64_t)pl.ctas_n * ks > (int64_t)pl.ctas_per_sm * w.num_sms) break;
+    best = ks;
+    if (pl.ctas_n * ks >= w.num_sms) break;
+  }
+  if (best > 0) {
+    pl.clu = best;
+    pl.gpc = (int)((w.groups + best - 1) / best);
+    pl.stages = std::max(1, (pl.gpc + gps - 1) / gps);
+    pl.act_off = pl.stages * pl.stage_bytes;
+    pl.seg_off = pl.act_off + act_bytes;
+    pl.bar_off = pl.seg_off + seg_bytes;
+    pl.smem = pl.bar_off + 8 * 2 * kMaxStages + 32;
+    pl.grid = pl.ctas_n * best;
     pl.maxp = 1;
     pl.ws_floats = 0;
   }
@@ -1027,6 +1109,23 @@ static cudaError_t launch_m1_t(const Weight& w, const GemvArgs& args, int grid, 
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 1024);
     if (e != cudaSuccess) return e;
     attr_set = true;
+  }
+  if (args.clu > 1) {  // a thread-block cluster of args.clu CTAs along x, plus the dependent launch
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = smem + 1024;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = args.clu;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, w.gv_wmap, w.gv_smap, w.gv_zmap, args);
   }
   return launch_pdl(kern, dim3(grid), dim3(kGemvThreads), smem + 1024, st, w.gv_wmap, w.gv_smap, w.gv_zmap,
                     args);
@@ -1202,6 +1301,8 @@ static tq4_status gemv_launch(const Weight& w, const void* a, int64_t m, tq4_dty
   args.spr = pl.spr;
   args.maxp = pl.maxp;
   args.dyn = pl.dyn;
+  args.clu = pl.clu;
+  args.gpc = pl.gpc;
   if (pro && pro->mode) {
     if (pl.mode != kM1 || m != 1 || a_t != TQ4_F32) {
       set_error("fused projection: needs M = 1, f32 activations and a 4-bit weight with block <= 128");
