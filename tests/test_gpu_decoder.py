@@ -109,12 +109,44 @@ def test_attention_decode_against_torch(pos, heads, kv_heads, head_dim):
     vp = lambda t: ctypes.c_void_p(t.data_ptr())
     fn = lib.tq4_attention_decode
     fn.argtypes = [ctypes.c_void_p] * 7 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
-    for _ in range(2):  # twice: the arrival counters must be back at zero after a call
+    for _ in range(2):  # twice: a call leaves nothing behind that changes the next
         _lib.check(fn(*[vp(t) for t in d], vp(p), vp(out), heads, kv_heads, head_dim, max_len,
                       ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
         torch.cuda.synchronize()
         assert o.rel_l2(out.double().cpu().numpy(), ref.numpy()) < 1e-5
     assert torch.equal(d[3][:, pos].cpu(), k_new) and torch.equal(d[4][:, pos].cpu(), v_new)
+
+
+@pytest.mark.parametrize("max_len,pos", [(40, 0), (40, 39), (33, 32), (1000, 517), (1000, 999), (4096, 3000)])
+def test_attention_decode_cache_lengths(max_len, pos):
+    """Caches of other lengths: a cluster of fewer than 8 ranks (short caches) and ranks that fold
+    several 32-position chunks into their running softmax (long caches)."""
+    lib = _lib.load()
+    heads, kv_heads, hd = 16, 8, 128
+    g = torch.Generator().manual_seed(max_len + pos)
+    dev = torch.device("cuda:0")
+    q = torch.randn(heads, hd, generator=g)
+    k_new, v_new = torch.randn(kv_heads, hd, generator=g), torch.randn(kv_heads, hd, generator=g)
+    k_cache = torch.randn(kv_heads, max_len, hd, generator=g)
+    v_cache = torch.randn(kv_heads, max_len, hd, generator=g)
+    k_ref, v_ref = k_cache.double().clone(), v_cache.double().clone()
+    k_ref[:, pos], v_ref[:, pos] = k_new.double(), v_new.double()
+    grp = heads // kv_heads
+    ref = torch.stack([torch.softmax(k_ref[h // grp, :pos + 1] @ q[h].double() / hd ** 0.5, 0) @ v_ref[h // grp, :pos + 1]
+                       for h in range(heads)])
+    d = [t.to(dev).contiguous() for t in (q, k_new, v_new, k_cache, v_cache)]
+    p = torch.tensor([pos], dtype=torch.int32, device=dev)
+    out = torch.empty(heads, hd, device=dev)
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+    fn = lib.tq4_attention_decode
+    fn.argtypes = [ctypes.c_void_p] * 7 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    _lib.check(fn(*[vp(t) for t in d], vp(p), vp(out), heads, kv_heads, hd, max_len,
+                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    assert o.rel_l2(out.double().cpu().numpy(), ref.numpy()) < 1e-5
+    assert torch.equal(d[3][:, pos].cpu(), k_new) and torch.equal(d[4][:, pos].cpu(), v_new)
+    untouched = [i for i in range(max_len) if i != pos]
+    assert torch.equal(d[3][:, untouched].cpu(), k_cache[:, untouched])
 
 
 def torch_reference_logits(dec, cfg, prompt, steps):

@@ -23,6 +23,7 @@ enum DeviceCode : int32_t {
   kDevTimeoutAccum = 0x104,       // GEMM: waited too long for the accumulator
   kDevTimeoutSplitK = 0x105,      // GEMV: split-K reduction counter inconsistent
   kDevTimeoutPeer = 0x106,        // sharded exchange: a peer's slice did not arrive in time
+  kDevTimeoutAttn = 0x107,        // decode attention: a K/V chunk copy did not arrive in time
   kDevBadArgument = 0x200,
 };
 

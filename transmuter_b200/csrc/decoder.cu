@@ -3,10 +3,9 @@
 // position and the tokens live in device memory so a decode step replays as one CUDA graph.
 #include "../../include/tq4_decoder.h"
 #include "internal.cuh"
+#include "sm100.cuh"
 
-#include <map>
-#include <memory>
-#include <mutex>
+#include <algorithm>
 
 namespace tq4 {
 
@@ -121,222 +120,281 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(float* __restrict__ q
   }
 }
 
-// One-token GroupQueryAttention, split over positions (flash-decoding). CTA (chunk c, KV head kvh)
-// takes positions [32c, 32c + 32) for all G = heads / kv_heads query heads of that KV head, so each
-// K/V row is read once per token. A chunk keeps its max m, sum l and unnormalised output
-// o = sum_p exp(s_p - m) v_p; the last chunk CTA of a KV head (atomic arrival count) combines them
-// in chunk order, so the result does not depend on scheduling. The CTA whose chunk holds the new
-// position writes k_new / v_new into the cache; the other chunks never read that row. A CTA first
-// copies its chunk of K and V into shared memory with 16-byte loads all in flight together (one
-// memory round trip), then works from there.
+// One-token GroupQueryAttention, split over positions (flash-decoding) within a thread-block
+// cluster. The C CTAs of KV head kvh (grid (C, kv_heads), cluster (C, 1, 1)) take 32-position
+// chunks in turn: rank r owns chunks r, r + C, ... and keeps, for each of the G = heads / kv_heads
+// query heads, a running max m, sum l and unnormalised output o = sum_p exp(s_p - m) v_p (online
+// softmax over its chunks). The ranks then combine (m, l, o) through distributed shared memory in
+// rank order, so the result does not depend on scheduling, and each rank writes a slice of the
+// output. The rank whose chunk holds position L - 1 writes k_new / v_new into the cache; every
+// chunk sees the new row from shared memory.
+//
+// Latency is the whole cost at decode sizes, so the memory round trips are few: the first chunk's
+// K and V rows travel as two bulk copies issued before the position is known (the rows of chunk r
+// lie inside the cache whatever the position; rows at or past L are never used), together with q,
+// k_new, v_new and the norm weights; only the RoPE table row waits for the position.
 constexpr int kAttnChunk = 32;
 constexpr int kAttnThreads = 128;
 constexpr int kAttnMaxGroup = 8;
 constexpr int kAttnMaxDim = 256;
+constexpr int kAttnMaxCluster = 8;
 
 __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
     const float* __restrict__ q, const float* __restrict__ k_new, const float* __restrict__ v_new,
     float* __restrict__ k_cache, float* __restrict__ v_cache, const int32_t* __restrict__ pos,
     float* __restrict__ out, int heads, int kv_heads, int head_dim, int max_len, float scale,
-    float* __restrict__ part, int* __restrict__ counters, int chunks_max, const float* __restrict__ q_w,
-    const float* __restrict__ k_w, const float* __restrict__ cos_t, const float* __restrict__ sin_t, float eps) {
-  pdl_wait();
-  pdl_trigger();
-  __shared__ float qs[kAttnMaxGroup * kAttnMaxDim];
+    const float* __restrict__ q_w, const float* __restrict__ k_w, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, float eps) {
+  __shared__ __align__(16) float qs[kAttnMaxGroup * kAttnMaxDim];
+  __shared__ __align__(16) float kn_s[kAttnMaxDim];
+  __shared__ __align__(16) float vn_s[kAttnMaxDim];
+  __shared__ __align__(16) float qw_s[kAttnMaxDim];
+  __shared__ __align__(16) float kw_s[kAttnMaxDim];
+  __shared__ float cs_s[kAttnMaxDim / 2], sn_s[kAttnMaxDim / 2];
   __shared__ float sc[kAttnMaxGroup][kAttnChunk];
-  __shared__ float ml[kAttnMaxGroup][2];
-  __shared__ int s_last;
-  const int G = heads / kv_heads;
-  const int c = blockIdx.x, kvh = blockIdx.y;
-  const int L = *pos + 1;
-  if (L < 1 || L > max_len) {  // position past the cache
-    if (threadIdx.x == 0 && c == 0) report(kDevBadArgument);
-    return;
-  }
-  const int nch = (L + kAttnChunk - 1) / kAttnChunk;
-  const int p0 = c * kAttnChunk;
-  if (p0 >= L) return;
-  const int np = min(kAttnChunk, L - p0);
-  const int64_t D = head_dim;
-  const float* kn = k_new + kvh * D;
-  const float* vn = v_new + kvh * D;
-  float* kc = k_cache + (int64_t)kvh * max_len * D;
-  float* vc = v_cache + (int64_t)kvh * max_len * D;
-  const bool has_new = (p0 + np == L);  // this chunk holds position L - 1
+  __shared__ float ml[kAttnMaxGroup][2];  // running max, running sum
+  __shared__ float alpha_s[kAttnMaxGroup];
+  __shared__ float part[kAttnMaxGroup * (kAttnMaxDim + 2)];  // o[g][0..D), m, l: read by the cluster
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int s_abort;
   extern __shared__ float4 kv_chunk[];  // K rows [kAttnChunk][D], then V rows
+
+  const int G = heads / kv_heads, D = head_dim, D4 = head_dim / 4;
+  const int C = (int)gridDim.x;  // the cluster spans x
+  const int r = (int)cluster_ctarank(), kvh = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float* ks = reinterpret_cast<float*>(kv_chunk);
   float* vs = ks + kAttnChunk * D;
-  const int D4 = head_dim / 4;
-#pragma unroll 8
-  for (int i = threadIdx.x; i < np * D4; i += kAttnThreads) {
-    const int pi = i / D4, d4 = i - pi * D4;
-    const bool nw = (p0 + pi == L - 1);
-    const float4* kr = reinterpret_cast<const float4*>(nw ? kn : kc + (int64_t)(p0 + pi) * D);
-    const float4* vr = reinterpret_cast<const float4*>(nw ? vn : vc + (int64_t)(p0 + pi) * D);
-    reinterpret_cast<float4*>(ks)[i] = kr[d4];
-    reinterpret_cast<float4*>(vs)[i] = vr[d4];
+  const uint32_t bar_a = smem_u32(&bar);
+  float* kc = k_cache + (int64_t)kvh * max_len * D;
+  float* vc = v_cache + (int64_t)kvh * max_len * D;
+
+  pdl_wait();
+  pdl_trigger();
+  // Trip 1: the first chunk's rows (bulk copies), the position, q, the new row, the norm weights.
+  const int rows0 = min(kAttnChunk, max_len - r * kAttnChunk);  // >= 1: C <= ceil(max_len / 32)
+  if (tid == 0) {
+    s_abort = 0;
+    mbar_init(bar_a, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    fence_proxy_async_smem();
+    const uint32_t bytes = (uint32_t)(rows0 * D * 4);
+    mbar_expect_tx(bar_a, 2 * bytes);
+    bulk_load(smem_u32(ks), kc + (int64_t)r * kAttnChunk * D, bytes, bar_a);
+    bulk_load(smem_u32(vs), vc + (int64_t)r * kAttnChunk * D, bytes, bar_a);
   }
-  for (int i = threadIdx.x; i < G * head_dim; i += kAttnThreads) qs[i] = q[(int64_t)kvh * G * D + i];
+  const int L = *pos + 1;
+  const float4* q4 = reinterpret_cast<const float4*>(q + (int64_t)kvh * G * D);
+  float4 qr[kAttnMaxGroup * kAttnMaxDim / 4 / kAttnThreads];
+#pragma unroll
+  for (int j = 0; j < kAttnMaxGroup * kAttnMaxDim / 4 / kAttnThreads; ++j) {
+    const int i = tid + j * kAttnThreads;
+    if (i < G * D4) qr[j] = q4[i];
+  }
+  float4 knr, vnr, qwr, kwr;
+  if (tid < D4) {
+    knr = reinterpret_cast<const float4*>(k_new + (int64_t)kvh * D)[tid];
+    vnr = reinterpret_cast<const float4*>(v_new + (int64_t)kvh * D)[tid];
+    if (q_w) {
+      qwr = reinterpret_cast<const float4*>(q_w)[tid];
+      kwr = reinterpret_cast<const float4*>(k_w)[tid];
+    }
+  }
+  const bool valid = L >= 1 && L <= max_len;  // the same for every CTA
+  const int half = D / 2;
+  float cv = 0.f, sv = 0.f;
+  if (q_w && valid && tid < half) {  // trip 2: the RoPE table row of position L - 1
+    cv = cos_t[(int64_t)(L - 1) * half + tid];
+    sv = sin_t[(int64_t)(L - 1) * half + tid];
+  }
+#pragma unroll
+  for (int j = 0; j < kAttnMaxGroup * kAttnMaxDim / 4 / kAttnThreads; ++j) {
+    const int i = tid + j * kAttnThreads;
+    if (i < G * D4) reinterpret_cast<float4*>(qs)[i] = qr[j];
+  }
+  if (tid < D4) {
+    reinterpret_cast<float4*>(kn_s)[tid] = knr;
+    reinterpret_cast<float4*>(vn_s)[tid] = vnr;
+    if (q_w) {
+      reinterpret_cast<float4*>(qw_s)[tid] = qwr;
+      reinterpret_cast<float4*>(kw_s)[tid] = kwr;
+    }
+  }
+  if (tid < half) {
+    cs_s[tid] = cv;
+    sn_s[tid] = sv;
+  }
+  if (tid < G) {
+    ml[tid][0] = -INFINITY;
+    ml[tid][1] = 0.f;
+  }
   __syncthreads();
-  float* knew_s = has_new ? ks + (L - 1 - p0) * D : nullptr;  // the new key's staged row
+  if (!valid) {  // position past the cache: every CTA sees it, none writes anything
+    if (tid == 0 && r == 0 && kvh == 0) report(kDevBadArgument);
+    mbar_drain(bar_a, 0);
+    return;
+  }
+
   if (q_w) {
     // Qwen3's per-head RMSNorm then rotate-half RoPE at position L - 1 (rms_norm/4,
-    // transformer.ex:1056-1069; rotate/4, :558-590), on the query heads and the new key.
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int rows = G + (has_new ? 1 : 0);
-    for (int r = warp; r < rows; r += kAttnThreads / 32) {
-      float* v = r < G ? qs + r * D : knew_s;
-      const float* w = r < G ? q_w : k_w;
+    // transformer.ex:1056-1069; rotate/4, :558-590), on the G query heads and the new key.
+    for (int row = warp; row <= G; row += kAttnThreads / 32) {
+      float* v = row < G ? qs + row * D : kn_s;
+      const float* w = row < G ? qw_s : kw_s;
       float ss = 0.f;
-      for (int d = lane; d < head_dim; d += 32) ss = fmaf(v[d], v[d], ss);
+      for (int d = lane; d < D; d += 32) ss = fmaf(v[d], v[d], ss);
       for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-      const float inv = 1.f / sqrtf(ss / (float)head_dim + eps);
+      const float inv = 1.f / sqrtf(ss / (float)D + eps);
       __syncwarp();
-      for (int d = lane; d < head_dim; d += 32) v[d] = v[d] * inv * w[d];
-    }
-    __syncthreads();
-    const int half = head_dim / 2;
-    const float* cr = cos_t + (int64_t)(L - 1) * half;
-    const float* sr = sin_t + (int64_t)(L - 1) * half;
-    for (int i = threadIdx.x; i < rows * half; i += kAttnThreads) {
-      const int r = i / half, j = i % half;
-      float* v = r < G ? qs + r * D : knew_s;
-      const float c = cr[j], sn = sr[j];
-      const float x1 = v[j], x2 = v[j + half];
-      v[j] = x1 * c - x2 * sn;
-      v[j + half] = x2 * c + x1 * sn;
+      for (int d = lane; d < D; d += 32) v[d] = v[d] * inv * w[d];
+      __syncwarp();
+      for (int j = lane; j < half; j += 32) {
+        const float c = cs_s[j], sn = sn_s[j];
+        const float x1 = v[j], x2 = v[j + half];
+        v[j] = x1 * c - x2 * sn;
+        v[j + half] = x2 * c + x1 * sn;
+      }
     }
     __syncthreads();
   }
-  if (has_new)
-    for (int d = threadIdx.x; d < head_dim; d += kAttnThreads) {
-      kc[(int64_t)(L - 1) * D + d] = knew_s[d];
-      vc[(int64_t)(L - 1) * D + d] = vn[d];
-    }
-  __syncthreads();
 
-  // scores: warp w takes positions w, w + 4, ...; lanes split head_dim
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = warp; i < np; i += kAttnThreads / 32) {
-    const float* kp = ks + i * D;
-    float dot[kAttnMaxGroup];
+  // This rank's chunks, each folded into the running (m, l, o) of every query head.
+  constexpr int kDPer = kAttnMaxDim / kAttnThreads;  // output columns per thread
+  float o[kDPer][kAttnMaxGroup];
 #pragma unroll
-    for (int g = 0; g < kAttnMaxGroup; ++g) dot[g] = 0.f;
-    for (int d = lane; d < head_dim; d += 32) {
-      const float kv = kp[d];
+  for (int j = 0; j < kDPer; ++j)
+#pragma unroll
+    for (int g = 0; g < kAttnMaxGroup; ++g) o[j][g] = 0.f;
+  uint32_t parity = 0;
+  mbar_wait(bar_a, 0, &s_abort, kDevTimeoutAttn);  // the first chunk's copies, used or not
+  for (int c = r; c * kAttnChunk < L; c += C) {
+    const int p0 = c * kAttnChunk, np = min(kAttnChunk, L - p0);
+    if (c != r) {  // a later chunk (contexts past 32 * C positions): the buffer is free again
+      __syncthreads();
+      parity ^= 1u;
+      if (tid == 0) {
+        fence_proxy_async_smem();
+        const uint32_t bytes = (uint32_t)(np * D * 4);
+        mbar_expect_tx(bar_a, 2 * bytes);
+        bulk_load(smem_u32(ks), kc + (int64_t)p0 * D, bytes, bar_a);
+        bulk_load(smem_u32(vs), vc + (int64_t)p0 * D, bytes, bar_a);
+      }
+      mbar_wait(bar_a, parity, &s_abort, kDevTimeoutAttn);
+    }
+    if (p0 + np == L)  // this chunk holds the new position: its row comes from k_new / v_new
+      for (int d = tid; d < D; d += kAttnThreads) {
+        ks[(np - 1) * D + d] = kn_s[d];
+        vs[(np - 1) * D + d] = vn_s[d];
+      }
+    __syncthreads();
+    // scores: warp w takes positions w, w + 4, ...; lanes split head_dim
+    for (int i = warp; i < np; i += kAttnThreads / 32) {
+      const float* kp = ks + i * D;
+      float dot[kAttnMaxGroup];
+#pragma unroll
+      for (int g = 0; g < kAttnMaxGroup; ++g) dot[g] = 0.f;
+      for (int d = lane; d < D; d += 32) {
+        const float kv = kp[d];
+#pragma unroll
+        for (int g = 0; g < kAttnMaxGroup; ++g)
+          if (g < G) dot[g] = fmaf(qs[g * D + d], kv, dot[g]);
+      }
+#pragma unroll
+      for (int g = 0; g < kAttnMaxGroup; ++g) {
+        if (g >= G) break;
+        float v = dot[g];
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0) sc[g][i] = v * scale;
+      }
+    }
+    __syncthreads();
+    // online softmax statistics: warp w takes heads w, w + 4, ...
+    for (int g = warp; g < G; g += kAttnThreads / 32) {
+      const float v = lane < np ? sc[g][lane] : -INFINITY;
+      float mc = v;
+      for (int off = 16; off > 0; off >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, off));
+      const float m_old = ml[g][0];
+      const float m_new = fmaxf(m_old, mc);
+      const float e = lane < np ? expf(v - m_new) : 0.f;
+      float l = e;
+      for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+      if (lane < np) sc[g][lane] = e;
+      __syncwarp();
+      if (lane == 0) {
+        const float alpha = expf(m_old - m_new);  // 0 on the first chunk (m_old = -inf)
+        alpha_s[g] = alpha;
+        ml[g][0] = m_new;
+        ml[g][1] = ml[g][1] * alpha + l;
+      }
+    }
+    __syncthreads();
+    // o[g][d] = alpha[g] o[g][d] + sum_p e[g][p] v[p][d]
+#pragma unroll
+    for (int j = 0; j < kDPer; ++j) {
+      const int d = tid + j * kAttnThreads;
+      if (d < D) {
+        float acc[kAttnMaxGroup];
+#pragma unroll
+        for (int g = 0; g < kAttnMaxGroup; ++g) acc[g] = 0.f;
+        for (int i = 0; i < np; ++i) {
+          const float vv = vs[i * D + d];
+#pragma unroll
+          for (int g = 0; g < kAttnMaxGroup; ++g)
+            if (g < G) acc[g] = fmaf(sc[g][i], vv, acc[g]);
+        }
+#pragma unroll
+        for (int g = 0; g < kAttnMaxGroup; ++g)
+          if (g < G) o[j][g] = fmaf(o[j][g], alpha_s[g], acc[g]);
+      }
+    }
+  }
+  // The rank that holds position L - 1 stores the new row (its chunk's bulk copies have landed).
+  if (((L - 1) / kAttnChunk) % C == r)
+    for (int d = tid; d < D; d += kAttnThreads) {
+      kc[(int64_t)(L - 1) * D + d] = kn_s[d];
+      vc[(int64_t)(L - 1) * D + d] = vn_s[d];
+    }
+  // Leave this rank's (o, m, l) for the cluster.
+#pragma unroll
+  for (int j = 0; j < kDPer; ++j) {
+    const int d = tid + j * kAttnThreads;
+    if (d < D)
 #pragma unroll
       for (int g = 0; g < kAttnMaxGroup; ++g)
-        if (g < G) dot[g] = fmaf(qs[g * head_dim + d], kv, dot[g]);
-    }
+        if (g < G) part[g * (D + 2) + d] = o[j][g];
+  }
+  if (tid < G) {
+    part[tid * (D + 2) + D] = ml[tid][0];
+    part[tid * (D + 2) + D + 1] = ml[tid][1];
+  }
+  cluster_sync_all();
+  // Combine in rank order; rank r writes outputs r * 128 + tid, then every C * 128 further.
+  for (int i = r * kAttnThreads + tid; i < G * D; i += C * kAttnThreads) {
+    const int g = i / D, d = i - g * D;
+    float mr[kAttnMaxCluster], lr[kAttnMaxCluster], orr[kAttnMaxCluster];
 #pragma unroll
-    for (int g = 0; g < kAttnMaxGroup; ++g) {
-      if (g >= G) break;
-      float v = dot[g];
-      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-      if (lane == 0) sc[g][i] = v * scale;
-    }
-  }
-  __syncthreads();
-  // chunk softmax statistics: warp w takes heads w, w + 4, ...
-  for (int g = warp; g < G; g += kAttnThreads / 32) {
-    const float v = lane < np ? sc[g][lane] : -INFINITY;
-    float m = v;
-    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    const float e = lane < np ? expf(v - m) : 0.f;
-    float l = e;
-    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-    if (lane < np) sc[g][lane] = e;
-    if (lane == 0) {
-      ml[g][0] = m;
-      ml[g][1] = l;
-    }
-  }
-  __syncthreads();
-  // o[g][d] = sum_p e[g][p] v[p][d]
-  const int64_t stride_c = (int64_t)G * (D + 2);
-  float* my = part + ((int64_t)kvh * chunks_max + c) * stride_c;
-  for (int d = threadIdx.x; d < head_dim; d += kAttnThreads) {
-    float o[kAttnMaxGroup];
-#pragma unroll
-    for (int g = 0; g < kAttnMaxGroup; ++g) o[g] = 0.f;
-    for (int i = 0; i < np; ++i) {
-      const float vv = vs[i * D + d];
-#pragma unroll
-      for (int g = 0; g < kAttnMaxGroup; ++g)
-        if (g < G) o[g] = fmaf(sc[g][i], vv, o[g]);
-    }
-#pragma unroll
-    for (int g = 0; g < kAttnMaxGroup; ++g) {
-      if (g >= G) break;
-      if (nch == 1)
-        out[((int64_t)kvh * G + g) * D + d] = o[g] / ml[g][1];
-      else
-        my[g * (D + 2) + d] = o[g];
-    }
-  }
-  if (nch == 1) return;
-  if (threadIdx.x < G) {
-    my[threadIdx.x * (D + 2) + D] = ml[threadIdx.x][0];
-    my[threadIdx.x * (D + 2) + D + 1] = ml[threadIdx.x][1];
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int prev = atomicAdd(&counters[kvh], 1);
-    s_last = (prev == nch - 1);
-    if (prev >= nch) report(kDevTimeoutSplitK);  // a counter left non-zero earlier
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  const float* base = part + (int64_t)kvh * chunks_max * stride_c;
-  for (int i = threadIdx.x; i < G * head_dim; i += kAttnThreads) {
-    const int g = i / head_dim, d = i % head_dim;
+    for (int cc = 0; cc < kAttnMaxCluster; ++cc)
+      if (cc < C) {
+        mr[cc] = ld_cluster_f32(part + g * (D + 2) + D, (unsigned)cc);
+        lr[cc] = ld_cluster_f32(part + g * (D + 2) + D + 1, (unsigned)cc);
+        orr[cc] = ld_cluster_f32(part + g * (D + 2) + d, (unsigned)cc);
+      }
     float M = -INFINITY;
-    for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, base[cc * stride_c + g * (D + 2) + D]);
+#pragma unroll
+    for (int cc = 0; cc < kAttnMaxCluster; ++cc)
+      if (cc < C) M = fmaxf(M, mr[cc]);
     float num = 0.f, den = 0.f;
-    for (int cc = 0; cc < nch; ++cc) {
-      const float* pc = base + cc * stride_c + g * (D + 2);
-      const float w = expf(pc[D] - M);
-      num = fmaf(w, pc[d], num);
-      den = fmaf(w, pc[D + 1], den);
-    }
+#pragma unroll
+    for (int cc = 0; cc < kAttnMaxCluster; ++cc)
+      if (cc < C) {
+        const float w = expf(mr[cc] - M);  // 0 for a rank without positions (m = -inf)
+        num = fmaf(w, orr[cc], num);
+        den = fmaf(w, lr[cc], den);
+      }
     out[((int64_t)kvh * G + g) * D + d] = num / den;
   }
-  if (threadIdx.x == 0) counters[kvh] = 0;
-}
-
-// Per-(device, stream) scratch of the attention partials and arrival counters.
-struct AttnScratch {
-  DeviceBuffer part, counters;
-};
-static std::mutex g_attn_mu;
-static std::map<std::pair<int, cudaStream_t>, std::unique_ptr<AttnScratch>> g_attn_scratch;
-
-static tq4_status attn_scratch(cudaStream_t st, int64_t part_bytes, int64_t counters, float** part, int** ctr) {
-  int dev = 0;
-  TQ4_CUDA(cudaGetDevice(&dev));
-  std::lock_guard<std::mutex> lock(g_attn_mu);
-  auto& slot = g_attn_scratch[{dev, st}];
-  if (!slot) slot.reset(new AttnScratch());
-  if (slot->part.bytes < part_bytes || slot->counters.bytes < counters * 4) {
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    TQ4_CUDA(cudaStreamIsCapturing(st, &cs));
-    if (cs != cudaStreamCaptureStatusNone) {
-      set_error("tq4_attention_decode: first call on a stream (or a larger cache) during stream capture; "
-                "call it once before capturing");
-      return TQ4_ERR_INVALID_ARGUMENT;
-    }
-    TQ4_CUDA(cudaStreamSynchronize(st));
-    if (slot->part.bytes < part_bytes) TQ4_TRY(slot->part.alloc(part_bytes));
-    if (slot->counters.bytes < counters * 4) {
-      TQ4_TRY(slot->counters.alloc(counters * 4));
-      TQ4_CUDA(cudaMemsetAsync(slot->counters.ptr, 0, counters * 4, st));
-    }
-  }
-  *part = static_cast<float*>(slot->part.ptr);
-  *ctr = static_cast<int*>(slot->counters.ptr);
-  return TQ4_OK;
+  if (s_abort) mbar_drain(bar_a, parity);  // a copy that timed out: give it one more bounded wait
+  cluster_sync_all();  // no rank leaves while another still reads its shared memory
 }
 
 __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ out,
@@ -486,29 +544,40 @@ tq4_status attention_impl(const float* q, const float* k_new, const float* v_new
   if (!q || !k_new || !v_new || !k_cache || !v_cache || !pos || !out || heads <= 0 || kv_heads <= 0 ||
       heads % kv_heads || heads / kv_heads > kAttnMaxGroup || head_dim <= 0 || head_dim > kAttnMaxDim ||
       (head_dim & 3) || max_len <= 0 || kv_heads > 65535 ||
-      ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new) |
-        reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15)) {
+      ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new) |
+        reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
+        reinterpret_cast<uintptr_t>(rope.q_w) | reinterpret_cast<uintptr_t>(rope.k_w)) & 15)) {
     set_error("tq4_attention_decode: bad arguments (heads a multiple of kv_heads, at most %d query heads per "
-              "KV head, head_dim a multiple of 4 and <= %d, K/V pointers 16-byte aligned)",
+              "KV head, head_dim a multiple of 4 and <= %d, q / K / V / norm-weight pointers 16-byte aligned)",
               kAttnMaxGroup, kAttnMaxDim);
     return TQ4_ERR_INVALID_ARGUMENT;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int G = heads / kv_heads;
   const int chunks = (max_len + kAttnChunk - 1) / kAttnChunk;
-  float* part = nullptr;
-  int* ctr = nullptr;
-  TQ4_TRY(attn_scratch(st, (int64_t)kv_heads * chunks * G * (head_dim + 2) * 4, kv_heads, &part, &ctr));
-  const size_t dyn = (size_t)2 * kAttnChunk * head_dim * sizeof(float);
+  const int C = std::min(kAttnMaxCluster, chunks);
   static bool attr_set = false;
   if (!attr_set) {
     TQ4_CUDA(cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   2 * kAttnChunk * kAttnMaxDim * (int)sizeof(float)));
     attr_set = true;
   }
-  TQ4_CUDA(launch_pdl(attention_decode_kernel, dim3(chunks, kv_heads), dim3(kAttnThreads), dyn, st, q, k_new, v_new,
-                      k_cache, v_cache, pos, out, heads, kv_heads, head_dim, max_len, 1.f / sqrtf((float)head_dim),
-                      part, ctr, chunks, rope.q_w, rope.k_w, rope.cos_t, rope.sin_t, rope.eps));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C, kv_heads);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = (size_t)2 * kAttnChunk * head_dim * sizeof(float);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  TQ4_CUDA(cudaLaunchKernelEx(&cfg, attention_decode_kernel, q, k_new, v_new, k_cache, v_cache, pos, out, heads,
+                              kv_heads, head_dim, max_len, 1.f / sqrtf((float)head_dim), rope.q_w, rope.k_w,
+                              rope.cos_t, rope.sin_t, rope.eps));
   return TQ4_OK;
 }
 }  // namespace

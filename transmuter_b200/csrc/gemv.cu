@@ -41,7 +41,6 @@ constexpr int kConsumers = 256;
 constexpr int kGemvThreads = kConsumers + 32;
 constexpr int kMaxStages = 4;
 constexpr int kSmemBudget = 110 * 1024;  // two CTAs per SM
-constexpr int kSmemBudget3 = 0;          // three CTAs per SM (M = 1 kernel): measured slower, off
 
 enum GemvMode { kCols = 0, kSegMT1 = 1, kSegMT2 = 2 };
 
@@ -72,6 +71,7 @@ struct GemvArgs {
   int spr;
   int maxp;
   int dyn;               // M = 1: whole row tiles handed out by an arrival counter (no partials)
+  int pre, bf_off;       // M = 1: B fragments prebuilt per CTA at bf_off (0: masked in the loop)
   int clu, gpc;          // M = 1: a row tile's K split over a cluster of `clu` CTAs, gpc groups each
   // M = 1, f32 activations: a transform applied while staging (decoder fusion). 1: RMSNorm,
   // a = x * rsqrt(mean(x^2) + eps) * pro_w; 2: SwiGLU, a = silu(x) * pro_b (K values each).
@@ -189,23 +189,6 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int w) {
   return w == 0 ? v.x : (w == 1 ? v.y : (w == 2 ? v.z : v.w));
 }
 
-// Thread-block cluster helpers (distributed shared memory).
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ float ld_cluster_f32(const float* local, unsigned rank) {
-  uint32_t addr = smem_u32(local), remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(addr), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-  return v;
-}
-__device__ __forceinline__ unsigned cluster_ctarank() {
-  unsigned r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
 }
@@ -239,9 +222,14 @@ __device__ __forceinline__ void load_act4(const void* a, int64_t m, int64_t k, i
 // depends only on its own activation row. Run by the 256 consumer threads. `act` and `segf`
 // point at position k0 (element k0 - kk is at act[kk]). PRECISE must match the weight_pairs
 // variant the consumers use.
-template <int BITS, tq4_dtype AT, bool PRECISE = (AT == TQ4_F32)>
+//
+// With BF_SPS > 0 (M = 1, the whole row, k0 = 0) each 4-value run also lands in the prebuilt B
+// fragment table `bfw` (uint2 units, zero-filled beforehand): 16-k slice ks, lane
+// 4 * ((ks / BF_SPS) % BF_NSEG) + (k / 4) % 4, half ks % 2 of slice pair ks / 2.
+template <int BITS, tq4_dtype AT, bool PRECISE = (AT == TQ4_F32), int BF_SPS = 0, int BF_NSEG = 8>
 __device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int kr, int mp,
-                                                  uint16_t* act, float4* segf, float pro_rs = 1.f) {
+                                                  uint16_t* act, float4* segf, float pro_rs = 1.f,
+                                                  uint2* bfw = nullptr) {
   constexpr bool BF = (AT == TQ4_BF16);
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
@@ -318,6 +306,11 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int
         packed.x = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
         packed.y = (uint32_t)h[2] | ((uint32_t)h[3] << 16);
         *reinterpret_cast<uint2*>(act + m * p.sk + kk) = packed;
+        if constexpr (BF_SPS > 0) {
+          const int ks = kk >> 4;
+          const int dst = ((ks >> 1) * 32 + 4 * ((ks / BF_SPS) % BF_NSEG) + ((kk >> 2) & 3)) * 2 + (ks & 1);
+          bfw[dst] = packed;
+        }
         if ((lane & (L - 1)) == 0) {
           const int s_idx = kk >> p.seg_log2;
           const float za = e_scale * sa;
@@ -677,26 +670,36 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
         tma_load_2d(st + p.sc_off, &map_s, row0, b0, full(s));
         if (p.has_zp) tma_load_2d(st + p.zc_off, &map_z, row0, b0, full(s));
       };
+      int s = 0;
+      uint32_t ph = 0;  // the ring's current lap parity
+      auto advance = [&]() {
+        ++gs;
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
+        }
+      };
       if (p.dyn) {
         // Row tile blockIdx.x first (prefetched before the previous kernel finishes), then the
         // tiles gridDim.x, gridDim.x + 1, ... in arrival order: CTAs that stream faster take more.
+        // A stage's tag is its (row tile, first group); row tile -1 says there is no more work.
         int rt = blockIdx.x;
         bool waited = false, ok = true;
         while (ok) {
           if (rt >= p.ctas_n) {  // no work left: a stage that only says so
-            const int s = gs % S;
-            if (!mbar_wait(empty(s), ((gs / S) & 1) ^ 1, abort_flag, kDevTimeoutStageEmpty)) break;
-            sinfo[s] = -1;
+            if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, kDevTimeoutStageEmpty)) break;
+            sinfo[2 * s] = -1;
             mbar_arrive(full(s));
-            ++gs;
+            advance();
             break;
           }
-          for (int c0 = 0; c0 < p.groups && ok; c0 += GPS, ++gs) {
-            const int s = gs % S;
-            ok = mbar_wait(empty(s), ((gs / S) & 1) ^ 1, abort_flag, kDevTimeoutStageEmpty);
+          for (int c0 = 0; c0 < p.groups && ok; c0 += GPS) {
+            ok = mbar_wait(empty(s), ph ^ 1u, abort_flag, kDevTimeoutStageEmpty);
             if (!ok) break;
-            sinfo[s] = rt * p.groups + c0;
+            sinfo[2 * s] = rt;
+            sinfo[2 * s + 1] = c0;
             issue(s, rt, c0, min(GPS, p.groups - c0));
+            advance();
           }
           if (!waited) {
             pdl_wait();  // the counters belong to the stream's order
@@ -705,13 +708,18 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
           rt = gridDim.x + atomicAdd(&p.counters[0], 1);
         }
       } else {
-        for (int u = u0; u < u1; ++gs) {
-          const int s = gs % S;
-          if (!mbar_wait(empty(s), ((gs / S) & 1) ^ 1, abort_flag, kDevTimeoutStageEmpty)) break;
-          const int rt = u / p.groups, c0 = u % p.groups;
+        int rt = u0 / p.groups, c0 = u0 - rt * p.groups;
+        for (int u = u0; u < u1;) {
+          if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, kDevTimeoutStageEmpty)) break;
           const int ng = min(min(GPS, p.groups - c0), u1 - u);  // a chunk never crosses a row tile
-          u += ng;
           issue(s, rt, c0, ng);
+          advance();
+          u += ng;
+          c0 += ng;
+          if (c0 == p.groups) {
+            c0 = 0;
+            ++rt;
+          }
         }
       }
       for (int g = max(0, gs - S); g < gs; ++g) mbar_drain(full(g % S), (g / S) & 1);
@@ -724,6 +732,11 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
   const int rl = warp * 16 + g;
   uint16_t* act = reinterpret_cast<uint16_t*>(smem + p.act_off);
   float4* segf = reinterpret_cast<float4*>(smem + p.seg_off);
+  uint4* bf = reinterpret_cast<uint4*>(smem + p.bf_off);
+  if (p.pre) {  // the prebuilt fragment table starts as zeros (before the wait: shared memory only)
+    for (int i = threadIdx.x; i < p.groups * 128; i += kConsumers) bf[i] = make_uint4(0u, 0u, 0u, 0u);
+    consumer_sync();  // before other threads' staging writes land in the same entries
+  }
   pdl_wait();  // activations, outputs and partials belong to the stream's order from here on
   float pro_rs = 1.f;
   if (AT == TQ4_F32 && p.pro == 1) {  // RMSNorm prologue: the whole row's mean square
@@ -742,7 +755,10 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
   if (u1 > u0) {
     // the activations of the groups this CTA's units touch (one or two runs, or the whole row)
     const int c_a = u0 % p.groups, c_b = (u1 - 1) % p.groups;
-    if (u1 - u0 >= p.groups) {
+    if (p.pre) {
+      stage_activations<4, AT, PRECISE, SPS, NSEG>(p, 0, p.groups * G, 1, act, segf, pro_rs,
+                                                   reinterpret_cast<uint2*>(bf));
+    } else if (u1 - u0 >= p.groups) {
       stage_activations<4, AT, PRECISE>(p, 0, p.groups * G, 1, act, segf, pro_rs);
     } else if (c_a <= c_b) {
       stage_activations<4, AT, PRECISE>(p, c_a * G, (c_b - c_a + 1) * G, 1, act + c_a * G,
@@ -755,39 +771,72 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
   }
   consumer_sync();
 
-  // 0/1 multipliers of this thread's B column for each stage column
+  // Prebuilt B fragments (the lm_head's row-tile hand-out, where a CTA reuses them for every
+  // row tile it takes): MMA column c takes the segments s with s % NSEG == c (an absolute
+  // assignment), and a lane's B fragment of 16-k slice ks is its four staged activations when
+  // its column g is the slice's, else zero: the 0/1 column mask applied once per CTA instead of
+  // in every MMA step. Layout [group][slice pair][lane] of uint4 (slices 2i, 2i+1): one 16-byte
+  // load per two MMAs.
+  const uint4* bfq = bf + lane;
+
+  // 0/1 multipliers of this thread's B column for each stage column (stages relative)
   const uint32_t one2 = BF ? 0x3F803F80u : 0x3C003C00u;
   uint32_t mask[NSEG];
 #pragma unroll
   for (int c = 0; c < NSEG; ++c) mask[c] = (g == c) ? one2 : 0u;
 
-  int gs = 0;
+  int s = 0;
+  uint32_t ph = 0;  // the ring's current lap parity
   bool ok = true;
   float acc0 = 0.f, acc8 = 0.f;
   int npub = 0, pub_rt[2] = {0, 0}, pub_pieces[2] = {0, 0};
-  for (int u = u0; u < u1; ++gs) {
-    const int s = gs % S;
-    int rt, c0, ng;
+  int rt = u0 / p.groups, c0 = u0 - rt * p.groups, ng = 0;  // walk of the static modes
+  for (int u = u0; u < u1;) {
     if (p.dyn) {
-      if (!mbar_wait(full(s), (gs / S) & 1, abort_flag, kDevTimeoutTmaFull)) break;
-      const int info = sinfo[s];
-      if (info < 0) break;  // the producer ran out of row tiles
-      rt = info / p.groups;
-      c0 = info % p.groups;
+      if (!mbar_wait(full(s), ph, abort_flag, kDevTimeoutTmaFull)) break;
+      rt = sinfo[2 * s];
+      if (rt < 0) break;  // the producer ran out of row tiles
+      c0 = sinfo[2 * s + 1];
       ng = min(GPS, p.groups - c0);
     } else {
-      rt = u / p.groups;
-      c0 = u % p.groups;
+      if (ng > 0) {  // the previous stage's groups
+        c0 += ng;
+        if (c0 == p.groups) {
+          c0 = 0;
+          ++rt;
+        }
+      }
       ng = min(min(GPS, p.groups - c0), u1 - u);
       u += ng;
-      if (ok) ok = mbar_wait(full(s), (gs / S) & 1, abort_flag, kDevTimeoutTmaFull);
+      if (ok) ok = mbar_wait(full(s), ph, abort_flag, kDevTimeoutTmaFull);
     }
     if (ok) {
       const uint8_t* st = smem + s * p.stage_bytes;
       const uint8_t* sc = st + p.sc_off;
       const uint8_t* zc = st + p.zc_off;
       const uint16_t* actk = act + c0 * G + 4 * t;
+      const uint4* bq = bfq + c0 * 128;
       float blk2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // even / odd steps
+      if (p.pre) {
+#pragma unroll
+        for (int gi = 0; gi < GPS; ++gi) {
+          if (gi < ng) {
+            const uint4 xa = *reinterpret_cast<const uint4*>(st + gi * kRows * 64 + rl * 64 + t * 16);
+            const uint4 xb = *reinterpret_cast<const uint4*>(st + gi * kRows * 64 + (rl + 8) * 64 + t * 16);
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+              const uint4 bb = bq[(gi * 4 + j / 2) * 32];
+              uint32_t a0, a1, a2, a3;
+              weight_pairs<4, BF, PRECISE>(word_of(xa, j / 2), j, a0, a2);
+              weight_pairs<4, BF, PRECISE>(word_of(xb, j / 2), j, a1, a3);
+              mma16816<BF>(blk2[0], a0, a1, a2, a3, bb.x, bb.y);
+              weight_pairs<4, BF, PRECISE>(word_of(xa, j / 2), j + 1, a0, a2);
+              weight_pairs<4, BF, PRECISE>(word_of(xb, j / 2), j + 1, a1, a3);
+              mma16816<BF>(blk2[1], a0, a1, a2, a3, bb.z, bb.w);
+            }
+          }
+        }
+      } else {
 #pragma unroll
       for (int gi = 0; gi < GPS; ++gi) {
         if (gi < ng) {
@@ -812,15 +861,18 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
           }
         }
       }
+      }
       float blk[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) blk[i] = blk2[0][i] + blk2[1][i];
-      // columns 2t, 2t+1 = segments 2t, 2t+1 of the stage
+      // Column c = 2t + h holds the stage's segment (c - s0) mod NSEG: s0 is the stage's first
+      // segment with prebuilt fragments (absolute columns), 0 when masked in the loop.
       const int nseg = ng * 8 / SPS;
+      const int s0 = p.pre ? (c0 * (8 / SPS)) % NSEG : 0;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int sg = 2 * t + h;
-        if (sg < nseg) {
+        const int sg = (2 * t + h - s0 + NSEG) % NSEG;
+        if (2 * t + h < NSEG && sg < nseg) {
           const int lb = (sg * SEG) >> p.bs_log2;  // the stage starts on a block boundary
           const float4 F = segf[(c0 * G) / SEG + sg];
           const float s_g = scale_to_f32(sc, lb * kScaleRows + rl, p.st_bytes, p.st_bf16);
@@ -837,6 +889,10 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty(s));
+    if (++s == S) {
+      s = 0;
+      ph ^= 1u;
+    }
 
     // end of this CTA's piece of row tile rt
     if (!p.clu && (c0 + ng == p.groups || u == u1)) {
@@ -948,11 +1004,15 @@ struct GemvPlan {
   int mode, ksplit, groups_per_split, ctas_n, stages, stage_bytes, sc_off, zc_off, act_off,
       seg_off, bar_off, sk, smem, items;
   // M = 1 stream-K (mode kM1)
-  int units, spr, maxp, grid, ctas_per_sm, dyn = 0, clu = 0, gpc = 0;
+  int units, spr, maxp, grid, ctas_per_sm, dyn = 0, clu = 0, gpc = 0, pre = 0, bf_off = 0;
   int64_t ws_floats;  // split-K / stream-K partials (0: none)
 };
 
 constexpr int kM1 = 3;
+// M = 1 shared-memory tail: 2 x kMaxStages mbarriers, the abort flag, two stage tags per stage.
+constexpr int kM1Tail = 8 * 2 * kMaxStages + 16 + 8 * kMaxStages;
+// Prebuilt B fragments of one 128-k group: 8 slices x 32 lanes x 8 bytes.
+constexpr int kBfGroupBytes = 8 * 32 * 8;
 
 // CTA that owns unit u when `units` units are split evenly over `grid` CTAs (host copy).
 static int owner_of(int64_t u, int64_t units, int64_t grid) { return (int)(((u + 1) * grid - 1) / units); }
@@ -971,21 +1031,24 @@ static bool plan_m1(const Weight& w, GemvPlan& pl) {
   const int kr = (int)w.groups * G;
   const int act_bytes = (kr * 2 + 15) / 16 * 16;
   const int seg_bytes = (kr / seg) * 16;
-  const int fixed = act_bytes + seg_bytes + 8 * 2 * kMaxStages + 32;
-  // three CTAs per SM when three stages fit in a third of the shared memory, else two
-  int stages = std::min(kMaxStages, (kSmemBudget3 - fixed) / pl.stage_bytes);
-  pl.ctas_per_sm = 3;
-  if (stages < 3) {
-    stages = std::min(kMaxStages, (kSmemBudget - fixed) / pl.stage_bytes);
-    pl.ctas_per_sm = 2;
-  }
+  const int fixed = act_bytes + seg_bytes + kM1Tail;
+  // Shared memory: the ring, the staged activations, the segment factors, the prebuilt B
+  // fragments of `bf_groups` groups, then barriers, the abort flag and the stage tags.
+  auto layout = [&](int stages, int bf_groups) {
+    pl.stages = stages;
+    pl.act_off = stages * pl.stage_bytes;
+    pl.seg_off = pl.act_off + act_bytes;
+    pl.bf_off = pl.seg_off + seg_bytes;
+    pl.bar_off = pl.bf_off + bf_groups * kBfGroupBytes;
+    pl.smem = pl.bar_off + kM1Tail;
+  };
+  // the most stages that fit with `extra` bytes of fragments
+  auto stages_with = [&](int extra) { return std::min(kMaxStages, (kSmemBudget - fixed - extra) / pl.stage_bytes); };
+  int stages = stages_with(0);
+  pl.ctas_per_sm = 2;
   if (stages < 2) return false;
   pl.mode = kM1;
-  pl.stages = stages;
-  pl.act_off = stages * pl.stage_bytes;
-  pl.seg_off = pl.act_off + act_bytes;
-  pl.bar_off = pl.seg_off + seg_bytes;
-  pl.smem = pl.bar_off + 8 * 2 * kMaxStages + 32;  // barriers, abort flag, stage tags
+  layout(stages, 0);
   pl.sk = kr + 16;
   pl.ctas_n = (int)(w.n_pad / kRows);
   pl.spr = (int)w.groups;
@@ -1001,6 +1064,15 @@ static bool plan_m1(const Weight& w, GemvPlan& pl) {
     pl.maxp = std::max(pl.maxp, pieces);
   }
   pl.ws_floats = pl.maxp > 1 ? (int64_t)pl.ctas_n * pl.maxp * kRows : 0;
+  // Prebuilt fragments (hand-out mode) when they leave the ring at least three stages (or all
+  // it had). The other modes use each fragment once, so building them would only add a step.
+  auto try_pre = [&](int bf_groups) {
+    const int sp = stages_with(bf_groups * kBfGroupBytes);
+    if (sp >= 2 && sp >= std::min(3, stages)) {
+      pl.pre = 1;
+      layout(sp, bf_groups);
+    }
+  };
   // Many row tiles per CTA (the lm_head): whole row tiles in arrival order instead of an even
   // static split, so the CTAs that get more memory bandwidth take more tiles and the call ends
   // with its CTAs together; no partial sums. Uses counters[0..1].
@@ -1008,6 +1080,7 @@ static bool plan_m1(const Weight& w, GemvPlan& pl) {
   if (pl.dyn) {
     pl.maxp = 1;
     pl.ws_floats = 0;
+    try_pre((int)w.groups);
     return true;
   }
   // Few row tiles (decode-sized calls): a row tile's K split over a cluster of up to 8 CTAs whose
@@ -1026,14 +1099,12 @@ static bool plan_m1(const Weight& w, GemvPlan& pl) {
   if (best > 0) {
     pl.clu = best;
     pl.gpc = (int)((w.groups + best - 1) / best);
-    pl.stages = std::max(1, (pl.gpc + gps - 1) / gps);
-    pl.act_off = pl.stages * pl.stage_bytes;
-    pl.seg_off = pl.act_off + act_bytes;
-    pl.bar_off = pl.seg_off + seg_bytes;
-    pl.smem = pl.bar_off + 8 * 2 * kMaxStages + 32;
+    const int need = std::max(1, (pl.gpc + gps - 1) / gps);
+    layout(need, 0);
     pl.grid = pl.ctas_n * best;
     pl.maxp = 1;
     pl.ws_floats = 0;
+    return true;
   }
   return true;
 }
@@ -1301,6 +1372,8 @@ static tq4_status gemv_launch(const Weight& w, const void* a, int64_t m, tq4_dty
   args.spr = pl.spr;
   args.maxp = pl.maxp;
   args.dyn = pl.dyn;
+  args.pre = pl.pre;
+  args.bf_off = pl.bf_off;
   args.clu = pl.clu;
   args.gpc = pl.gpc;
   if (pro && pro->mode) {
