@@ -167,6 +167,20 @@ __device__ __forceinline__ float act_factor(int k) {
   return 1.f;
 }
 
+// 1 / act_factor (a power of two).
+template <int BITS, bool BF, bool PRECISE>
+__device__ __forceinline__ float act_factor_inv(int k) {
+  if constexpr (BF) return 1.f;
+  if constexpr (BITS == 4 && PRECISE) return 16.f;
+  if constexpr (BITS == 4) return (k & 2) ? 16.f : 1.f;
+  if constexpr (BITS == 2 && PRECISE) return 1.f;
+  if constexpr (BITS == 2) {
+    const int i = 2 * ((k >> 4) & 1) + ((k >> 1) & 1);
+    return i == 0 ? 1.f : (i == 1 ? 4.f : (i == 2 ? 16.f : 64.f));
+  }
+  return 1.f;
+}
+
 template <bool BF>
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -273,17 +287,18 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int
       for (int off = 1; off < L; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
       float e_scale = 1.f, inv = 1.f;
       if (mx > 0.f && mx <= 3.402823466e38f) {
-        int ex;
-        frexpf(mx, &ex);                             // mx = f * 2^ex, f in [0.5, 1)
+        // mx = f * 2^ex with f in [0.5, 1): ex = biased exponent - 126 (subnormals clamp below)
+        const int ex = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 126;
         const int s = max(-126, min(127, ex - 15));  // mx / 2^s in [2^14, 2^15)
-        e_scale = ldexpf(1.f, s);
-        inv = ldexpf(1.f, -s);
+        e_scale = __uint_as_float((uint32_t)(s + 127) << 23);
+        inv = s < 127 ? __uint_as_float((uint32_t)(127 - s) << 23) : 5.8774717541e-39f;  // 2^-s
       }
       uint16_t h[4];
       float sv = 0.f, sa = 0.f;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float c = act_factor<BITS, BF, PRECISE>(kk + e);  // kk: a multiple of 4
+        const float c_inv = act_factor_inv<BITS, BF, PRECISE>(kk + e);
         float val;
         if constexpr (BF) {
           const __nv_bfloat16 b = __float2bfloat16_rn(a4[u][e] * inv * c);
@@ -295,7 +310,7 @@ __device__ __forceinline__ void stage_activations(const GemvArgs& p, int k0, int
           val = __half2float(b);
         }
         sv += val;
-        sa += val / c;  // exact: c is a power of two
+        sa += val * c_inv;  // exact: c is a power of two
       }
       for (int off = 1; off < L; off <<= 1) {
         sv += __shfl_xor_sync(0xffffffffu, sv, off);
@@ -681,9 +696,18 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
       };
       if (p.dyn) {
         // Row tile blockIdx.x first (prefetched before the previous kernel finishes), then the
-        // tiles gridDim.x, gridDim.x + 1, ... in arrival order: CTAs that stream faster take more.
+        // tiles gridDim.x, gridDim.x + 1, ... in ticket order: CTAs that stream faster take more.
         // A stage's tag is its (row tile, first group); row tile -1 says there is no more work.
-        int rt = blockIdx.x;
+        // Every CTA takes tickets until one fails, so a call takes exactly ctas_n tickets
+        // (ctas_n - gridDim.x tiles, gridDim.x failures): the taker of ticket ctas_n - 1 is the
+        // call's last and puts the counter back to zero for the next call on the stream. The
+        // next ticket is taken when a tile's first stage is issued, off the issue path.
+        auto take = [&]() {
+          const int v = atomicAdd(&p.counters[0], 1);
+          if (v == p.ctas_n - 1) p.counters[0] = 0;
+          return (int)gridDim.x + v;
+        };
+        int rt = blockIdx.x, next = 0;
         bool waited = false, ok = true;
         while (ok) {
           if (rt >= p.ctas_n) {  // no work left: a stage that only says so
@@ -700,12 +724,14 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
             sinfo[2 * s + 1] = c0;
             issue(s, rt, c0, min(GPS, p.groups - c0));
             advance();
+            if (c0 == 0 && waited) next = take();
           }
           if (!waited) {
-            pdl_wait();  // the counters belong to the stream's order
+            pdl_wait();  // the counter belongs to the stream's order
             waited = true;
+            next = take();
           }
-          rt = gridDim.x + atomicAdd(&p.counters[0], 1);
+          rt = next;
         }
       } else {
         int rt = u0 / p.groups, c0 = u0 - rt * p.groups;
@@ -952,19 +978,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
     return;
   }
 
-  if (p.dyn) {
-    // The producer's last (failed) take preceded the stage that stopped the consumers, so when
-    // every CTA has counted itself here no take is left: the last one resets the counters.
-    consumer_sync();
-    if (threadIdx.x == 0) {
-      __threadfence();
-      if (atomicAdd(&p.counters[1], 1) == (int)gridDim.x - 1) {
-        p.counters[0] = 0;
-        p.counters[1] = 0;
-      }
-    }
-    return;
-  }
+  if (p.dyn) return;  // the producer's last ticket put the counter back
 
   // Publish the shared pieces: after a consumer barrier one thread fences (making every
   // consumer's partial stores visible) and counts the arrivals; the last CTA of a row tile sums
@@ -1075,7 +1089,7 @@ static bool plan_m1(const Weight& w, GemvPlan& pl) {
   };
   // Many row tiles per CTA (the lm_head): whole row tiles in arrival order instead of an even
   // static split, so the CTAs that get more memory bandwidth take more tiles and the call ends
-  // with its CTAs together; no partial sums. Uses counters[0..1].
+  // with its CTAs together; no partial sums. Uses counters[0].
   pl.dyn = pl.ctas_n >= 2 * pl.grid;
   if (pl.dyn) {
     pl.maxp = 1;
@@ -1387,7 +1401,7 @@ static tq4_status gemv_launch(const Weight& w, const void* a, int64_t m, tq4_dty
     args.pro_eps = pro->eps;
   }
   args.n_pad = w.n_pad;
-  const int nctr = pl.dyn ? 2 : (pl.ws_floats > 0 ? pl.ctas_n : 0);
+  const int nctr = pl.dyn ? 1 : (pl.ws_floats > 0 ? pl.ctas_n : 0);
   if (pl.ws_floats > 0 || nctr > 0) {
     if ((pl.ws_floats > 0 && (ws == nullptr || pl.ws_floats > ws_capacity_floats)) || counters == nullptr ||
         nctr > ctr_capacity) {
@@ -1432,10 +1446,10 @@ tq4_status run_gemv_fused(const Weight& w, const float* x, const float* x2, cons
 }
 
 // Counters a call uses (zero-initialised, left at zero by the kernel): one per row tile for split
-// partial sums, two for the M = 1 row-tile hand-out, none otherwise.
+// partial sums, one for the M = 1 row-tile hand-out, none otherwise.
 int64_t gemv_counter_count(const Weight& w, int64_t m) {
   const GemvPlan pl = plan_gemv(w, m);
-  return pl.dyn ? 2 : (pl.ws_floats > 0 ? pl.ctas_n : 0);
+  return pl.dyn ? 1 : (pl.ws_floats > 0 ? pl.ctas_n : 0);
 }
 
 tq4_status run_gemv(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,
