@@ -299,6 +299,41 @@ def test_device_status_clean():
     assert device_status() == 0
 
 
+HANDOUT_M1 = [
+    # K, N, bs, zp, scale type, A type, T, bias: N >= 592 row tiles, the row-tile hand-out
+    (1024, 76011, 32, "none", "f32", "f32", "f32", False),
+    (1024, 76160, 32, "packed", "f16", "f16", "f16", True),
+    (2048, 76800, 16, "float", "f32", "f32", "f32", False),
+    (512, 77000, 32, "none", "bf16", "bf16", "bf16", False),
+    (1000, 76100, 32, "packed", "f32", "bf16", "f32", True),
+    (4096, 75800, 32, "none", "f16", "f32", "f16", False),
+]
+
+
+@pytest.mark.parametrize("k,n,bs,zp,st,at,t,bias", HANDOUT_M1)
+def test_m1_row_tile_hand_out(k, n, bs, zp, st, at, t, bias):
+    """M = 1 with many row tiles per CTA (the lm_head shape) takes whole row tiles by ticket and
+    multiplies with B fragments prebuilt during the activation staging: every activation type,
+    blocks of 16 and 32, zero points, bias, ragged N and K. Against an fp64 product over the
+    bit-exact dequantized weight; back-to-back calls give the same bits (no partial sums)."""
+    cfg = workloads.Config(f"tc-{k}-{n}-{bs}-{zp}-{st}-{at}", k, n, 1, bits=4, block_size=bs, scale_type=st,
+                           zp=zp, a_type=at, bias=bias)
+    p = workloads.make(cfg)
+    w = weight_for(cfg, p, t)
+    a = to_dev(p["A"], at)
+    bias_t = to_dev(p["bias"], at) if bias else None
+    ys = [w.matmul(a, bias_t) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert torch.equal(ys[0], ys[1]) and torch.equal(ys[0], ys[2])
+    want = a.double() @ w.dequantize().double().T
+    if bias:
+        want = want + bias_t.double()
+    y = ys[0].double()
+    assert torch.isfinite(y).all()
+    assert ((y - want).norm() / want.norm()).item() < TOL[at]
+    assert device_status() == 0
+
+
 def test_lm_head_row_tiles_handed_out_in_arrival_order():
     """The 151936-row lm_head at M = 1 hands whole row tiles to CTAs through an arrival counter
     that the last CTA resets: back-to-back calls on one handle (the next call's prefetch overlaps
