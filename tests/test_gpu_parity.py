@@ -194,6 +194,10 @@ LARGE_M = [
     (2048, 384, 200, 4, 128, "packed", "f16", "f16", "f16", True),
     (1024, 512, 130, 4, 64, "packed", "bf16", "bf16", "bf16", False),
     (512, 320, 33, 8, 32, "float", "f16", "f16", "f16", False),
+    # K split over a cluster of 8 CTAs (few weight-row tiles): f16 with zero points, and f32 A /
+    # f32 weights (row scale and weight exponent applied after the cross-CTA sum) with bias
+    (4096, 1024, 256, 4, 128, "packed", "f16", "f16", "f16", False),
+    (4096, 640, 100, 4, 32, "none", "f32", "f32", "f32", True),
 ]
 
 

@@ -169,6 +169,7 @@ struct GemmArgs {
   int64_t ldy;
   const float* row_scale;  // per activation row factor of an f32 A carried as scaled f16, or null
   const int32_t* wexp;     // per weight row exponent of f32 weights carried as scaled f16 / bf16, or null
+  int ks;                  // CTAs splitting K in a cluster (1: none)
 };
 
 constexpr int kDeqWarps = 16;      // dequantising / epilogue warps: 4 per TMEM lane quarter
@@ -211,8 +212,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * WN, m0 = blockIdx.y * TM;
-  const int KT = p.ktiles;
+  // Split K: the ks CTAs of a cluster (consecutive along x) take consecutive k-tile ranges.
+  int kr = 0, n0 = blockIdx.x * WN, kt0 = 0, KT = p.ktiles;  // this CTA's k-tiles: [kt0, kt0 + KT)
+  const int m0 = blockIdx.y * TM;
+  if (p.ks > 1) {
+    kr = blockIdx.x % p.ks;
+    n0 = (blockIdx.x / p.ks) * WN;
+    kt0 = p.ktiles * kr / p.ks;
+    KT = p.ktiles * (kr + 1) / p.ks - kt0;
+  }
   const uint32_t tx_a = L::ACT_BYTES;
   const uint32_t tx_w = L::WP_BYTES + WN * p.nb * p.st_bytes * (p.has_zp ? 2 : 1);
 
@@ -252,9 +260,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int pre = min(S, KT);
       for (int kt = 0; kt < pre; ++kt) {
         const uint32_t st = base + kt * p.stage_bytes;
-        const int b0 = (kt * 128) >> p.bs_log2;
+        const int b0 = ((kt0 + kt) * 128) >> p.bs_log2;
         mbar_expect_tx(wfull(kt), tx_w);
-        tma_load_2d(st + L::ACT_BYTES, &map_w, kt * 64, n0, wfull(kt));
+        tma_load_2d(st + L::ACT_BYTES, &map_w, (kt0 + kt) * 64, n0, wfull(kt));
         tma_load_2d(st + p.sc_off, &map_s, n0, b0, wfull(kt));
         if (p.has_zp) tma_load_2d(st + p.zc_off, &map_z, n0, b0, wfull(kt));
       }
@@ -262,8 +270,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int kt = 0; kt < pre; ++kt) {
         const uint32_t st = base + kt * p.stage_bytes;
         mbar_expect_tx(full(kt), tx_a);
-        tma_load_2d(st, &map_a, kt * 128, m0, full(kt));
-        tma_load_2d(st + L::ACT_BYTES / 2, &map_a, kt * 128 + 64, m0, full(kt));
+        tma_load_2d(st, &map_a, (kt0 + kt) * 128, m0, full(kt));
+        tma_load_2d(st + L::ACT_BYTES / 2, &map_a, (kt0 + kt) * 128 + 64, m0, full(kt));
       }
       int issued = pre;
       for (int kt = pre; kt < KT; ++kt) {
@@ -271,14 +279,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t ph = (kt / S) & 1;
         if (!mbar_wait(empty(s), ph ^ 1, abort_flag, kDevTimeoutStageEmpty)) break;
         const uint32_t st = base + s * p.stage_bytes;
-        const int b0 = (kt * 128) >> p.bs_log2;
+        const int b0 = ((kt0 + kt) * 128) >> p.bs_log2;
         mbar_expect_tx(wfull(s), tx_w);
-        tma_load_2d(st + L::ACT_BYTES, &map_w, kt * 64, n0, wfull(s));
+        tma_load_2d(st + L::ACT_BYTES, &map_w, (kt0 + kt) * 64, n0, wfull(s));
         tma_load_2d(st + p.sc_off, &map_s, n0, b0, wfull(s));
         if (p.has_zp) tma_load_2d(st + p.zc_off, &map_z, n0, b0, wfull(s));
         mbar_expect_tx(full(s), tx_a);
-        tma_load_2d(st, &map_a, kt * 128, m0, full(s));
-        tma_load_2d(st + L::ACT_BYTES / 2, &map_a, kt * 128 + 64, m0, full(s));
+        tma_load_2d(st, &map_a, (kt0 + kt) * 128, m0, full(s));
+        tma_load_2d(st + L::ACT_BYTES / 2, &map_a, (kt0 + kt) * 128 + 64, m0, full(s));
         issued = kt + 1;
       }
       // the copies still in flight complete before the CTA exits (bounded)
@@ -329,13 +337,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint4 v = *reinterpret_cast<const uint4*>(st + L::ACT_BYTES + r * 64 + ((tp ^ ((r >> 1) & 3)) << 4));
       const uint8_t* sc = st + p.sc_off;
       const uint8_t* zc = st + p.zc_off;
-      const int b0 = (kt * 128) >> p.bs_log2;
+      const int b0 = ((kt0 + kt) * 128) >> p.bs_log2;
       const uint32_t col0 = lane_addr + TM + a * 64 + 2 * tp;  // column 8j + 2tp holds k = 16j + 4tp, +1
       uint32_t s2 = 0, oz2 = 0, oz16n = 0;
       float scv = 0.f, z = 0.f;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int lb = ((kt * 128 + 16 * j) >> p.bs_log2) - b0;  // staged block row
+        const int lb = (((kt0 + kt) * 128 + 16 * j) >> p.bs_log2) - b0;  // staged block row
         const bool new_block = (j == 0) || (((16 * j) & ((1 << p.bs_log2) - 1)) == 0);
         const uint32_t x = (j < 2) ? v.x : (j < 4) ? v.y : (j < 6) ? v.z : v.w;
         uint32_t w0, w1;
@@ -401,8 +409,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const bool n_ok = n < p.N;
     const float bias_v = (p.bias && n_ok) ? load_as_f32(p.bias, n, p.bias_t) : 0.f;
     const bool run = __all_sync(0xffffffffu, ok && !*abort_flag);
-    if (run) {
-      constexpr int CPW = TM / 4;  // activation rows (TMEM columns) per warp
+    constexpr int CPW = TM / 4;  // activation rows (TMEM columns) per warp
+    if (run && p.ks > 1) {  // split K: this CTA's raw sums, [TM][128] f32, for the cluster to add
+#pragma unroll 1
+      for (int c = tp * CPW; c < (tp + 1) * CPW; c += 8) {
+        uint32_t rr[8];
+        tmem_ld8(lane_addr + c, rr);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) reinterpret_cast<float*>(smem)[(c + i) * WN + r] = __uint_as_float(rr[i]);
+      }
+    } else if (run) {
 #pragma unroll 1
       for (int c = tp * CPW; c < (tp + 1) * CPW; c += 8) {
         uint32_t rr[8];
@@ -422,7 +438,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     asm volatile("bar.sync 1, %0;" ::"n"(32 * kDeqWarps) : "memory");
-    if (run) {
+    if (run && p.ks == 1) {
       const int rows = min(TM, p.M - m0);
       const int cpr = WN * ys / 16;  // 16-byte chunks per tile row
       const int epc = 16 / ys;       // elements per chunk
@@ -447,6 +463,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kTmemCols));
+  }
+  if (p.ks > 1) {
+    // Every CTA of the cluster has its raw [TM][128] sums in shared memory. Rank kr adds the
+    // ranks' sums of activation rows [kr TM / ks, (kr + 1) TM / ks) in rank order (the result
+    // does not depend on scheduling), finishes them like the single-CTA epilogue (weight-row
+    // exponent, activation-row scale, bias) and stores Y. The second barrier keeps every CTA's
+    // shared memory alive until all ranks have read it.
+    cluster_sync_all();
+    const float* part = reinterpret_cast<const float*>(smem);
+    const int rows = min(TM, p.M - m0);
+    const int r_lo = kr * TM / p.ks, r_hi = min(rows, (kr + 1) * TM / p.ks);
+    const int units = max(0, r_hi - r_lo) * (WN / 4);
+    for (int i = threadIdx.x; i < units; i += kGemmThreads) {
+      const int ml = r_lo + i / (WN / 4), c = (i % (WN / 4)) * 4;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int q = 0; q < p.ks; ++q) {
+        const float4 x = ld_cluster_f32x4(part + ml * WN + c, (unsigned)q);
+        v[0] += x.x;
+        v[1] += x.y;
+        v[2] += x.z;
+        v[3] += x.w;
+      }
+      const float rs = p.row_scale ? p.row_scale[m0 + ml] : 1.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int64_t n = (int64_t)n0 + c + e;
+        if (n >= p.N) break;
+        float y = v[e];
+        if (T == TQ4_F32 && p.wexp) y = ldexpf(y, p.wexp[n]);
+        y *= rs;  // a power of two: exact
+        if (p.bias) y = round_to(y, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
+        store_from_f32(p.y, (int64_t)(m0 + ml) * p.ldy + n, p.y_t, y);
+      }
+    }
+    cluster_sync_all();
   }
 }
 
@@ -610,8 +661,27 @@ static tq4_status launch_gemm_t(const CUtensorMap& ma, const Weight& w, GemmArgs
     TQ4_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
     attr_set = true;
   }
-  const dim3 grid((args.N + WN - 1) / WN, (args.M + TM - 1) / TM);
-  TQ4_CUDA(launch_pdl(kern, grid, dim3(kGemmThreads), pl.smem, st, ma, w.wmaps[0], w.smaps[0], w.zmaps[0], args));
+  const dim3 grid(((args.N + WN - 1) / WN) * args.ks, (args.M + TM - 1) / TM);
+  if (args.ks == 1) {
+    TQ4_CUDA(launch_pdl(kern, grid, dim3(kGemmThreads), pl.smem, st, ma, w.wmaps[0], w.smaps[0], w.zmaps[0], args));
+    return TQ4_OK;
+  }
+  // split K: a cluster of ks CTAs along x, plus the dependent launch
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = args.ks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  TQ4_CUDA(cudaLaunchKernelEx(&cfg, kern, ma, w.wmaps[0], w.smaps[0], w.zmaps[0], args));
   return TQ4_OK;
 }
 
@@ -635,13 +705,32 @@ static bool gemm_eligible(const Weight& w, const void* a, tq4_dtype a_t) {
 
 // Activation rows per CTA: no wider than M needs, and the largest tile that still gives half the
 // SMs a tile.
-static int choose_tm(const Weight& w, int64_t m) {
+// When that leaves only a 64- or 32-row tile (each weight row dequantised again for every narrow
+// activation tile), the widest tile with K split over a cluster of ks CTAs instead (ks a power
+// of two up to 8, tiles x ks within one wave, at least 4 k-tiles per CTA).
+static int choose_tm(const Weight& w, int64_t m, int* ks) {
   const int64_t nt = (w.desc.N + WN - 1) / WN;
+  *ks = 1;
+  int narrow = 32;
   for (int tm : {256, 128, 64}) {
     if (tm / 2 >= m) continue;  // the half-size tile already covers M
-    if (((m + tm - 1) / tm) * nt >= w.num_sms / 2) return tm;
+    if (((m + tm - 1) / tm) * nt >= w.num_sms / 2) {
+      if (tm >= 128) return tm;
+      narrow = tm;
+      break;
+    }
   }
-  return 32;
+  for (int tm : {256, 128, 64}) {
+    if (tm / 2 >= m) continue;
+    const int64_t tiles = ((m + tm - 1) / tm) * nt;
+    int k = 1;
+    while (k < 8 && tiles * k * 2 <= w.num_sms && w.groups / (k * 2) >= 4) k *= 2;
+    if (k > 1) {
+      *ks = k;
+      return tm;
+    }
+  }
+  return narrow;
 }
 
 tq4_status run_gemm_tc(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,
@@ -658,7 +747,8 @@ tq4_status run_gemm_tc(const Weight& w, const void* a, int64_t m, tq4_dtype a_t,
     a_t = TQ4_F16;
     row_scale = rs;
   }
-  const int tm = choose_tm(w, m);
+  int ks = 1;
+  const int tm = choose_tm(w, m, &ks);
   CUtensorMap ma;
   const CUtensorMapDataType adt = a_t == TQ4_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   TQ4_TRY(make_map(&ma, adt, a, w.desc.K, m, w.desc.K * 2, 64, tm, CU_TENSOR_MAP_SWIZZLE_128B));
@@ -680,6 +770,7 @@ tq4_status run_gemm_tc(const Weight& w, const void* a, int64_t m, tq4_dtype a_t,
   args.ldy = ldy;
   args.row_scale = row_scale;
   args.wexp = static_cast<const int32_t*>(w.wexp.ptr);
+  args.ks = ks;
   const bool bf = a_t == TQ4_BF16;
   switch (tm) {
     case 256: return bf ? launch_gemm_tm<256, true>(ma, w, args, st) : launch_gemm_tm<256, false>(ma, w, args, st);

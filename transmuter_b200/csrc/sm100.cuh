@@ -101,6 +101,17 @@ __device__ __forceinline__ float ld_cluster_f32(const float* local, unsigned ran
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
   return v;
 }
+// 16 bytes of another cluster rank's shared memory at the address of `local` in this CTA's.
+__device__ __forceinline__ float4 ld_cluster_f32x4(const float* local, unsigned rank) {
+  uint32_t addr = smem_u32(local), remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(addr), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
+  return v;
+}
 __device__ __forceinline__ unsigned cluster_ctarank() {
   unsigned r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
