@@ -290,3 +290,47 @@ def test_attention_decode_rope_matches_separate_steps(pos):
     assert o.rel_l2(out1.double().cpu().numpy(), out2.double().cpu().numpy()) < 1e-5
     assert o.rel_l2(kc1[:, pos].double().cpu().numpy(), kc2[:, pos].double().cpu().numpy()) < 1e-6
     assert torch.equal(vc1, vc2)
+
+
+@pytest.mark.parametrize("n,offset,kind", [(151936, 0, "ties"), (151937, 1, "nan"), (1000, 3, "ties"),
+                                           (7, 0, "neg_inf"), (152000, 2, "plain")])
+def test_argmax_advance_rule(n, offset, kind):
+    """tq4_argmax_advance: greedy next token = the lowest index among equal maxima, NaN never wins
+    (all -inf gives index 0), a forced token wins over the argmax; the log and position advance.
+    Ties across the scanning CTAs' slices, odd n and unaligned logits pointers included."""
+    lib = _lib.load()
+    dev = torch.device("cuda:0")
+    r = np.random.default_rng(n + offset)
+    x = r.standard_normal(n + offset).astype(np.float32)
+    v = x[offset:]
+    if kind == "ties":
+        top = np.float32(9.0)
+        for i in (n - 1, n // 3, n // 2 + 1, 5):
+            v[i] = top
+    elif kind == "nan":
+        v[r.integers(0, n, 50)] = np.nan
+        v[n - 2] = np.float32(7.5)
+    elif kind == "neg_inf":
+        v[:] = -np.inf
+    # first occurrence of the maximum = the lowest index among equal maxima; NaN never wins, and
+    # an all -inf row gives index 0 (the kernel's rule)
+    want = int(np.argmax(np.where(np.isnan(v), -np.inf, v)))
+    buf = torch.from_numpy(x).to(dev)
+    logits = buf[offset:]
+    max_len = 16
+    forced = torch.full((max_len,), -1, dtype=torch.int64, device=dev)
+    forced[3] = 1234
+    pos = torch.tensor([1], dtype=torch.int32, device=dev)
+    token = torch.zeros(1, dtype=torch.int64, device=dev)
+    log = torch.full((max_len,), -7, dtype=torch.int64, device=dev)
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+    fn = lib.tq4_argmax_advance
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                   ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _lib.check(fn(vp(logits), n, vp(forced), max_len, vp(pos), vp(token), vp(log), max_len, st))
+    torch.cuda.synchronize()
+    assert int(pos.item()) == 2 and int(token.item()) == want and int(log[2].item()) == want
+    _lib.check(fn(vp(logits), n, vp(forced), max_len, vp(pos), vp(token), vp(log), max_len, st))  # forced step
+    torch.cuda.synchronize()
+    assert int(pos.item()) == 3 and int(token.item()) == 1234 and int(log[3].item()) == 1234
