@@ -170,6 +170,7 @@ struct GemmArgs {
   const float* row_scale;  // per activation row factor of an f32 A carried as scaled f16, or null
   const int32_t* wexp;     // per weight row exponent of f32 weights carried as scaled f16 / bf16, or null
   int ks;                  // CTAs splitting K in a cluster (1: none)
+  int s16;                 // f32 weights with the handle's f16 block scales (scales16): packed dequant
 };
 
 constexpr int kDeqWarps = 16;      // dequantising / epilogue warps: 4 per TMEM lane quarter
@@ -327,6 +328,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     constexpr bool T_SAME = (BF && T == TQ4_BF16) || (!BF && T == TQ4_F16);
     const int we = (T == TQ4_F32 && p.wexp) ? p.wexp[n0 + r] : 0;  // n0 + r < n_pad
+    // 2^we and 2^-we once per thread: multiplying by them rounds exactly like ldexpf while both
+    // are normal numbers; ldexpf itself for the rare rows outside that range
+    const bool pw_ok = we > -126 && we < 126;
+    const float pw_up = ldexpf(1.f, we), pw_down = ldexpf(1.f, -we);
     for (int kt = 0; kt < KT; ++kt) {
       const int s = kt % S, a = kt % kASlots;
       if (!mbar_wait(wfull(s), (kt / S) & 1, abort_flag, kDevTimeoutTmaFull)) break;
@@ -347,8 +352,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const bool new_block = (j == 0) || (((16 * j) & ((1 << p.bs_log2) - 1)) == 0);
         const uint32_t x = (j < 2) ? v.x : (j < 4) ? v.y : (j < 6) ? v.z : v.w;
         uint32_t w0, w1;
-        if (T_SAME && p.int_zp) {
+        if ((T_SAME || (T == TQ4_F32 && p.s16)) && p.int_zp) {
           // (O + q) - (O + z) is exact in the MMA type; one more multiply gives RN_T((q - z) * s)
+          // (f32 weights: times the f16 s * 2^-we of the handle's scales16)
           if (new_block) {
             const uint32_t sv = reinterpret_cast<const uint16_t*>(sc)[lb * WN + r];
             s2 = sv | (sv << 16);
@@ -371,7 +377,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         } else {
           // f32 weights: (q - z) * s * 2^-we, exact scaling of the f32 product before its rounding
           if (new_block) {
-            scv = ldexpf(scale_to_f32(sc, lb * WN + r, p.st_bytes, T == TQ4_BF16), -we);
+            const float sraw = scale_to_f32(sc, lb * WN + r, p.st_bytes, T == TQ4_BF16);
+            scv = pw_ok ? sraw * pw_down : ldexpf(sraw, -we);
             z = p.has_zp ? scale_to_f32(zc, lb * WN + r, p.st_bytes, T == TQ4_BF16) : p.z_const;
           }
           uint32_t q0, q1;
@@ -427,7 +434,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int i = 0; i < 8; ++i) {
           const int ml = c + i;
           float v = __uint_as_float(rr[i]);
-          if (we) v = ldexpf(v, we);
+          if (we) v = pw_ok ? v * pw_up : ldexpf(v, we);
           if (p.row_scale && m0 + ml < p.M) v *= p.row_scale[m0 + ml];  // a power of two: exact
           if (p.bias) v = round_to(v, p.y_t) + bias_v;
           uint8_t* dst = smem + ((int64_t)ml * WN + r) * ys;
@@ -614,6 +621,12 @@ tq4_status make_weight_maps(Weight& w) {
                      CU_TENSOR_MAP_SWIZZLE_NONE));
   else
     w.zmaps[0] = w.smaps[0];  // never loaded
+  w.s16_ok = false;
+  if (w.scales16.ptr) {
+    TQ4_TRY(make_map(&w.smap16, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.scales16.ptr, w.n_pad, w.blocks_pad, w.n_pad * 2, WN,
+                     nb, CU_TENSOR_MAP_SWIZZLE_NONE));
+    w.s16_ok = true;
+  }
   w.wmaps_ok = true;
   return TQ4_OK;
 }
@@ -625,10 +638,9 @@ struct GemmPlan {
 };
 
 template <int TM>
-static GemmPlan plan_gemm_smem(const Weight& w) {
+static GemmPlan plan_gemm_smem(const Weight& w, int st) {  // st: bytes of a staged scale
   using L = GemmTile<TM>;
   GemmPlan pl{};
-  const int st = dtype_size(w.desc.dequant_dtype);
   const int sc_bytes = WN * gemm_scale_blocks(w) * st;
   pl.sc_off = L::FIXED;
   pl.zc_off = pl.sc_off + (sc_bytes + 127) / 128 * 128;
@@ -646,7 +658,7 @@ static GemmPlan plan_gemm_smem(const Weight& w) {
 
 template <int TM, bool BF, tq4_dtype T>
 static tq4_status launch_gemm_t(const CUtensorMap& ma, const Weight& w, GemmArgs args, cudaStream_t st) {
-  const GemmPlan pl = plan_gemm_smem<TM>(w);
+  const GemmPlan pl = plan_gemm_smem<TM>(w, args.st_bytes);
   if (pl.stages < 2) {
     set_error("GEMM: the stage does not fit shared memory");
     return TQ4_ERR_UNSUPPORTED;
@@ -663,7 +675,8 @@ static tq4_status launch_gemm_t(const CUtensorMap& ma, const Weight& w, GemmArgs
   }
   const dim3 grid(((args.N + WN - 1) / WN) * args.ks, (args.M + TM - 1) / TM);
   if (args.ks == 1) {
-    TQ4_CUDA(launch_pdl(kern, grid, dim3(kGemmThreads), pl.smem, st, ma, w.wmaps[0], w.smaps[0], w.zmaps[0], args));
+    TQ4_CUDA(launch_pdl(kern, grid, dim3(kGemmThreads), pl.smem, st, ma, w.wmaps[0], args.s16 ? w.smap16 : w.smaps[0],
+                        w.zmaps[0], args));
     return TQ4_OK;
   }
   // split K: a cluster of ks CTAs along x, plus the dependent launch
@@ -681,7 +694,7 @@ static tq4_status launch_gemm_t(const CUtensorMap& ma, const Weight& w, GemmArgs
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  TQ4_CUDA(cudaLaunchKernelEx(&cfg, kern, ma, w.wmaps[0], w.smaps[0], w.zmaps[0], args));
+  TQ4_CUDA(cudaLaunchKernelEx(&cfg, kern, ma, w.wmaps[0], args.s16 ? w.smap16 : w.smaps[0], w.zmaps[0], args));
   return TQ4_OK;
 }
 
@@ -771,6 +784,9 @@ tq4_status run_gemm_tc(const Weight& w, const void* a, int64_t m, tq4_dtype a_t,
   args.row_scale = row_scale;
   args.wexp = static_cast<const int32_t*>(w.wexp.ptr);
   args.ks = ks;
+  // f32 weights without zero points under f16 activations: the f16 block scales
+  args.s16 = (w.s16_ok && a_t == TQ4_F16) ? 1 : 0;
+  if (args.s16) args.st_bytes = 2;
   const bool bf = a_t == TQ4_BF16;
   switch (tm) {
     case 256: return bf ? launch_gemm_tm<256, true>(ma, w, args, st) : launch_gemm_tm<256, false>(ma, w, args, st);

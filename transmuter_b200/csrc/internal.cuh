@@ -133,6 +133,10 @@ struct tq4_weight {
   // tensor-core GEMM carries row n's weights as f16 (q - z) * s * 2^-wexp[n] (kept in the normal
   // f16 range) and multiplies its outputs back by 2^wexp[n].
   tq4::DeviceBuffer wexp;
+  // [blocks_pad][n_pad] f16, f32 4-bit weights without zero points: RN_f16(s * 2^-wexp[n]), the
+  // tensor-core GEMM's block scales (read by TMA like 2-byte scales; one rounding more than
+  // scaling the f32 product). Empty otherwise.
+  tq4::DeviceBuffer scales16;
   int num_sms = 148;
   // split-K workspaces of the GEMV, one per CUDA stream (a tq4::WorkspaceMap, made on first use)
   void* ws_mutex = nullptr;
@@ -142,6 +146,8 @@ struct tq4_weight {
   alignas(64) CUtensorMap smaps[3];
   alignas(64) CUtensorMap zmaps[3];
   bool wmaps_ok = false;
+  alignas(64) CUtensorMap smap16;  // scales16 with the GEMM's box, when scales16 exists
+  bool s16_ok = false;
   // TMA descriptors of the GEMV: 128 packed rows x 64 bytes, and 136 rows x gv_nbs blocks of the
   // scales / zero points; gv_gps groups per pipeline stage
   alignas(64) CUtensorMap gv_wmap;

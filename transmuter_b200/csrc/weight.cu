@@ -167,19 +167,26 @@ static void launch_unpack_zp(const Weight& w, const uint8_t* zp, T* dst, cudaStr
 // (frexp exponent of that maximum; 0 for an all-zero or non-finite row).
 __global__ void row_exponent_kernel(const float* __restrict__ scales, const float* __restrict__ zps, float z_const,
                                     int64_t blocks, int64_t n, int64_t n_pad, float qmax, int32_t* __restrict__ out) {
-  const int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (r >= n_pad) return;
-  float mx = 0.f;
-  if (r < n) {
-    for (int64_t b = 0; b < blocks; ++b) {
-      const float s = fabsf(scales[b * n_pad + r]);
-      const float z = zps ? zps[b * n_pad + r] : z_const;
-      mx = fmaxf(mx, s * fmaxf(fabsf(z), fabsf(qmax - z)));
+  for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < n_pad; r += (int64_t)gridDim.x * blockDim.x) {
+    float mx = 0.f;
+    if (r < n) {
+      for (int64_t b = 0; b < blocks; ++b) {
+        const float s = fabsf(scales[b * n_pad + r]);
+        const float z = zps ? zps[b * n_pad + r] : z_const;
+        mx = fmaxf(mx, s * fmaxf(fabsf(z), fabsf(qmax - z)));
+      }
     }
+    int e = 0;
+    if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);
+    out[r] = e;
   }
-  int e = 0;
-  if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);
-  out[r] = e;
+}
+
+// The GEMM's f16 block scales of f32 weights: s * 2^-wexp[n] rounded once to f16.
+__global__ void scale16_kernel(const float* __restrict__ scales, const int32_t* __restrict__ wexp,
+                               int64_t n_pad, int64_t total, __half* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = __float2half_rn(ldexpf(scales[i], -wexp[i % n_pad]));
 }
 
 tq4_status prepare_weight(Weight& w, const void* b_src, const void* s_src, const void* zp_src) {
@@ -235,6 +242,14 @@ tq4_status prepare_weight(Weight& w, const void* b_src, const void* s_src, const
         static_cast<const float*>(w.scales.ptr), static_cast<const float*>(w.zps.ptr), w.z_const, w.blocks,
         d.N, w.n_pad, 15.f, static_cast<int32_t*>(w.wexp.ptr));
     TQ4_CUDA(cudaGetLastError());
+    if (d.zp_kind == TQ4_ZP_NONE) {
+      const int64_t total = w.n_pad * w.blocks_pad;
+      TQ4_TRY(w.scales16.alloc(total * 2));
+      scale16_kernel<<<grid_for(total, 256), 256, 0, st>>>(static_cast<const float*>(w.scales.ptr),
+                                                            static_cast<const int32_t*>(w.wexp.ptr), w.n_pad,
+                                                            total, static_cast<__half*>(w.scales16.ptr));
+      TQ4_CUDA(cudaGetLastError());
+    }
   }
   // The staging buffers are freed when this function returns; finish the kernels first.
   TQ4_CUDA(cudaStreamSynchronize(st));
