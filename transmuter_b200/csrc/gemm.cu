@@ -177,8 +177,8 @@ constexpr int kDeqWarps = 16;      // dequantising / epilogue warps: 4 per TMEM 
 constexpr int kGemmThreads = 64 + 32 * kDeqWarps;  // + the producer and MMA warps
 constexpr int WN = 128;            // weight rows per CTA: the MMA's M and the TMEM lanes
 constexpr int kMaxStages = 8;      // shared-memory stages
-constexpr int kASlots = 4;         // dequantised weight stages in TMEM, 64 columns each
-constexpr int kTmemCols = 512;
+constexpr int kASlots = 4;         // dequantised weight stages in TMEM, 64 columns each (at most)
+constexpr int kSmemSM = 233472;    // shared memory of an SM
 
 template <int TM>
 struct GemmTile {
@@ -186,11 +186,17 @@ struct GemmTile {
   static constexpr int WP_BYTES = WN * 64;        // packed
   static constexpr int FIXED = ACT_BYTES + WP_BYTES;
   static_assert(TM % 32 == 0 && TM >= 32 && TM <= 256, "MMA N");
-  static_assert(TM + kASlots * 64 <= kTmemCols, "TMEM columns");
+  // Tiles of at most 64 activation rows: 3 weight slots in 256 TMEM columns, two CTAs per SM (the
+  // second CTA's start-up and epilogue overlap the first's work); wider tiles: 4 slots, all 512
+  // columns, one CTA per SM.
+  static constexpr int SLOTS = TM <= 64 ? 3 : 4;
+  static constexpr int COLS = TM <= 64 ? 256 : 512;
+  static constexpr int CTAS = TM <= 64 ? 2 : 1;
+  static_assert(TM + SLOTS * 64 <= COLS && SLOTS <= kASlots, "TMEM columns");
 };
 
 template <int TM, bool BF, tq4_dtype T>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads, GemmTile<TM>::CTAS)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                 const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_z,
                 const GemmArgs p) {
@@ -231,7 +237,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(wfull(s), 1);
       mbar_init(empty(s), 1 + kDeqWarps);  // the MMAs' commit + the dequantising warps
     }
-    for (int a = 0; a < kASlots; ++a) {
+    for (int a = 0; a < L::SLOTS; ++a) {
       mbar_init(afull(a), kDeqWarps);
       mbar_init(aempty(a), 1);
     }
@@ -240,7 +246,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32((const void*)tmem_slot)), "r"((uint32_t)kTmemCols));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32((const void*)tmem_slot)), "r"((uint32_t)L::COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
@@ -303,9 +309,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                  ((uint32_t)(TM >> 3) << 17) | ((uint32_t)(WN >> 4) << 24);
       bool ok = true;
       for (int kt = 0; kt < KT && ok; ++kt) {
-        const int s = kt % S, a = kt % kASlots;
+        const int s = kt % S, a = kt % L::SLOTS;
         ok = mbar_wait(full(s), (kt / S) & 1, abort_flag, kDevTimeoutTmaFull) &&
-             mbar_wait(afull(a), (kt / kASlots) & 1, abort_flag, kDevTimeoutDequant);
+             mbar_wait(afull(a), (kt / L::SLOTS) & 1, abort_flag, kDevTimeoutDequant);
         if (!ok) break;
         asm volatile("tcgen05.fence::after_thread_sync;");
         const uint32_t act = base + s * p.stage_bytes;
@@ -333,9 +339,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const bool pw_ok = we > -126 && we < 126;
     const float pw_up = ldexpf(1.f, we), pw_down = ldexpf(1.f, -we);
     for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % S, a = kt % kASlots;
+      const int s = kt % S, a = kt % L::SLOTS;
       if (!mbar_wait(wfull(s), (kt / S) & 1, abort_flag, kDevTimeoutTmaFull)) break;
-      if (!mbar_wait(aempty(a), ((kt / kASlots) & 1) ^ 1, abort_flag, kDevTimeoutDequant)) break;
+      if (!mbar_wait(aempty(a), ((kt / L::SLOTS) & 1) ^ 1, abort_flag, kDevTimeoutDequant)) break;
       const uint8_t* st = smem + s * p.stage_bytes;
       // the 64-byte swizzle puts piece tp of row r at 16 * (tp ^ ((r >> 1) & 3)): the 8 lanes of
       // each load phase read 8 different bank groups
@@ -469,7 +475,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kTmemCols));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)L::COLS));
   }
   if (p.ks > 1) {
     // Every CTA of the cluster has its raw [TM][128] sums in shared memory. Rank kr adds the
@@ -647,12 +653,13 @@ static GemmPlan plan_gemm_smem(const Weight& w, int st) {  // st: bytes of a sta
   const int end = pl.zc_off + (w.zps.ptr ? sc_bytes : 0);
   pl.stage_bytes = (end + 1023) / 1024 * 1024;
   const int fixed = 1024 + 8 * (3 * kMaxStages + 2 * kASlots + 1) + 16;
-  pl.stages = std::min(kMaxStages, (kSmemLimit - fixed) / pl.stage_bytes);
+  // L::CTAS GEMM CTAs per SM, and no more: a CTA that allocates tensor memory should never share
+  // its SM with a CTA that could only sit blocked in its own allocation. Each CTA asks for more
+  // than 1 / (CTAS + 1) of the SM's shared memory (the 1 KB per CTA the runtime keeps included).
+  const int cap = L::CTAS == 1 ? kSmemLimit : kSmemSM / L::CTAS - 1024;
+  pl.stages = std::min(kMaxStages, (cap - fixed) / pl.stage_bytes);
   pl.smem = fixed + pl.stages * pl.stage_bytes;
-  // One GEMM CTA per SM: every CTA allocates all 512 TMEM columns, so a second CTA on the SM
-  // (from the next kernel on the stream, launched early) could only sit blocked in its
-  // allocation. Asking for more than half the SM's shared memory rules that out.
-  pl.smem = std::max(pl.smem, kSmemLimit / 2 + 1024);
+  pl.smem = std::max(pl.smem, kSmemSM / (L::CTAS + 1) + 1024);
   return pl;
 }
 
