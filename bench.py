@@ -153,7 +153,7 @@ def cpu_reference(cfg, p, steps, warmup, budget_s):
 # ---- our path --------------------------------------------------------------------------------
 def launches_per_call(cfg, m, sharded_world=1):
     """libtq4 kernels per call (NCCL's own kernels are not counted)."""
-    if m <= 16:
+    if m <= 8 or (m <= 16 and cfg.bits != 4):
         n = 1                                   # the GEMV
     elif cfg.bits == 4:
         n = 2 if cfg.a_type == "f32" else 1     # (row-scaled f16 copy of A) + the tcgen05 GEMM
