@@ -36,7 +36,8 @@ typedef enum {
   TQ4_ERR_NCCL = 4,             /* an NCCL call failed or NCCL is not loadable */
   TQ4_ERR_OUT_OF_MEMORY = 5,
   TQ4_ERR_TIMEOUT = 6,          /* a bounded wait (device or host) ran out */
-  TQ4_ERR_DEVICE = 7            /* a kernel reported an error through the device status word */
+  TQ4_ERR_DEVICE = 7,           /* a kernel reported an error through the device status word */
+  TQ4_ERR_IO = 8                /* a file given to tq4_weight_create_from cannot be opened or read */
 } tq4_status;
 
 typedef enum { TQ4_F32 = 0, TQ4_F16 = 1, TQ4_BF16 = 2, TQ4_U8 = 3 } tq4_dtype;
@@ -80,6 +81,30 @@ tq4_status tq4_weight_input_sizes(const tq4_weight_desc* desc, int64_t* b_bytes,
 tq4_status tq4_weight_create(const tq4_weight_desc* desc, const void* b, int64_t b_bytes,
                              const void* scales, const void* zp, int device, tq4_weight** out);
 
+/* One input of tq4_weight_create_from: bytes in memory, or an initializer whose data an ONNX
+ * model keeps in a file beside it (TensorProto data_location EXTERNAL, with the external_data
+ * entries "location", "offset" and "length"; lib/transmuter/ops.ex:680-695). */
+typedef struct {
+  const void* data;   /* host or device memory; used when path is NULL */
+  const char* path;   /* the file: the model's directory joined with "location" */
+  int64_t offset;     /* "offset" (0 when the entry is absent) */
+  int64_t length;     /* "length" in bytes; -1 when absent: from offset to the end of the file.
+                         For data, its byte count (-1: the size the descriptor implies). */
+} tq4_source;
+
+/* tq4_weight_create with each input given as a tq4_source. Replaces the read of a deferred
+ * initializer at move time (Transmuter.DeferredTensor.value/1, lib/transmuter/deferred_tensor.ex
+ * :27, read by move/2 at lib/transmuter.ex:1159, and Ops.read_external/2 at ops.ex:680-695): the
+ * file range streams to the device through a few pinned chunks, without a host copy of the
+ * tensor. Each input's byte count must be the one the descriptor implies (tq4_weight_input_sizes).
+ * A file that cannot be opened is TQ4_ERR_IO and a range past its end TQ4_ERR_INVALID_ARGUMENT,
+ * both found before any device work; a read that fails later is TQ4_ERR_IO. `zp` may be NULL when
+ * desc->zp_kind is TQ4_ZP_NONE. The handle is the one tq4_weight_create makes from the same
+ * bytes. */
+tq4_status tq4_weight_create_from(const tq4_weight_desc* desc, const tq4_source* b,
+                                  const tq4_source* scales, const tq4_source* zp, int device,
+                                  tq4_weight** out);
+
 tq4_status tq4_weight_destroy(tq4_weight* w);
 
 /* The handle's attributes and the device bytes it holds. */
@@ -88,8 +113,10 @@ tq4_status tq4_weight_info(const tq4_weight* w, tq4_weight_desc* desc, int64_t* 
 /* Replaces the MatMulNBits clause (quantized.ex:30-46) for a weight the handle holds:
  *   Y[M, N] = A[M, K] . W^T (+ bias[N]),  W = dequantize_weight(...) in desc.dequant_dtype.
  * A (a_dtype F32/F16/BF16), bias (bias_dtype; NULL for none) and Y (y_dtype) are device
- * pointers, row-major and dense. M >= 0 (M = 0 is a no-op). Calls with M <= 16 run the fused
- * unpack-dequant-GEMV kernel; larger M run the tensor-core GEMM. */
+ * pointers, row-major and dense. M >= 0 (M = 0 is a no-op). Calls with M <= 8 run the fused
+ * unpack-dequant-GEMV kernel; larger M run the tensor-core GEMM, except that calls with
+ * 9 <= M <= 16 it cannot take (bits other than 4, an A that is not 16-byte aligned) run the GEMV
+ * too. */
 tq4_status tq4_matmul(const tq4_weight* w, const void* a, int64_t m, tq4_dtype a_dtype,
                       const void* bias, tq4_dtype bias_dtype, void* y, tq4_dtype y_dtype,
                       void* stream);

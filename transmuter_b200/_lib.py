@@ -13,7 +13,7 @@ LIB_PATH = os.path.join(HERE, "libtq4.so")
 TQ4_OK = 0
 STATUS = {
     0: "ok", 1: "invalid argument", 2: "unsupported", 3: "CUDA error", 4: "NCCL error",
-    5: "out of device memory", 6: "timed out", 7: "device-side error",
+    5: "out of device memory", 6: "timed out", 7: "device-side error", 8: "file error",
 }
 F32, F16, BF16, U8 = 0, 1, 2, 3
 ZP_NONE, ZP_PACKED, ZP_FLOAT = 0, 1, 2
@@ -21,7 +21,8 @@ UNIQUE_ID_BYTES = 128
 
 # Every symbol include/tq4.h declares (the CPU tests check the library exports each one).
 EXPORTS = [
-    "tq4_weight_input_sizes", "tq4_weight_create", "tq4_weight_destroy", "tq4_weight_info",
+    "tq4_weight_input_sizes", "tq4_weight_create", "tq4_weight_create_from", "tq4_weight_destroy",
+    "tq4_weight_info",
     "tq4_matmul", "tq4_matmul_noalloc", "tq4_dequantize", "tq4_gather_rows", "tq4_device_status", "tq4_last_error",
     "tq4_status_string", "tq4_comm_unique_id", "tq4_comm_create", "tq4_comm_destroy",
     "tq4_sharded_create", "tq4_sharded_rows", "tq4_sharded_matmul", "tq4_sharded_destroy",
@@ -36,6 +37,15 @@ class WeightDesc(ctypes.Structure):
         ("K", ctypes.c_int64), ("N", ctypes.c_int64), ("bits", ctypes.c_int32),
         ("block_size", ctypes.c_int32), ("scale_dtype", ctypes.c_int), ("zp_kind", ctypes.c_int),
         ("zp_dtype", ctypes.c_int), ("dequant_dtype", ctypes.c_int),
+    ]
+
+
+class Source(ctypes.Structure):
+    """``tq4_source``: bytes in memory (``data``), or ``length`` bytes of the file ``path`` from
+    ``offset`` (-1: to the end of the file)."""
+    _fields_ = [
+        ("data", ctypes.c_void_p), ("path", ctypes.c_char_p), ("offset", ctypes.c_int64),
+        ("length", ctypes.c_int64),
     ]
 
 
@@ -66,6 +76,7 @@ def load():
         sig = {
             "tq4_weight_input_sizes": [P(WeightDesc), P(i64), P(i64), P(i64)],
             "tq4_weight_create": [P(WeightDesc), vp, i64, vp, vp, ctypes.c_int, P(vp)],
+            "tq4_weight_create_from": [P(WeightDesc), P(Source), P(Source), P(Source), ctypes.c_int, P(vp)],
             "tq4_weight_destroy": [vp],
             "tq4_weight_info": [vp, P(WeightDesc), P(i64)],
             "tq4_matmul": [vp, vp, i64, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int, vp],

@@ -75,6 +75,56 @@ static tq4_status check_desc(const tq4_weight_desc* d) {
   return TQ4_OK;
 }
 
+// The handle of a checked description and resolved inputs, on `device`.
+static tq4_status create_weight(const tq4_weight_desc* d, const Source& b, const Source& s,
+                                const Source* z, int device, tq4_weight** out, const char* fn) {
+  int ndev = 0;
+  TQ4_CUDA(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) {
+    set_error("%s: device %d out of range (%d devices)", fn, device, ndev);
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  int prev = 0;
+  TQ4_CUDA(cudaGetDevice(&prev));
+  TQ4_CUDA(cudaSetDevice(device));
+
+  tq4_weight* w = new tq4_weight();
+  w->desc = *d;
+  w->device = device;
+  w->blocks = (d->K + d->block_size - 1) / d->block_size;
+  const int64_t G = 512 / d->bits;
+  const int64_t k_valid = w->blocks * d->block_size;
+  w->k_pad = (k_valid + G - 1) / G * G;
+  w->row_bytes = w->k_pad * d->bits / 8;
+  w->groups = w->row_bytes / 64;
+  w->n_pad = (d->N + 127) / 128 * 128;
+  const int64_t bp = (w->k_pad + d->block_size - 1) / d->block_size;
+  w->blocks_pad = (bp + 7) / 8 * 8;
+  while ((1 << w->bs_log2) < d->block_size) ++w->bs_log2;
+  w->z_const = (float)(1 << (d->bits - 1));
+  cudaDeviceProp prop;
+  tq4_status st = TQ4_OK;
+  if (cudaGetDeviceProperties(&prop, device) == cudaSuccess) w->num_sms = prop.multiProcessorCount;
+  if (cudaStreamCreateWithFlags(&w->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    set_error("%s: cudaStreamCreate failed", fn);
+    st = TQ4_ERR_CUDA;
+  }
+  const int tsz = dtype_size(d->dequant_dtype);
+  if (st == TQ4_OK) st = w->q.alloc(w->n_pad * w->row_bytes);
+  if (st == TQ4_OK) st = w->scales.alloc(w->n_pad * w->blocks_pad * tsz);
+  if (st == TQ4_OK && d->zp_kind != TQ4_ZP_NONE) st = w->zps.alloc(w->n_pad * w->blocks_pad * tsz);
+  if (st == TQ4_OK) st = prepare_weight(*w, b, s, z);
+  if (st == TQ4_OK) st = make_weight_maps(*w);
+  if (st == TQ4_OK) st = make_gemv_maps(*w);
+  cudaSetDevice(prev);
+  if (st != TQ4_OK) {
+    tq4_weight_destroy(w);
+    return st;
+  }
+  *out = w;
+  return TQ4_OK;
+}
+
 }  // namespace tq4
 
 using namespace tq4;
@@ -91,6 +141,7 @@ const char* tq4_status_string(tq4_status s) {
     case TQ4_ERR_OUT_OF_MEMORY: return "out of device memory";
     case TQ4_ERR_TIMEOUT: return "timed out";
     case TQ4_ERR_DEVICE: return "device-side error";
+    case TQ4_ERR_IO: return "file error";
   }
   return "unknown status";
 }
@@ -144,51 +195,43 @@ tq4_status tq4_weight_create(const tq4_weight_desc* d, const void* b, int64_t b_
     set_error("MatMulNBits: zero points declared but not given");
     return TQ4_ERR_INVALID_ARGUMENT;
   }
-  int ndev = 0;
-  TQ4_CUDA(cudaGetDeviceCount(&ndev));
-  if (device < 0 || device >= ndev) {
-    set_error("tq4_weight_create: device %d out of range (%d devices)", device, ndev);
+  int64_t s_bytes = 0, z_bytes = 0;
+  TQ4_TRY(tq4_weight_input_sizes(d, nullptr, &s_bytes, &z_bytes));
+  Source bs, ss, zs;
+  bs.data = b;
+  bs.length = need_b;
+  ss.data = scales;
+  ss.length = s_bytes;
+  zs.data = zp;
+  zs.length = z_bytes;
+  return create_weight(d, bs, ss, d->zp_kind != TQ4_ZP_NONE ? &zs : nullptr, device, out,
+                       "tq4_weight_create");
+}
+
+tq4_status tq4_weight_create_from(const tq4_weight_desc* d, const tq4_source* b,
+                                  const tq4_source* scales, const tq4_source* zp, int device,
+                                  tq4_weight** out) {
+  clear_error();
+  if (!out) {
+    set_error("tq4_weight_create_from: null output handle");
     return TQ4_ERR_INVALID_ARGUMENT;
   }
-  int prev = 0;
-  TQ4_CUDA(cudaGetDevice(&prev));
-  TQ4_CUDA(cudaSetDevice(device));
-
-  tq4_weight* w = new tq4_weight();
-  w->desc = *d;
-  w->device = device;
-  w->blocks = (d->K + d->block_size - 1) / d->block_size;
-  const int64_t G = 512 / d->bits;
-  const int64_t k_valid = w->blocks * d->block_size;
-  w->k_pad = (k_valid + G - 1) / G * G;
-  w->row_bytes = w->k_pad * d->bits / 8;
-  w->groups = w->row_bytes / 64;
-  w->n_pad = (d->N + 127) / 128 * 128;
-  const int64_t bp = (w->k_pad + d->block_size - 1) / d->block_size;
-  w->blocks_pad = (bp + 7) / 8 * 8;
-  while ((1 << w->bs_log2) < d->block_size) ++w->bs_log2;
-  w->z_const = (float)(1 << (d->bits - 1));
-  cudaDeviceProp prop;
-  tq4_status st = TQ4_OK;
-  if (cudaGetDeviceProperties(&prop, device) == cudaSuccess) w->num_sms = prop.multiProcessorCount;
-  if (cudaStreamCreateWithFlags(&w->stream, cudaStreamNonBlocking) != cudaSuccess) {
-    set_error("tq4_weight_create: cudaStreamCreate failed");
-    st = TQ4_ERR_CUDA;
+  *out = nullptr;
+  TQ4_TRY(check_desc(d));
+  int64_t b_bytes = 0, s_bytes = 0, z_bytes = 0;
+  TQ4_TRY(tq4_weight_input_sizes(d, &b_bytes, &s_bytes, &z_bytes));
+  Source bs, ss, zs;
+  TQ4_TRY(resolve_source(b, b_bytes, "B", &bs));
+  TQ4_TRY(resolve_source(scales, s_bytes, "scales", &ss));
+  if (d->zp_kind != TQ4_ZP_NONE) {
+    if (!zp) {
+      set_error("MatMulNBits: zero points declared but not given");
+      return TQ4_ERR_INVALID_ARGUMENT;
+    }
+    TQ4_TRY(resolve_source(zp, z_bytes, "zero points", &zs));
   }
-  const int tsz = dtype_size(d->dequant_dtype);
-  if (st == TQ4_OK) st = w->q.alloc(w->n_pad * w->row_bytes);
-  if (st == TQ4_OK) st = w->scales.alloc(w->n_pad * w->blocks_pad * tsz);
-  if (st == TQ4_OK && d->zp_kind != TQ4_ZP_NONE) st = w->zps.alloc(w->n_pad * w->blocks_pad * tsz);
-  if (st == TQ4_OK) st = prepare_weight(*w, b, scales, zp);
-  if (st == TQ4_OK) st = make_weight_maps(*w);
-  if (st == TQ4_OK) st = make_gemv_maps(*w);
-  cudaSetDevice(prev);
-  if (st != TQ4_OK) {
-    tq4_weight_destroy(w);
-    return st;
-  }
-  *out = w;
-  return TQ4_OK;
+  return create_weight(d, bs, ss, d->zp_kind != TQ4_ZP_NONE ? &zs : nullptr, device, out,
+                       "tq4_weight_create_from");
 }
 
 tq4_status tq4_weight_destroy(tq4_weight* w) {

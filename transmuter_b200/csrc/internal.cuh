@@ -160,7 +160,23 @@ struct tq4_weight {
 namespace tq4 {
 using Weight = tq4_weight;
 
-tq4_status prepare_weight(Weight& w, const void* b, const void* scales, const void* zp);
+// Where one raw input of a weight comes from: `length` bytes of memory at `data` (host or device),
+// or, when `path` is set, `length` bytes of that file from `offset` (ONNX external data).
+struct Source {
+  const void* data = nullptr;
+  std::string path;
+  int64_t offset = 0;
+  int64_t length = 0;
+};
+// Checks one tq4_source against the byte count `expect` the descriptor implies, resolving a file
+// range that runs to the end of the file; `what` names the input in the message.
+tq4_status resolve_source(const tq4_source* in, int64_t expect, const char* what, Source* out);
+// Copies a source's bytes to `dst` (device memory of `device`, the current device). Memory copies
+// are queued on `st`; a file range is read by host threads and has reached the device on return.
+tq4_status fill_device(void* dst, const Source& src, int device, cudaStream_t st);
+// Stages the raw inputs on the device and rewrites them into the handle's layout; `zp` is null
+// when the weight has no zero-point input.
+tq4_status prepare_weight(Weight& w, const Source& b, const Source& scales, const Source* zp);
 tq4_status make_weight_maps(Weight& w);
 tq4_status make_gemv_maps(Weight& w);
 // A 2-D tiled TMA descriptor (cuTensorMapEncodeTiled through the runtime's driver entry point).

@@ -189,7 +189,7 @@ __global__ void scale16_kernel(const float* __restrict__ scales, const int32_t* 
     out[i] = __float2half_rn(ldexpf(scales[i], -wexp[i % n_pad]));
 }
 
-tq4_status prepare_weight(Weight& w, const void* b_src, const void* s_src, const void* zp_src) {
+tq4_status prepare_weight(Weight& w, const Source& b_src, const Source& s_src, const Source* zp_src) {
   const tq4_weight_desc& d = w.desc;
   cudaStream_t st = w.stream;
   const int64_t raw_row = w.blocks * d.block_size * d.bits / 8;
@@ -199,14 +199,18 @@ tq4_status prepare_weight(Weight& w, const void* b_src, const void* s_src, const
   if (d.zp_kind == TQ4_ZP_PACKED) zp_bytes = d.N * ((w.blocks * d.bits + 7) / 8);
   if (d.zp_kind == TQ4_ZP_FLOAT) zp_bytes = d.N * w.blocks * dtype_size(d.zp_dtype);
 
-  // Staging copies of the raw inputs (host or device memory; cudaMemcpyDefault resolves both).
+  // Staging copies of the raw inputs: memory (host or device) or file ranges.
+  if (b_src.length != b_bytes || s_src.length != s_bytes || (zp_src ? zp_src->length : 0) != zp_bytes) {
+    set_error("MatMulNBits: input sizes do not match the description");
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
   DeviceBuffer raw_b, raw_s, raw_z;
   TQ4_TRY(raw_b.alloc(b_bytes));
   TQ4_TRY(raw_s.alloc(s_bytes));
   if (zp_bytes) TQ4_TRY(raw_z.alloc(zp_bytes));
-  TQ4_CUDA(cudaMemcpyAsync(raw_b.ptr, b_src, b_bytes, cudaMemcpyDefault, st));
-  TQ4_CUDA(cudaMemcpyAsync(raw_s.ptr, s_src, s_bytes, cudaMemcpyDefault, st));
-  if (zp_bytes) TQ4_CUDA(cudaMemcpyAsync(raw_z.ptr, zp_src, zp_bytes, cudaMemcpyDefault, st));
+  TQ4_TRY(fill_device(raw_b.ptr, b_src, w.device, st));
+  TQ4_TRY(fill_device(raw_s.ptr, s_src, w.device, st));
+  if (zp_bytes) TQ4_TRY(fill_device(raw_z.ptr, *zp_src, w.device, st));
 
   const int64_t words = w.n_pad * w.row_bytes / 4;
   const int grid = grid_for(words, 256);

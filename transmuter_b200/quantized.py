@@ -11,23 +11,24 @@ Reference interface (georgeguimaraes/transmuter 2.0.0):
   lib/transmuter/emlx.ex:104-148 is the precedent for a backend-owned packed weight). Here the
   weight is a ``PackedWeight``: a tq4 handle that keeps B packed on the GPU.
 
+B, scales and zero points may be ``DeferredTensor`` values (initializers in an ONNX external
+data file, ``deferred.py``): the weight then reads their file ranges straight to the GPU.
+
 Errors follow the reference: unsupported inputs raise ``ArgumentError`` (quantized.ex:33-34).
 """
 
 import ctypes
+import math
 from dataclasses import dataclass, field
 
 import torch
 
 from . import _lib
+from .deferred import ArgumentError, DeferredTensor, shape_type
 
 TORCH_TO_TQ4 = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16, torch.uint8: _lib.U8}
 TQ4_TO_TORCH = {v: k for k, v in TORCH_TO_TQ4.items()}
 NAME_TO_TORCH = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
-
-
-class ArgumentError(ValueError):
-    """The reference's ArgumentError."""
 
 
 @dataclass
@@ -79,6 +80,23 @@ def _stream(device):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+def _nbytes(x):
+    if isinstance(x, DeferredTensor):
+        return x.nbytes
+    return x.numel() * x.element_size()
+
+
+def _source(x, nbytes):
+    """A ``tq4_source`` for a tensor (its memory) or a deferred tensor (its file range)."""
+    src = _lib.Source()
+    if isinstance(x, DeferredTensor):
+        path, offset, length = x.source()
+        src.path, src.offset, src.length = path.encode(), offset, length
+    else:
+        src.data, src.length = x.data_ptr(), nbytes
+    return src
+
+
 class PackedWeight:
     """A MatMulNBits weight held packed on one GPU by a tq4 handle (the "B:packed" value of a
     moved model). ``dtype`` is the type T it dequantizes in."""
@@ -86,43 +104,55 @@ class PackedWeight:
     def __init__(self, attrs, b, scales, zero_points=None, dtype=None, device=None):
         k, n, bits, bs = attrs
         self.k, self.n, self.bits, self.block_size = k, n, bits, bs
-        if b.dtype != torch.uint8:
-            raise ArgumentError(f"MatMulNBits B must be u8, got {b.dtype}")
-        if scales.dtype not in (torch.float32, torch.float16, torch.bfloat16):
-            raise ArgumentError(f"MatMulNBits scales must be a float tensor, got {scales.dtype}")
-        self.dtype = dtype or scales.dtype
+        b_type, s_type = shape_type(b)[1], shape_type(scales)[1]
+        z_type = shape_type(zero_points)[1] if zero_points is not None else None
+        if b_type != torch.uint8:
+            raise ArgumentError(f"MatMulNBits B must be u8, got {b_type}")
+        if s_type not in (torch.float32, torch.float16, torch.bfloat16):
+            raise ArgumentError(f"MatMulNBits scales must be a float tensor, got {s_type}")
+        self.dtype = dtype or s_type
         desc = _lib.WeightDesc()
         desc.K, desc.N, desc.bits, desc.block_size = k, n, bits, bs
-        desc.scale_dtype = TORCH_TO_TQ4[scales.dtype]
+        desc.scale_dtype = TORCH_TO_TQ4[s_type]
         desc.dequant_dtype = TORCH_TO_TQ4[self.dtype]
         if zero_points is None:
             desc.zp_kind, desc.zp_dtype = _lib.ZP_NONE, _lib.U8
-        elif zero_points.dtype == torch.uint8:
+        elif z_type == torch.uint8:
             desc.zp_kind, desc.zp_dtype = _lib.ZP_PACKED, _lib.U8
-        elif zero_points.dtype in (torch.float32, torch.float16, torch.bfloat16):
-            desc.zp_kind, desc.zp_dtype = _lib.ZP_FLOAT, TORCH_TO_TQ4[zero_points.dtype]
+        elif z_type in (torch.float32, torch.float16, torch.bfloat16):
+            desc.zp_kind, desc.zp_dtype = _lib.ZP_FLOAT, TORCH_TO_TQ4[z_type]
         else:
-            raise ArgumentError(f"MatMulNBits zero points must be u8 or float, got {zero_points.dtype}")
+            raise ArgumentError(f"MatMulNBits zero points must be u8 or float, got {z_type}")
         self.desc = desc
         if device is None:
-            device = b.device if b.is_cuda else torch.device("cuda", torch.cuda.current_device())
+            device = b.device if isinstance(b, torch.Tensor) and b.is_cuda else torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device)
         lib = _lib.load()
         sizes = [ctypes.c_int64() for _ in range(3)]
         _lib.check(lib.tq4_weight_input_sizes(ctypes.byref(desc), *[ctypes.byref(s) for s in sizes]))
         b_bytes, s_bytes, z_bytes = (s.value for s in sizes)
-        host = [x.contiguous() for x in (b, scales)] + ([zero_points.contiguous()] if zero_points is not None else [])
-        if host[0].numel() != b_bytes:
-            raise ArgumentError(f"MatMulNBits B has {host[0].numel()} bytes, expected {b_bytes}")
-        if host[1].numel() * host[1].element_size() != s_bytes:
-            raise ArgumentError(f"MatMulNBits scales have {host[1].numel()} values, expected {s_bytes // host[1].element_size()}")
-        if zero_points is not None and host[2].numel() * host[2].element_size() != z_bytes:
-            raise ArgumentError(f"MatMulNBits zero points have {host[2].numel() * host[2].element_size()} bytes, expected {z_bytes}")
+        inputs = [x if isinstance(x, DeferredTensor) else x.contiguous() for x in (b, scales)]
+        if zero_points is not None:
+            inputs.append(zero_points if isinstance(zero_points, DeferredTensor) else zero_points.contiguous())
+        got = [_nbytes(x) for x in inputs]
+        if got[0] != b_bytes:
+            raise ArgumentError(f"MatMulNBits B has {got[0]} bytes, expected {b_bytes}")
+        if got[1] != s_bytes:
+            raise ArgumentError(f"MatMulNBits scales have {got[1]} bytes, expected {s_bytes}")
+        if zero_points is not None and got[2] != z_bytes:
+            raise ArgumentError(f"MatMulNBits zero points have {got[2]} bytes, expected {z_bytes}")
         handle = ctypes.c_void_p()
-        _lib.check(lib.tq4_weight_create(
-            ctypes.byref(desc), _ptr(host[0]), b_bytes, _ptr(host[1]),
-            _ptr(host[2]) if zero_points is not None else None, self.device.index or 0,
-            ctypes.byref(handle)))
+        if any(isinstance(x, DeferredTensor) for x in inputs):
+            sources = [_source(x, nb) for x, nb in zip(inputs, got)]
+            _lib.check(lib.tq4_weight_create_from(
+                ctypes.byref(desc), ctypes.byref(sources[0]), ctypes.byref(sources[1]),
+                ctypes.byref(sources[2]) if zero_points is not None else None,
+                self.device.index or 0, ctypes.byref(handle)))
+        else:
+            _lib.check(lib.tq4_weight_create(
+                ctypes.byref(desc), _ptr(inputs[0]), b_bytes, _ptr(inputs[1]),
+                _ptr(inputs[2]) if zero_points is not None else None, self.device.index or 0,
+                ctypes.byref(handle)))
         self._handle = handle
         self._lib = lib
 
@@ -182,17 +212,20 @@ class PackedWeight:
 def packable(node, b, scales, g_idx=None):
     """``packable?/2`` (lib/transmuter.ex:1209-1225), widened: a K that is not a multiple of
     block_size is packable too (its B rows hold whole padded blocks)."""
-    if node.op_type != "MatMulNBits" or scales is None or g_idx is not None:
+    if node.op_type != "MatMulNBits" or scales is None or g_idx is not None or b is None:
         return False
     k, n, bits, bs = nbits_sizes(node)
     blocks = -(-k // bs)
-    return bits in (2, 4, 8) and b is not None and b.dtype == torch.uint8 and b.numel() == n * blocks * bs * bits // 8
+    # packed_bytes?/2 (lib/transmuter.ex:1219-1226) reads the shape and type of a tensor or of a
+    # deferred one without reading its data
+    shape, dtype = shape_type(b)
+    return bits in (2, 4, 8) and dtype == torch.uint8 and math.prod(shape) == n * blocks * bs * bits // 8
 
 
 def move_weight(node, b, scales, zero_points=None, compute_type=None, device=None):
     """The weight ``move/2`` builds for one node (lib/transmuter.ex:1155-1164,1230-1240), in the
-    scales' type after ``compute_type``."""
-    dtype = upcast(scales.dtype, compute_type)
+    scales' type after ``compute_type``. B, scales and zero points may be deferred tensors."""
+    dtype = upcast(shape_type(scales)[1], compute_type)
     return PackedWeight(nbits_sizes(node), b, scales, zero_points, dtype=dtype, device=device)
 
 
