@@ -24,6 +24,7 @@ enum DeviceCode : int32_t {
   kDevTimeoutSplitK = 0x105,      // GEMV: split-K reduction counter inconsistent
   kDevTimeoutPeer = 0x106,        // sharded exchange: a peer's slice did not arrive in time
   kDevTimeoutAttn = 0x107,        // decode attention: a K/V chunk copy did not arrive in time
+  kDevTimeoutStaged = 0x108,      // GEMV: waited too long for the activations to be staged
   kDevBadArgument = 0x200,
 };
 

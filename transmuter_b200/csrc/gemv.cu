@@ -619,7 +619,8 @@ __device__ __forceinline__ int unit_first(int b, int units, int grid) {
   return (int)((int64_t)b * units / grid);
 }
 
-template <tq4_dtype AT, int SPS>
+// HOLD (the stream-K mode): the producer issues one stage, then waits for the activations.
+template <tq4_dtype AT, int SPS, bool HOLD>
 __global__ void __launch_bounds__(kGemvThreads, 3)
     gemv_m1_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_s,
                    const __grid_constant__ CUtensorMap map_z, const GemvArgs p) {
@@ -645,6 +646,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
   auto empty = [&](int s) { return bars + 8 * (kMaxStages + s); };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + p.bar_off + 8 * 2 * kMaxStages);
   volatile int* sinfo = reinterpret_cast<volatile int*>(smem + p.bar_off + 8 * 2 * kMaxStages + 16);  // dyn
+  const uint32_t staged = bars + 8 * 2 * kMaxStages + 16 + 8 * kMaxStages;
   int u0, u1;
   if (p.dyn) {
     u0 = 0;
@@ -664,6 +666,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
       mbar_init(full(s), 1);
       mbar_init(empty(s), 8);
     }
+    if constexpr (HOLD) mbar_init(staged, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -734,12 +737,21 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
           rt = next;
         }
       } else {
+        // Stream-K shares: only the first stage is issued before the activations are staged. A
+        // share is a few stages more than the ring holds, and with the ring full the consumers'
+        // loads of the activation row queued behind the whole grid's weight copies (clock stamps:
+        // 3.5 us to stage 8 KB). Cluster shares fit their rings and are all issued at once.
         int rt = u0 / p.groups, c0 = u0 - rt * p.groups;
+        bool held = HOLD;
         for (int u = u0; u < u1;) {
           if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, kDevTimeoutStageEmpty)) break;
           const int ng = min(min(GPS, p.groups - c0), u1 - u);  // a chunk never crosses a row tile
           issue(s, rt, c0, ng);
           advance();
+          if (HOLD && held) {
+            held = false;
+            if (!mbar_wait(staged, 0, abort_flag, kDevTimeoutStaged)) break;
+          }
           u += ng;
           c0 += ng;
           if (c0 == p.groups) {
@@ -796,6 +808,9 @@ __global__ void __launch_bounds__(kGemvThreads, 3)
     }
   }
   consumer_sync();
+  if constexpr (HOLD) {
+    if (threadIdx.x == 0) mbar_arrive(staged);
+  }
 
   // Prebuilt B fragments (the lm_head's row-tile hand-out, where a CTA reuses them for every
   // row tile it takes): MMA column c takes the segments s with s % NSEG == c (an absolute
@@ -1023,8 +1038,9 @@ struct GemvPlan {
 };
 
 constexpr int kM1 = 3;
-// M = 1 shared-memory tail: 2 x kMaxStages mbarriers, the abort flag, two stage tags per stage.
-constexpr int kM1Tail = 8 * 2 * kMaxStages + 16 + 8 * kMaxStages;
+// M = 1 shared-memory tail: 2 x kMaxStages mbarriers, the abort flag, two stage tags per stage,
+// the "activations staged" mbarrier.
+constexpr int kM1Tail = 8 * 2 * kMaxStages + 16 + 8 * kMaxStages + 8;
 // Prebuilt B fragments of one 128-k group: 8 slices x 32 lanes x 8 bytes.
 constexpr int kBfGroupBytes = 8 * 32 * 8;
 
@@ -1186,9 +1202,9 @@ static GemvPlan plan_gemv(const Weight& w, int64_t m) {
   return pl;
 }
 
-template <tq4_dtype AT, int SPS>
+template <tq4_dtype AT, int SPS, bool HOLD>
 static cudaError_t launch_m1_t(const Weight& w, const GemvArgs& args, int grid, int smem, cudaStream_t st) {
-  auto kern = gemv_m1_kernel<AT, SPS>;
+  auto kern = gemv_m1_kernel<AT, SPS, HOLD>;
   static bool attr_set = false;  // once per instantiation
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 1024);
@@ -1216,14 +1232,20 @@ static cudaError_t launch_m1_t(const Weight& w, const GemvArgs& args, int grid, 
                     args);
 }
 
+template <tq4_dtype AT, bool HOLD>
+static cudaError_t launch_m1_hold(const Weight& w, const GemvArgs& args, int grid, int smem, cudaStream_t st) {
+  switch (std::min<int>(w.desc.block_size, 128) / 16) {
+    case 1: return launch_m1_t<AT, 1, HOLD>(w, args, grid, smem, st);
+    case 2: return launch_m1_t<AT, 2, HOLD>(w, args, grid, smem, st);
+    case 4: return launch_m1_t<AT, 4, HOLD>(w, args, grid, smem, st);
+    default: return launch_m1_t<AT, 8, HOLD>(w, args, grid, smem, st);
+  }
+}
+
 template <tq4_dtype AT>
 static cudaError_t launch_m1_sps(const Weight& w, const GemvArgs& args, int grid, int smem, cudaStream_t st) {
-  switch (std::min<int>(w.desc.block_size, 128) / 16) {
-    case 1: return launch_m1_t<AT, 1>(w, args, grid, smem, st);
-    case 2: return launch_m1_t<AT, 2>(w, args, grid, smem, st);
-    case 4: return launch_m1_t<AT, 4>(w, args, grid, smem, st);
-    default: return launch_m1_t<AT, 8>(w, args, grid, smem, st);
-  }
+  if (args.dyn || args.clu) return launch_m1_hold<AT, false>(w, args, grid, smem, st);
+  return launch_m1_hold<AT, true>(w, args, grid, smem, st);
 }
 
 template <int BITS, tq4_dtype AT, int MODE>
