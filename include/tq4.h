@@ -177,6 +177,12 @@ tq4_status tq4_sharded_create(const tq4_weight_desc* desc, const void* b, int64_
                               const void* scales, const void* zp, tq4_comm* comm,
                               tq4_sharded** out);
 
+/* tq4_sharded_create with each FULL input given as a tq4_source: a file range (ONNX external
+ * data) is narrowed to this rank's rows, so each rank reads only its share of the file. */
+tq4_status tq4_sharded_create_from(const tq4_weight_desc* desc, const tq4_source* b,
+                                   const tq4_source* scales, const tq4_source* zp, tq4_comm* comm,
+                                   tq4_sharded** out);
+
 /* This rank's first row and row count. */
 tq4_status tq4_sharded_rows(const tq4_sharded* s, int64_t* first, int64_t* count);
 

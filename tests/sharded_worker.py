@@ -1,7 +1,8 @@
 """One rank of the N-sharded MatMulNBits GPU test (launched by tests/test_gpu_sharded.py through
 torch.distributed.run, one process per GPU).
 
-Every rank builds the same seeded weights, takes its rows through tq4_sharded_create, runs
+Every rank builds the same seeded weights, takes its rows through tq4_sharded_create (and, for one
+weight, through tq4_sharded_create_from reading an external data file), runs
 tq4_sharded_matmul twice in a row on different inputs (its GEMV / GEMM, then the assembly of Y:
 NCCL's all-gather for small outputs, the NVLink peer exchange for slices of 4 MB and more) and
 compares the full Y with the unsharded handle on its own GPU. The columns come from
@@ -14,6 +15,7 @@ Exit status 0 when every case agrees on every rank.
 import json
 import os
 import sys
+import tempfile
 from datetime import timedelta
 
 import numpy as np
@@ -24,6 +26,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 from oracle import matmul_nbits as o  # noqa: E402
 from transmuter_b200 import sharded, workloads  # noqa: E402
+from transmuter_b200.deferred import DeferredTensor, TensorProto  # noqa: E402
 from transmuter_b200.quantized import PackedWeight  # noqa: E402
 
 CASES = [  # (K, N, M, zero points, A type, scale type)
@@ -37,6 +40,43 @@ CASES = [  # (K, N, M, zero points, A type, scale type)
     (1024, 151936, 16, "none", "f32", "f32"),
 ]
 TT = {"f32": torch.float32, "f16": torch.float16}
+
+
+def external_case(comm, rank, dev):
+    """The same weight as ONNX external data (tq4_sharded_create_from): each rank reads only its
+    rows of the file, and its Y must equal the one built from memory, bit for bit."""
+    k, n, bs = 4096, 14336, 128
+    cfg = workloads.Config("shard-gpu-external", k, n, 4, block_size=bs, zp="packed", a_type="f16", scale_type="f16")
+    p = workloads.make(cfg)
+    where = [tempfile.mkdtemp(prefix="tq4-shard-") if rank == 0 else None]
+    dist.broadcast_object_list(where, src=0)
+    d = where[0]
+    arrays = [("B", p["B"], 2), ("scales", p["scales"], 10), ("zero_points", p["zp"], 2)]
+    if rank == 0:
+        with open(os.path.join(d, "data"), "wb") as f:
+            f.write(b"\0" * 7)
+            for _, arr, _ in arrays:
+                f.write(np.ascontiguousarray(arr).tobytes())
+    dist.barrier()
+    deferred, off = [], 7
+    for i, (name, arr, ty) in enumerate(arrays):
+        entries = [("location", "data"), ("offset", str(off))] + ([("length", str(arr.nbytes))] if i < 2 else [])
+        deferred.append(DeferredTensor.new(TensorProto(name, list(arr.shape), ty, "EXTERNAL", entries), d))
+        off += arr.nbytes
+    mem = [torch.from_numpy(np.ascontiguousarray(arr)).to(dev) for _, arr, _ in arrays]
+    a = torch.from_numpy(np.ascontiguousarray(p["A"])).to(dev)
+    sw_f = sharded.ShardedWeight(comm, (k, n, 4, bs), *deferred, dtype=torch.float16)
+    sw_m = sharded.ShardedWeight(comm, (k, n, 4, bs), *mem, dtype=torch.float16)
+    y_f, y_m = sw_f.matmul(a), sw_m.matmul(a)
+    torch.cuda.synchronize()
+    exact = torch.equal(y_f, y_m) and (sw_f.first, sw_f.count) == (sw_m.first, sw_m.count)
+    sw_f.close()
+    sw_m.close()
+    dist.barrier()
+    if rank == 0:
+        os.remove(os.path.join(d, "data"))
+        os.rmdir(d)
+    return ("shard-gpu-external", 0.0 if exact else 1.0, 0.5)
 
 
 def main():
@@ -67,6 +107,7 @@ def main():
         worst.append((cfg.name, err, 1e-6 if at == "f32" else 1e-4))
         sw.close()
         pw.close()
+    worst.append(external_case(comm, rank, dev))
     comm.close()
     ok = all(e < tol for _, e, tol in worst)
     flags = torch.tensor([int(ok)])

@@ -156,3 +156,10 @@ def test_packed_weight_checks_deferred_sizes_before_the_device(files):
     with pytest.raises(_lib.Tq4Error, match="past the end"):
         PackedWeight((64, 8, 4, 16), b, s_far, device="cuda:0")
     assert os.path.getsize(files / "data") == 384
+
+
+def test_sharded_create_from_checks_arguments():
+    lib = _lib.load()
+    h = ctypes.c_void_p()
+    assert lib.tq4_sharded_create_from(None, None, None, None, None, ctypes.byref(h)) == 1
+    assert "null argument" in _lib.last_error() and not h.value

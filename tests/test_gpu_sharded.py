@@ -13,6 +13,7 @@ import torch
 
 from oracle import matmul_nbits as o
 from transmuter_b200 import sharded, workloads
+from transmuter_b200.deferred import DeferredTensor, TensorProto
 from transmuter_b200.quantized import PackedWeight
 
 pytestmark = pytest.mark.gpu
@@ -38,6 +39,30 @@ def test_one_rank_sharded_equals_unsharded(m):
     assert o.rel_l2(y_sh.double().cpu().numpy(), ref) < 5e-3
     sw.close()
     pw.close()
+    comm.close()
+
+
+def test_one_rank_sharded_from_external_data(tmp_path):
+    """tq4_sharded_create_from: the rank's rows read from an external data file give the Y of
+    the same rows given in memory."""
+    dev = torch.device("cuda:0")
+    cfg = workloads.Config("shard-one-external", 1024, 3000, 3, zp="packed", a_type="f16", scale_type="f16")
+    p = workloads.make(cfg)
+    arrays = [("B", p["B"], 2), ("scales", p["scales"], 10), ("zero_points", p["zp"], 2)]
+    blob, deferred = bytearray(b"\1" * 5), []
+    for name, arr, ty in arrays:
+        entries = [("location", "data"), ("offset", str(len(blob))), ("length", str(arr.nbytes))]
+        deferred.append(DeferredTensor.new(TensorProto(name, list(arr.shape), ty, "EXTERNAL", entries), str(tmp_path)))
+        blob += np.ascontiguousarray(arr).tobytes()
+    (tmp_path / "data").write_bytes(bytes(blob))
+    a = torch.from_numpy(p["A"]).to(dev)
+    comm = sharded.Comm(sharded.Comm.unique_id(), 1, 0, 0, timeout_ms=30000)
+    sw_f = sharded.ShardedWeight(comm, (1024, 3000, 4, 32), *deferred, dtype=torch.float16)
+    sw_m = sharded.ShardedWeight(comm, (1024, 3000, 4, 32), *[torch.from_numpy(x).to(dev) for _, x, _ in arrays],
+                                 dtype=torch.float16)
+    assert torch.equal(sw_f.matmul(a), sw_m.matmul(a))
+    sw_f.close()
+    sw_m.close()
     comm.close()
 
 

@@ -25,7 +25,7 @@ EXPORTS = [
     "tq4_weight_info",
     "tq4_matmul", "tq4_matmul_noalloc", "tq4_dequantize", "tq4_gather_rows", "tq4_device_status", "tq4_last_error",
     "tq4_status_string", "tq4_comm_unique_id", "tq4_comm_create", "tq4_comm_destroy",
-    "tq4_sharded_create", "tq4_sharded_rows", "tq4_sharded_matmul", "tq4_sharded_destroy",
+    "tq4_sharded_create", "tq4_sharded_create_from", "tq4_sharded_rows", "tq4_sharded_matmul", "tq4_sharded_destroy",
     # include/tq4_decoder.h
     "tq4_add_rmsnorm", "tq4_qk_norm_rope", "tq4_attention_decode", "tq4_attention_decode_rope",
     "tq4_matmul_fused", "tq4_silu_mul", "tq4_argmax_advance",
@@ -88,6 +88,7 @@ def load():
             "tq4_comm_create": [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P(vp)],
             "tq4_comm_destroy": [vp],
             "tq4_sharded_create": [P(WeightDesc), vp, i64, vp, vp, vp, P(vp)],
+            "tq4_sharded_create_from": [P(WeightDesc), P(Source), P(Source), P(Source), vp, P(vp)],
             "tq4_sharded_rows": [vp, P(i64), P(i64)],
             "tq4_sharded_matmul": [vp, vp, i64, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int, vp],
             "tq4_sharded_destroy": [vp],

@@ -410,6 +410,18 @@ tq4_status tq4_comm_destroy(tq4_comm* c) {
   return TQ4_OK;
 }
 
+// A sharded handle without its local weight: this rank's share of the N rows.
+static tq4_sharded* new_sharded(const tq4_weight_desc* d, tq4_comm* comm) {
+  tq4_sharded* s = new tq4_sharded();
+  s->comm = comm;
+  s->desc = *d;
+  const int64_t P = comm->nranks;
+  s->share = ((d->N + P - 1) / P + 15) / 16 * 16;
+  s->first = std::min<int64_t>(d->N, comm->rank * s->share);
+  s->count = std::min<int64_t>(d->N - s->first, s->share);
+  return s;
+}
+
 tq4_status tq4_sharded_create(const tq4_weight_desc* d, const void* b, int64_t b_bytes,
                               const void* scales, const void* zp, tq4_comm* comm,
                               tq4_sharded** out) {
@@ -425,13 +437,7 @@ tq4_status tq4_sharded_create(const tq4_weight_desc* d, const void* b, int64_t b
               (long long)b_bytes, (long long)need_b);
     return TQ4_ERR_INVALID_ARGUMENT;
   }
-  tq4_sharded* s = new tq4_sharded();
-  s->comm = comm;
-  s->desc = *d;
-  const int64_t P = comm->nranks;
-  s->share = ((d->N + P - 1) / P + 15) / 16 * 16;
-  s->first = std::min<int64_t>(d->N, comm->rank * s->share);
-  s->count = std::min<int64_t>(d->N - s->first, s->share);
+  tq4_sharded* s = new_sharded(d, comm);
   if (s->count > 0) {
     const int64_t blocks = (d->K + d->block_size - 1) / d->block_size;
     const int64_t raw_row = blocks * d->block_size * d->bits / 8;
@@ -443,6 +449,58 @@ tq4_status tq4_sharded_create(const tq4_weight_desc* d, const void* b, int64_t b
     if (d->zp_kind == TQ4_ZP_PACKED) zb = static_cast<const uint8_t*>(zp) + s->first * ((blocks * d->bits + 7) / 8);
     if (d->zp_kind == TQ4_ZP_FLOAT) zb = static_cast<const uint8_t*>(zp) + s->first * blocks * dtype_size(d->zp_dtype);
     tq4_status st = tq4_weight_create(&ld, bb, s->count * raw_row, sb, zb, comm->device, &s->local);
+    if (st != TQ4_OK) {
+      delete s;
+      return st;
+    }
+  }
+  *out = s;
+  return TQ4_OK;
+}
+
+tq4_status tq4_sharded_create_from(const tq4_weight_desc* d, const tq4_source* b,
+                                   const tq4_source* scales, const tq4_source* zp, tq4_comm* comm,
+                                   tq4_sharded** out) {
+  if (!out || !comm || !d) {
+    set_error("tq4_sharded_create_from: null argument");
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  *out = nullptr;
+  int64_t b_bytes = 0, s_bytes = 0, z_bytes = 0;
+  TQ4_TRY(tq4_weight_input_sizes(d, &b_bytes, &s_bytes, &z_bytes));
+  // The full inputs are checked (files, ranges, sizes) on every rank before any device work.
+  Source fb, fs, fz;
+  TQ4_TRY(resolve_source(b, b_bytes, "B", &fb));
+  TQ4_TRY(resolve_source(scales, s_bytes, "scales", &fs));
+  const bool has_zp = d->zp_kind != TQ4_ZP_NONE;
+  if (has_zp) {
+    if (!zp) {
+      set_error("MatMulNBits: zero points declared but not given");
+      return TQ4_ERR_INVALID_ARGUMENT;
+    }
+    TQ4_TRY(resolve_source(zp, z_bytes, "zero points", &fz));
+  }
+  tq4_sharded* s = new_sharded(d, comm);
+  if (s->count > 0) {
+    // Every input is N rows of equal size, so this rank's rows are one contiguous range of each:
+    // a file range is narrowed, and the rank reads only its rows.
+    auto rows_of = [&](const Source& src, int64_t total) {
+      const int64_t row = total / d->N;
+      tq4_source t{};
+      if (src.path.empty()) {
+        t.data = static_cast<const uint8_t*>(src.data) + s->first * row;
+      } else {
+        t.path = src.path.c_str();
+        t.offset = src.offset + s->first * row;
+      }
+      t.length = s->count * row;
+      return t;
+    };
+    tq4_weight_desc ld = *d;
+    ld.N = s->count;
+    const tq4_source lb = rows_of(fb, b_bytes), ls = rows_of(fs, s_bytes);
+    const tq4_source lz = has_zp ? rows_of(fz, z_bytes) : tq4_source{};
+    const tq4_status st = tq4_weight_create_from(&ld, &lb, &ls, has_zp ? &lz : nullptr, comm->device, &s->local);
     if (st != TQ4_OK) {
       delete s;
       return st;

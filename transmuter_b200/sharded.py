@@ -4,6 +4,8 @@
 Each rank owns ``share`` = ceil(N/P) rounded up to 16 rows of B, scales and zero points, computes
 its columns of Y, and an NCCL all-gather over NVLink builds Y on every rank. The row plan below
 is the same arithmetic as ``csrc/sharded.cu`` (kept here so the bookkeeping is testable on CPU).
+B, scales and zero points may be deferred tensors (ONNX external data): each rank then reads only
+its rows of the files (``tq4_sharded_create_from``).
 """
 
 import ctypes
@@ -11,7 +13,8 @@ import ctypes
 import torch
 
 from . import _lib
-from .quantized import TORCH_TO_TQ4, ArgumentError, _ptr, _stream
+from .deferred import DeferredTensor
+from .quantized import TORCH_TO_TQ4, ArgumentError, _nbytes, _ptr, _source, _stream
 
 
 def shard_share(n, nranks):
@@ -81,12 +84,21 @@ class ShardedWeight:
         self.k, self.n, self.comm = k, n, comm
         self.device = torch.device("cuda", comm.device)
         lib = _lib.load()
-        b = b.contiguous()
-        scales = scales.contiguous()
-        zero_points = zero_points.contiguous() if zero_points is not None else None
         handle = ctypes.c_void_p()
-        _lib.check(lib.tq4_sharded_create(ctypes.byref(desc), _ptr(b), b.numel(), _ptr(scales),
-                                          _ptr(zero_points), comm._handle, ctypes.byref(handle)))
+        inputs = [b, scales] + ([zero_points] if zero_points is not None else [])
+        if any(isinstance(x, DeferredTensor) for x in inputs):
+            # ONNX external data: each rank reads only its rows of the files
+            sources = [_source(x if isinstance(x, DeferredTensor) else x.contiguous(), _nbytes(x)) for x in inputs]
+            _lib.check(lib.tq4_sharded_create_from(
+                ctypes.byref(desc), ctypes.byref(sources[0]), ctypes.byref(sources[1]),
+                ctypes.byref(sources[2]) if zero_points is not None else None, comm._handle,
+                ctypes.byref(handle)))
+        else:
+            b = b.contiguous()
+            scales = scales.contiguous()
+            zero_points = zero_points.contiguous() if zero_points is not None else None
+            _lib.check(lib.tq4_sharded_create(ctypes.byref(desc), _ptr(b), b.numel(), _ptr(scales),
+                                              _ptr(zero_points), comm._handle, ctypes.byref(handle)))
         self._handle, self._lib = handle, lib
         first, count = ctypes.c_int64(), ctypes.c_int64()
         _lib.check(lib.tq4_sharded_rows(handle, ctypes.byref(first), ctypes.byref(count)))
