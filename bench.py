@@ -16,7 +16,8 @@ through the public API with A copied from pinned host memory and Y read back eac
 
 `--impl reference` times the reference's arithmetic on the host cores instead (the CPU oracle's
 moved-weight path: weights dequantized once as lib/transmuter.ex:1230-1240 does, then a dense
-f32 BLAS product per call, as EXLA's CPU client runs a moved model).
+f32 BLAS product per call, as EXLA's CPU client runs a moved model; `cpu_baseline.in_graph` also
+times the per-call unpack + dequantize path of a model that was not moved).
 """
 
 import argparse
@@ -150,6 +151,34 @@ def cpu_reference(cfg, p, steps, warmup, budget_s):
     return metric_value(cfg, sec), len(times), sample
 
 
+def in_graph(cfg, p, budget_s=8.0):
+    """The in-graph CPU figure as a cpu_baseline entry (the headline value stays the faster
+    moved-weight path)."""
+    v, n, sample = cpu_in_graph(cfg, p, budget_s)
+    return {"value": v, "unit": cfg.metric, "calls": n, "sample": sample}
+
+
+def cpu_in_graph(cfg, p, budget_s):
+    """The oracle's in-graph path on the host cores: each call unpacks and dequantizes W in A's
+    type (quantized.ex:42, packed.ex:9-36), then the f32 BLAS A @ W^T. This is what a model that
+    was not moved runs per call. At least one call; further calls while within budget_s.
+    Returns (value in the metric's unit, calls timed, sample text)."""
+    from oracle import matmul_nbits as o
+    a32 = np.ascontiguousarray(np.asarray(p["A"], np.float32))
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while not times or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        w = o.dequantize_weight(p["B"], p["scales"], p["zp"], cfg.k, cfg.n, cfg.bits, cfg.block_size, cfg.a_type)
+        y = a32 @ np.asarray(w, np.float32).T
+        times.append(time.perf_counter() - t0)
+        del w, y
+    sec = sum(times) / len(times)
+    sample = (f"oracle in-graph path (unpack + dequantize in {cfg.a_type} every call, then numpy/BLAS "
+              f"f32 A@W^T), {len(times)} calls of the full {cfg.m}x{cfg.k}x{cfg.n} workload")
+    return metric_value(cfg, sec), len(times), sample
+
+
 # ---- our path --------------------------------------------------------------------------------
 def launches_per_call(cfg, m, sharded_world=1):
     """libtq4 kernels per call (NCCL's own kernels are not counted)."""
@@ -197,7 +226,8 @@ def main():
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded; shapes and distributions of the config)", "config": config,
                 "cpu_baseline": {"value": value, "unit": cfg.metric, "cores": cores, "kind": "port",
-                                 "sample": sample + f" ({n_timed} of {steps} steps timed)"},
+                                 "sample": sample + f" ({n_timed} of {steps} steps timed)",
+                                 "in_graph": in_graph(cfg, p)},
                 "e2e": {"value": value, "unit": cfg.metric, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
@@ -373,7 +403,7 @@ def main():
         if world == 1 and not args.no_cpu_baseline:
             v, n_timed, sample = cpu_reference(cfg, p, 50, 1, budget_s=20.0)
             line["cpu_baseline"] = {"value": v, "unit": cfg.metric, "cores": blas_threads(), "kind": "port",
-                                    "sample": sample}
+                                    "sample": sample, "in_graph": in_graph(cfg, p)}
         print(json.dumps(line), flush=True)
 
     for w in weights:
