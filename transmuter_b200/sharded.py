@@ -29,6 +29,14 @@ def shard_rows(n, nranks, rank):
     return first, min(n - first, share)
 
 
+def shard_range(offset, total_bytes, n, nranks, rank):
+    """(offset, length) of rank ``rank``'s rows within an input of N equal rows stored from
+    ``offset`` in a file: the narrowing ``tq4_sharded_create_from`` applies to external data."""
+    row = total_bytes // n
+    first, count = shard_rows(n, nranks, rank)
+    return offset + first * row, count * row
+
+
 def unshard(gathered, m, n, nranks):
     """[P, M, share] (the all-gather order) -> [M, N]."""
     share = shard_share(n, nranks)
