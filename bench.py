@@ -1,23 +1,29 @@
 """Benchmark of the B200 MatMulNBits hot path (libtq4) on the north-star configs.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c3m1] [--impl ours|reference]
 
 A step is one MatMulNBits call (one pass of the hot path over one batch of activations). The
-default workload is the prefill-shaped config (C2: A f16 [512, 1024], K=1024, N=3072, 4-bit,
-block 32, f16 scales, packed zero points; metric TFLOP/s). Other workloads: c1 (decode, M=1,
-GB/s), c3m1 / c3m64 (151936-column lm_head, GB/s; N-sharded when run on several GPUs, Y
-assembled over NVLink), c5-<K>x<N>-m<M> (Llama-3-8B shapes), c4 (the q4 decoder, tok/s).
+default workload is the lm_head-shaped config C3 at M = 1 (A f32 [1, 1024], K=1024, N=151936,
+4-bit, block 32, f32 scales, no zero points; metric HBM GB/s), the first metric the north star
+names. Under ``--gpus N`` (torchrun, one rank per GPU) it runs N-sharded: each rank holds 1/N of
+the weight rows and Y is assembled on every rank over NVLink (strong scaling). Other workloads:
+c1 (decode, M=1, GB/s), c2 (prefill M=512, TFLOP/s), c3m64, c5-<K>x<N>-m<M> (Llama-3-8B shapes;
+N-sharded under --gpus N), c4 (the q4 decoder, tok/s; independent replicas under --gpus N).
 
-Timing: W untimed warm-up steps, then exactly K steps between barriers and synchronizes, timed
-with CUDA events on the launching stream; max over ranks. Consecutive steps rotate over R
-independent copies of (weights, A, Y) whose total exceeds twice the L2, so no step reads
-another step's data from L2. `value` has the inputs resident in HBM; `e2e` times the same calls
-through the public API with A copied from pinned host memory and Y read back each step.
+Timing: W untimed warm-up steps; the K steps are captured in one CUDA graph, which is replayed
+back to back (a replay holds K steps, or a multiple of K when K steps take under 2 ms) until the
+timed region lasts at least one second, between barriers and synchronizes; CUDA events on the
+launching stream, max over ranks; the line gives the replays and the calls timed. Consecutive
+steps rotate over R independent copies of (weights, A, Y) whose total exceeds twice the L2, so no
+step reads another step's data from L2. `value` has the inputs resident in HBM; `e2e` times the
+same calls through the public API with A copied from pinned host memory and Y read back each step.
 
 `--impl reference` times the reference's arithmetic on the host cores instead (the CPU oracle's
 moved-weight path: weights dequantized once as lib/transmuter.ex:1230-1240 does, then a dense
 f32 BLAS product per call, as EXLA's CPU client runs a moved model; `cpu_baseline.in_graph` also
-times the per-call unpack + dequantize path of a model that was not moved).
+times the per-call unpack + dequantize path of a model that was not moved). CPU figures are the
+median of at least 20 calls after 3 warm-up calls (fewer calls, stated in the sample, when one
+call exceeds the time budget).
 """
 
 import argparse
@@ -44,7 +50,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="c2")
+    ap.add_argument("--workload", default="c3m1")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -128,26 +134,30 @@ def blas_threads():
 
 def cpu_reference(cfg, p, steps, warmup, budget_s):
     """The oracle's moved-weight path on the host cores: W dequantized once (not timed), then a
-    dense f32 A @ W^T per call. Returns (value in the metric's unit, calls timed, sample text)."""
+    dense f32 A @ W^T per call. `warmup` (at least 3) untimed calls, then `steps` (at least 20)
+    timed calls, fewer only when the calls would exceed budget_s (at least 3). Returns (value in
+    the metric's unit from the MEDIAN call time, calls timed, sample text)."""
     from oracle import matmul_nbits as o
     t = cfg.scale_type
     w = o.dequantize_weight(p["B"], p["scales"], p["zp"], cfg.k, cfg.n, cfg.bits, cfg.block_size, t)
     w32 = np.ascontiguousarray(w.astype(np.float32))
+    del w
     a32 = np.ascontiguousarray(np.asarray(p["A"], np.float32))
-    for _ in range(max(1, warmup)):
+    for _ in range(max(3, warmup)):
         a32 @ w32.T
+    want = max(20, steps)
     times = []
     t_end = time.perf_counter() + budget_s
-    for _ in range(steps):
+    for _ in range(want):
         t0 = time.perf_counter()
         y = a32 @ w32.T
         times.append(time.perf_counter() - t0)
-        if time.perf_counter() > t_end:
+        if len(times) >= 3 and time.perf_counter() > t_end:
             break
-    sec = sum(times) / len(times)
+    sec = statistics.median(times)
     del y
-    sample = (f"oracle moved-weight path (dequantize once, then numpy/BLAS f32 A@W^T), "
-              f"{len(times)} calls of the full {cfg.m}x{cfg.k}x{cfg.n} workload")
+    sample = (f"oracle moved-weight path (dequantize once, then numpy/BLAS f32 A@W^T): median of "
+              f"{len(times)} calls after {max(3, warmup)} warm-up calls, full {cfg.m}x{cfg.k}x{cfg.n} workload")
     return metric_value(cfg, sec), len(times), sample
 
 
@@ -161,22 +171,47 @@ def in_graph(cfg, p, budget_s=8.0):
 def cpu_in_graph(cfg, p, budget_s):
     """The oracle's in-graph path on the host cores: each call unpacks and dequantizes W in A's
     type (quantized.ex:42, packed.ex:9-36), then the f32 BLAS A @ W^T. This is what a model that
-    was not moved runs per call. At least one call; further calls while within budget_s.
-    Returns (value in the metric's unit, calls timed, sample text)."""
+    was not moved runs per call. At least one call; further calls while within budget_s (at most
+    20). Returns (value in the metric's unit from the median call, calls timed, sample text)."""
     from oracle import matmul_nbits as o
     a32 = np.ascontiguousarray(np.asarray(p["A"], np.float32))
     times = []
     t_end = time.perf_counter() + budget_s
-    while not times or time.perf_counter() < t_end:
+    while not times or (time.perf_counter() < t_end and len(times) < 20):
         t0 = time.perf_counter()
         w = o.dequantize_weight(p["B"], p["scales"], p["zp"], cfg.k, cfg.n, cfg.bits, cfg.block_size, cfg.a_type)
         y = a32 @ np.asarray(w, np.float32).T
         times.append(time.perf_counter() - t0)
         del w, y
-    sec = sum(times) / len(times)
+    sec = statistics.median(times)
     sample = (f"oracle in-graph path (unpack + dequantize in {cfg.a_type} every call, then numpy/BLAS "
-              f"f32 A@W^T), {len(times)} calls of the full {cfg.m}x{cfg.k}x{cfg.n} workload")
+              f"f32 A@W^T): median of {len(times)} calls of the full {cfg.m}x{cfg.k}x{cfg.n} workload")
     return metric_value(cfg, sec), len(times), sample
+
+
+def workload_config(cfg, world):
+    """The `config` of both arms' lines (identical, so the two arms name the same run): the
+    workload, how the GPU arm splits it over `world` GPUs and how it keeps steps out of L2."""
+    sharded = sharded_workload(cfg, world)
+    per_copy = cfg.algorithmic_bytes() / (world if sharded else 1)
+    copies = rotation_copies(per_copy)
+    if sharded:
+        par = f"N-sharded over {world} GPUs (each rank 1/{world} of the weight rows); Y assembled on every rank over NVLink"
+    else:
+        par = "single GPU" if world == 1 else f"{world} independent replicas (dp{world})"
+    return {"workload": cfg.name, "M": cfg.m, "K": cfg.k, "N": cfg.n, "bits": cfg.bits,
+            "block_size": cfg.block_size, "scales": cfg.scale_type, "zero_points": cfg.zp,
+            "activations": cfg.a_type, "parallelism": par,
+            "l2": f"rotating {copies} copies of weights+A+Y per GPU ({copies * per_copy / 2**20:.0f} MiB > 2x L2)"}
+
+
+def sharded_workload(cfg, world):
+    """C3 and C5 are N-sharded across the GPUs; the others run independent replicas."""
+    return world > 1 and cfg.name.startswith(("c3", "c5"))
+
+
+def rotation_copies(per_copy_bytes):
+    return min(64, max(2, int(np.ceil(2 * L2_BYTES / per_copy_bytes))))
 
 
 # ---- our path --------------------------------------------------------------------------------
@@ -209,9 +244,8 @@ def main():
     if args.workload not in workloads.CONFIGS:
         raise SystemExit(f"unknown workload {args.workload}; one of {sorted(workloads.CONFIGS)}")
     cfg = workloads.CONFIGS[args.workload]
-    config = {"workload": cfg.name, "M": cfg.m, "K": cfg.k, "N": cfg.n, "bits": cfg.bits,
-              "block_size": cfg.block_size, "scales": cfg.scale_type, "zero_points": cfg.zp,
-              "activations": cfg.a_type, "parallelism": "single" if world == 1 else None}
+    config = workload_config(cfg, world)
+    sharded_run = sharded_workload(cfg, world)
 
     if args.impl == "reference":
         if rank != 0:
@@ -220,13 +254,13 @@ def main():
         p = workloads.make(cfg)
         value, n_timed, sample = cpu_reference(cfg, p, steps, args.warmup, budget_s=120.0)
         cores = blas_threads()
-        config["parallelism"] = "host cores"
-        line = {"impl": "reference", "metric": METRIC, "value": value, "unit": cfg.metric, "n_gpus": args.gpus,
+        line = {"impl": "reference", "metric": METRIC, "value": value, "unit": cfg.metric, "n_gpus": world,
                 "steps": steps, "warmup": args.warmup, "ms_per_step": metric_to_ms(cfg, value),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-                "data": "synthetic (seeded; shapes and distributions of the config)", "config": config,
+                "higher_is_better": True, "scaling": "strong" if sharded_run else "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic (seeded; shapes and distributions of the config)",
+                "config": config,
                 "cpu_baseline": {"value": value, "unit": cfg.metric, "cores": cores, "kind": "port",
-                                 "sample": sample + f" ({n_timed} of {steps} steps timed)",
+                                 "sample": sample + " (the whole workload on the host cores of rank 0)",
                                  "in_graph": in_graph(cfg, p)},
                 "e2e": {"value": value, "unit": cfg.metric, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
@@ -244,7 +278,6 @@ def main():
     from transmuter_b200 import sharded as shd
     TT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
 
-    sharded_run = world > 1 and args.workload.startswith(("c3", "c5"))
     # weak scaling (independent batches per rank) unless the workload is N-sharded
     p = workloads.make(cfg, seed_name=cfg.name if (world == 1 or sharded_run) else f"{cfg.name}/rank{rank}")
 
@@ -257,18 +290,13 @@ def main():
     attrs = (cfg.k, cfg.n, cfg.bits, cfg.block_size)
     zp_t = cfg.scale_type if cfg.zp == "float" else None
     per_copy = cfg.algorithmic_bytes() / (world if sharded_run else 1)
-    copies = max(2, int(np.ceil(2 * L2_BYTES / per_copy)))
-    copies = min(copies, 64)
+    copies = rotation_copies(per_copy)
     comm = None
     if sharded_run:
         uid = shd.Comm.unique_id() if rank == 0 else bytes(128)
         obj = [uid]
         dist.broadcast_object_list(obj, src=0)
         comm = shd.Comm(obj[0], world, rank, local_rank, timeout_ms=120000)
-        config["parallelism"] = (f"N-sharded over {world} GPUs; Y assembled by NVLink peer loads "
-                                 f"(slices >= 4 MB) or NCCL all-gather")
-    else:
-        config["parallelism"] = "single GPU" if world == 1 else f"{world} independent replicas (dp{world})"
     weights, acts, outs = [], [], []
     b_d, s_d, z_d = to_dev(p["B"]), to_dev(p["scales"], cfg.scale_type), to_dev(p["zp"], zp_t)
     for i in range(copies):
@@ -279,7 +307,6 @@ def main():
         acts.append(to_dev(p["A"], cfg.a_type))
         outs.append(torch.empty((cfg.m, cfg.n), dtype=TT[cfg.a_type], device=dev))
     del b_d, s_d, z_d
-    config["l2"] = f"rotating {copies} copies of weights+A+Y ({copies * per_copy / 2**20:.0f} MiB > 2x L2)"
     stream = torch.cuda.current_stream(dev)
 
     def step(i):
@@ -290,26 +317,30 @@ def main():
         if world > 1:
             dist.barrier()
 
-    # calibration for a default step count (about one second of timed work)
-    for i in range(max(3, args.warmup)):
+    def agree(x, op):
+        """The same value on every rank (every rank takes the same steps)."""
+        if world > 1:
+            t = torch.tensor([x], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=op)
+            x = t.item()
+        return x
+
+    for i in range(max(3, args.warmup)):  # warm-up steps
         step(i)
     torch.cuda.synchronize()
-    if args.steps is None:
-        t0 = time.perf_counter()
-        for i in range(20):
-            step(i)
-        torch.cuda.synchronize()
-        est = (time.perf_counter() - t0) / 20
-        steps = int(min(20000, max(50, 1.0 / max(est, 1e-6))))
-        if world > 1:
-            t = torch.tensor([steps], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MIN)
-            steps = int(t.item())
-    else:
-        steps = args.steps
+    # per-step time estimate: sizes the default K and the replay count
+    t0 = time.perf_counter()
+    for i in range(20):
+        step(i)
+    torch.cuda.synchronize()
+    est = agree((time.perf_counter() - t0) / 20, dist.ReduceOp.MAX)
+    steps = args.steps or int(min(20000, max(50, 0.05 / max(est, 1e-7))))
+    # One replay holds the K steps, or the smallest multiple of K that takes 2 ms, so the graph
+    # launch between replays stays a small share of the region.
+    per_replay = steps * max(1, int(np.ceil(0.002 / max(steps * est, 1e-9))))
 
-    # The K timed steps are one CUDA graph (the calls are launch-bound at small sizes); the
-    # graph's stream is warmed first so no workspace is allocated during capture.
+    # The timed steps are one CUDA graph (the calls are launch-bound at small sizes); the graph's
+    # stream is warmed first so no workspace is allocated during capture.
     gstream = torch.cuda.Stream(dev)
     with torch.cuda.stream(gstream):
         for i in range(max(3, args.warmup, copies)):  # every copy: its workspaces exist before capture
@@ -317,28 +348,36 @@ def main():
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=gstream):
-        for i in range(steps):
+        for i in range(per_replay):
             step(i)
     torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # one untimed replay measures the replay time; then enough replays for >= 1 s
+    barrier()
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    # (sized for 1.2 s: the measured replay is a cold one, the timed replays run warm)
+    replays = int(agree(max(1, int(np.ceil(1200.0 / max(e0.elapsed_time(e1), 1e-3)))),
+                        dist.ReduceOp.MAX))
 
     sampler = ClockSampler(local_rank)
     sampler.start()
     barrier()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    graph.replay()
+    for _ in range(replays):
+        graph.replay()
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop()
-    ms = e0.elapsed_time(e1)
+    ms_total = agree(e0.elapsed_time(e1), dist.ReduceOp.MAX)
     del graph
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t.item()
-    sec_per_call = ms / 1e3 / steps
+    timed_calls = replays * per_replay
+    ms = ms_total / timed_calls  # per step
+    sec_per_call = ms / 1e3
     units = world if not sharded_run else 1
     value = metric_value(cfg, sec_per_call) * units
 
@@ -346,7 +385,7 @@ def main():
     a_host = torch.from_numpy(np.ascontiguousarray(p["A"]))
     a_host = (a_host.to(torch.bfloat16) if cfg.a_type == "bf16" else a_host).pin_memory()
     y_host = torch.empty((cfg.m, cfg.n), dtype=TT[cfg.a_type]).pin_memory()
-    e2e_steps = max(10, min(steps, 2000))
+    e2e_steps = int(max(10, min(2000, 0.5 / max(est, 1e-7))))
     for i in range(3):
         acts[i % copies].copy_(a_host, non_blocking=True)
         step(i)
@@ -389,19 +428,24 @@ def main():
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": cfg.metric, "n_gpus": world, "steps": steps,
-                "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "replays": replays, "steps_per_replay": per_replay, "timed_steps": timed_calls,
+                "timed_region_ms": ms_total,
                 "scaling": "strong" if sharded_run else "weak", "vs_baseline": None,
                 "dtype": cfg.a_type, "data": "synthetic (seeded; shapes and distributions of the config)",
                 "config": config,
                 "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                              "frac": achieved / peak, "traffic": traffic,
-                             "peak_source": f"{pk_kind} ({'burst' if bound == 'tensor' else 'copy'})"},
+                             "peak_source": f"{pk_kind} ({'burst' if bound == 'tensor' else 'copy'})",
+                             "scope": ("one GPU's share of the whole step (its 1/N of the weight through the "
+                                       "MatMulNBits kernel, plus the assembly of Y)") if sharded_run else
+                                      "the MatMulNBits kernel (the whole step)"},
                 "e2e": {"value": e2e_value, "unit": cfg.metric,
                         "h2d_bytes_per_step": int(a_host.numel() * a_host.element_size()),
                         "d2h_bytes_per_step": int(y_host.numel() * y_host.element_size())},
-                "gpu_launches": steps * launches, "clocks": clocks}
+                "gpu_launches": timed_calls * launches, "clocks": clocks}
         if world == 1 and not args.no_cpu_baseline:
-            v, n_timed, sample = cpu_reference(cfg, p, 50, 1, budget_s=20.0)
+            v, n_timed, sample = cpu_reference(cfg, p, 20, 3, budget_s=20.0)
             line["cpu_baseline"] = {"value": v, "unit": cfg.metric, "cores": blas_threads(), "kind": "port",
                                     "sample": sample, "in_graph": in_graph(cfg, p)}
         print(json.dumps(line), flush=True)

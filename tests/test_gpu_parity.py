@@ -241,6 +241,47 @@ def test_c2_full_size():
     assert o.rel_l2(y, ref) < 5e-3
 
 
+C5_SHAPES = [(4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096)]
+
+
+@pytest.mark.parametrize("m", [1, 16, 256, 4096])
+@pytest.mark.parametrize("k,n", C5_SHAPES)
+def test_c5_full_size(k, n, m):
+    """Every Llama-shaped call that bench.py times, at its full size and with its own seeded
+    inputs (f16 scales, packed zero points, f16 A), against the oracle's MatMulNBits clause
+    (quantized.ex:30-46): M = 1 and 16 take the GEMV / narrow GEMM, M = 256 the K-split cluster
+    GEMM on the shapes with few weight-row tiles, M = 4096 the 256-row GEMM tiles. At M = 4096 the
+    oracle runs on 48 sampled activation rows (rows are independent)."""
+    cfg = workloads.CONFIGS[f"c5-{k}x{n}-m{m}"]
+    p = workloads.make(cfg)
+    w = weight_for(cfg, p, "f16")
+    y = w.matmul(to_dev(p["A"]))
+    rows = np.arange(m) if m <= 256 else np.sort(np.random.default_rng(5).choice(m, 48, replace=False))
+    ref, ref_t = o.matmul_nbits(p["attrs"], p["A"][rows], p["B"], p["scales"], p["zp"])
+    assert ref_t == "f16"
+    got = as_np32(y[torch.from_numpy(rows).to(DEV)])
+    assert np.isfinite(got).all()
+    assert o.rel_l2(got, ref) < TOL["f16"], o.rel_l2(got, ref)
+    assert device_status() == 0
+
+
+@pytest.mark.parametrize("name", ["c3m1", "c3m64"])
+def test_c3_against_oracle_on_sampled_weight_rows(name):
+    """The 151936-column lm_head at M = 1 and 64 (f32 A, f32 scales), each with its own bench seed,
+    against the oracle's MatMulNBits clause on 4096 sampled weight rows (output columns are
+    independent: the oracle gets those rows of B and of the scales, and N = 4096)."""
+    cfg = workloads.CONFIGS[name]
+    p = workloads.make(cfg)
+    w = weight_for(cfg, p, "f32")
+    y = as_np32(w.matmul(to_dev(p["A"])))
+    cols = np.sort(np.random.default_rng(11).choice(cfg.n, 4096, replace=False))
+    attrs = dict(p["attrs"], N=len(cols))
+    scales = p["scales"].reshape(cfg.n, cfg.blocks)[cols].reshape(-1)
+    ref, _ = o.matmul_nbits(attrs, p["A"], p["B"][cols], scales, None)
+    assert o.rel_l2(y[:, cols], ref) < TOL["f32"], o.rel_l2(y[:, cols], ref)
+    assert device_status() == 0
+
+
 def test_c3_lm_head_full_size_property():
     """151936 x 1024 at M = 1 and 64: Y equals A . W^T with W from tq4_dequantize (itself checked
     bit-exact against the oracle on sampled rows), in float64 on the CPU."""

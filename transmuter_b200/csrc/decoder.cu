@@ -555,12 +555,8 @@ tq4_status attention_impl(const float* q, const float* k_new, const float* v_new
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int chunks = (max_len + kAttnChunk - 1) / kAttnChunk;
   const int C = std::min(kAttnMaxCluster, chunks);
-  static bool attr_set = false;
-  if (!attr_set) {
-    TQ4_CUDA(cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  2 * kAttnChunk * kAttnMaxDim * (int)sizeof(float)));
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_set{0};  // per device
+  TQ4_CUDA(set_smem_limit_once(attention_decode_kernel, 2 * kAttnChunk * kAttnMaxDim * (int)sizeof(float), attr_set));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(C, kv_heads);
   cfg.blockDim = dim3(kAttnThreads);

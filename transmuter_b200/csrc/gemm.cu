@@ -573,16 +573,15 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
+  // looked up once per process (a function-local static: thread-safe initialisation)
+  static const EncodeTiledFn fn = []() -> EncodeTiledFn {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
+      return reinterpret_cast<EncodeTiledFn>(p);
+    return nullptr;
+  }();
   return fn;
 }
 
@@ -675,11 +674,8 @@ static tq4_status launch_gemm_t(const CUtensorMap& ma, const Weight& w, GemmArgs
   args.sc_off = pl.sc_off;
   args.zc_off = pl.zc_off;
   auto kern = gemm_kernel<TM, BF, T>;
-  static bool attr_set = false;  // once per instantiation, at the largest size it can ask for
-  if (!attr_set) {
-    TQ4_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_set{0};  // per device, at the largest size it can ask for
+  TQ4_CUDA(set_smem_limit_once(kern, kSmemLimit, attr_set));
   const dim3 grid(((args.N + WN - 1) / WN) * args.ks, (args.M + TM - 1) / TM);
   if (args.ks == 1) {
     TQ4_CUDA(launch_pdl(kern, grid, dim3(kGemmThreads), pl.smem, st, ma, w.wmaps[0], args.s16 ? w.smap16 : w.smaps[0],

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -82,6 +83,21 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) applies to the device that is current when it
+// is called, so it is made once per (kernel, device): `done` holds one bit per device (ordinals
+// 0..63). Two threads may both set it the first time; the call is idempotent.
+template <typename F>
+cudaError_t set_smem_limit_once(F kern, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const bool tracked = dev >= 0 && dev < 64;
+  if (tracked && ((done.load(std::memory_order_acquire) >> dev) & 1u)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && tracked) done.fetch_or(uint64_t(1) << dev, std::memory_order_acq_rel);
+  return e;
 }
 
 // A device allocation owned by a handle (freed on destruction).

@@ -551,17 +551,19 @@ tq4_status tq4_sharded_matmul(const tq4_sharded* cs, const void* a, int64_t m, t
     const int64_t chunks = m * P * (s->share * ys / 16);
     // Every block waits for the last one's signal, so the grid must be resident all at once: no
     // more blocks than the SMs hold together (occupancy of this kernel, looked up once per device).
-    static int resident[64] = {0};
+    static std::atomic<int> resident[64];  // zero-initialised (static storage)
     int dev = s->comm->device;
     if (dev < 0 || dev >= 64) dev = 0;
-    if (resident[dev] == 0) {
+    int res = resident[dev].load(std::memory_order_relaxed);
+    if (res == 0) {
       int per_sm = 0, sms = 0;
       TQ4_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, exchange_kernel, kExThreads, 0));
       TQ4_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, s->comm->device));
-      resident[dev] = std::max(1, per_sm * sms);
+      res = std::max(1, per_sm * sms);
+      resident[dev].store(res, std::memory_order_relaxed);
     }
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((chunks + kExThreads - 1) / kExThreads,
-                                                                  std::min(resident[dev], 4 * 148)));
+                                                                  std::min(res, 4 * 148)));
     exchange_kernel<<<grid, kExThreads, 0, st>>>(pa, static_cast<unsigned long long*>(s->flags.ptr), s->comm->rank,
                                                  (int)P, m, s->share, s->desc.N, ys, static_cast<uint8_t*>(y));
     TQ4_CUDA(cudaGetLastError());
