@@ -379,6 +379,68 @@ def test_m1_row_tile_hand_out(k, n, bs, zp, st, at, t, bias):
     assert device_status() == 0
 
 
+UNITS_M1 = [
+    # K, N, bs, zp, scale type, A type, T, bias: M = 1 with at most 8 packed groups per row (K <= 1024),
+    # the 32-row-unit kernel: every block size (16 .. 256), zero-point kind and activation type,
+    # K not a multiple of 128 or of the block, N not a multiple of 32, fewer units than CTAs
+    (1024, 5000, 16, "float", "f32", "f32", "f32", True),
+    (1000, 4099, 32, "packed", "f16", "f16", "f16", True),
+    (72, 40, 32, "none", "f32", "f32", "f32", True),
+    (512, 20000, 64, "packed", "bf16", "bf16", "bf16", False),
+    (896, 9000, 128, "none", "f32", "f32", "f32", False),
+    (1024, 12345, 256, "packed", "f32", "f32", "f32", True),
+    (768, 600, 32, "none", "f16", "f32", "f16", False),
+    (1024, 70001, 32, "none", "f32", "bf16", "f32", False),
+    (640, 33, 64, "float", "f16", "f16", "f16", True),
+]
+
+
+@pytest.mark.parametrize("k,n,bs,zp,st,at,t,bias", UNITS_M1)
+def test_m1_units_kernel(k, n, bs, zp, st, at, t, bias):
+    """M = 1 over 32-row units (8 consumer warps, warp w on packed group w, B fragments in
+    registers, the last warp of a unit adding the groups' partials): against an fp64 product over
+    the bit-exact dequantized weight; three calls in a row give the same bits (the unit tickets
+    are back at zero after each call), and the device status stays clean."""
+    cfg = workloads.Config(f"units-{k}-{n}-{bs}-{zp}-{st}-{at}-{t}", k, n, 1, bits=4, block_size=bs,
+                           scale_type=st, zp=zp, a_type=at, bias=bias)
+    p = workloads.make(cfg)
+    w = weight_for(cfg, p, t)
+    a = to_dev(p["A"], at)
+    bias_t = to_dev(p["bias"], at) if bias else None
+    ys = [w.matmul(a, bias_t) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert torch.equal(ys[0], ys[1]) and torch.equal(ys[0], ys[2])
+    wd = o.dequantize_weight(p["B"], p["scales"], p["zp"], k, n, 4, bs, t)
+    want = np.asarray(p["A"], np.float64) @ wd.astype(np.float64).T
+    if bias:
+        want = want + np.asarray(p["bias"], np.float64)
+    got = as_np32(ys[0])
+    assert np.isfinite(got).all()
+    assert o.rel_l2(got, want) < TOL[at], o.rel_l2(got, want)
+    assert device_status() == 0
+
+
+def test_m1_units_interleaved_handles_on_one_stream():
+    """Back-to-back calls of different handles on one stream, without synchronising: each handle's
+    unit tickets are its own and every call starts from a counter at zero."""
+    cfgs = [workloads.Config(f"inter-{i}", 1024, n, 1) for i, n in enumerate((151936, 3072, 40000))]
+    ps = [workloads.make(c) for c in cfgs]
+    ws = [weight_for(c, p, "f32") for c, p in zip(cfgs, ps)]
+    a = [to_dev(p["A"]) for p in ps]
+    first = [w.matmul(x) for w, x in zip(ws, a)]
+    again = []
+    for _ in range(3):
+        again.append([w.matmul(x) for w, x in zip(ws, a)])
+    torch.cuda.synchronize()
+    for rnd in again:
+        for y0, y in zip(first, rnd):
+            assert torch.equal(y0, y)
+    for w, x, y in zip(ws, a, first):
+        want = x.double() @ w.dequantize().double().T
+        assert ((y.double() - want).norm() / want.norm()).item() < 1e-3
+    assert device_status() == 0
+
+
 def test_lm_head_row_tiles_handed_out_in_arrival_order():
     """The 151936-row lm_head at M = 1 hands whole row tiles to CTAs through an arrival counter
     that the last CTA resets: back-to-back calls on one handle (the next call's prefetch overlaps

@@ -6,6 +6,7 @@
 #include <cstdarg>
 
 #include "internal.cuh"
+#include "rows.cuh"
 
 namespace tq4 {
 
@@ -116,6 +117,7 @@ static tq4_status create_weight(const tq4_weight_desc* d, const Source& b, const
   if (st == TQ4_OK) st = prepare_weight(*w, b, s, z);
   if (st == TQ4_OK) st = make_weight_maps(*w);
   if (st == TQ4_OK) st = make_gemv_maps(*w);
+  if (st == TQ4_OK) st = make_rows_maps(*w);
   cudaSetDevice(prev);
   if (st != TQ4_OK) {
     tq4_weight_destroy(w);

@@ -32,6 +32,7 @@
 
 #include "fragments.cuh"
 #include "internal.cuh"
+#include "rows.cuh"
 #include "sm100.cuh"
 
 namespace tq4 {
@@ -1227,6 +1228,16 @@ static tq4_status gemv_launch(const Weight& w, const void* a, int64_t m, tq4_dty
     set_error("GEMV: the handle has no TMA descriptors");
     return TQ4_ERR_CUDA;
   }
+  if (m == 1 && !(pro && pro->mode) && rows_eligible(w)) {
+    // one activation row, at most 8 packed groups: the 32-row-unit kernel (gemv_rows.cu)
+    if (counters == nullptr || ctr_capacity < 1) {
+      set_error("GEMV: the unit hand-out needs one counter");
+      return TQ4_ERR_INVALID_ARGUMENT;
+    }
+    RowsDst dst;
+    dst.y[0] = y;
+    return run_gemv_rows(w, a, a_t, bias, bias_t, y_t, dst, counters, st);
+  }
   const GemvPlan pl = plan_gemv(w, m);
   GemvArgs args{};
   args.a = a;
@@ -1308,27 +1319,38 @@ static tq4_status gemv_launch(const Weight& w, const void* a, int64_t m, tq4_dty
   return TQ4_OK;
 }
 
-int64_t gemv_workspace_floats(const Weight& w, int64_t m) { return plan_gemv(w, m).ws_floats; }
+// Workspace of a plain call (tq4_matmul, tq4_matmul_noalloc): partial-sum floats and counters.
+int64_t gemv_workspace_floats(const Weight& w, int64_t m) {
+  if (m == 1 && rows_eligible(w)) return 0;
+  return plan_gemv(w, m).ws_floats;
+}
 
-int64_t gemv_counter_count(const Weight& w, int64_t m);
+// Counters a call of the 128-row kernels uses (zero-initialised, left at zero by the kernel): one
+// per row tile for split partial sums, one for the M = 1 row-tile hand-out, none otherwise.
+static int64_t tile_counter_count(const Weight& w, int64_t m) {
+  const GemvPlan pl = plan_gemv(w, m);
+  return pl.dyn ? 1 : (pl.ws_floats > 0 ? pl.ctas_n : 0);
+}
 
 // The decoder's fused projection (include/tq4_decoder.h, tq4_matmul_fused).
 tq4_status run_gemv_fused(const Weight& w, const float* x, const float* x2, const float* norm_w, float eps,
                           int mode, const float* residual, float* y, cudaStream_t st) {
   float* ws = nullptr;
   int* ctr = nullptr;
-  const int64_t need = gemv_workspace_floats(w, 1);
-  const int64_t nctr = gemv_counter_count(w, 1);
+  // a staging transform runs in the 128-row kernel; without one the call is a plain M = 1 call
+  const bool plain = mode == 0 && rows_eligible(w);
+  const int64_t need = plain ? 0 : plan_gemv(w, 1).ws_floats;
+  const int64_t nctr = plain ? 1 : tile_counter_count(w, 1);
   if (need > 0 || nctr > 0) TQ4_TRY(gemv_workspace(w, st, need * 4, nctr, &ws, &ctr));
   GemvPrologue pro{mode, norm_w, x2, eps};
   return gemv_launch(w, x, 1, TQ4_F32, residual, TQ4_F32, y, TQ4_F32, w.desc.N, st, ws, ctr, need, nctr, &pro);
 }
 
-// Counters a call uses (zero-initialised, left at zero by the kernel): one per row tile for split
-// partial sums, one for the M = 1 row-tile hand-out, none otherwise.
+// Counters a plain call uses (zero-initialised, left at zero by the kernel): the unit hand-out of
+// the 32-row-unit kernel, or those of the 128-row kernels.
 int64_t gemv_counter_count(const Weight& w, int64_t m) {
-  const GemvPlan pl = plan_gemv(w, m);
-  return pl.dyn ? 1 : (pl.ws_floats > 0 ? pl.ctas_n : 0);
+  if (m == 1 && rows_eligible(w)) return 1;
+  return tile_counter_count(w, m);
 }
 
 tq4_status run_gemv(const Weight& w, const void* a, int64_t m, tq4_dtype a_t, const void* bias,

@@ -171,6 +171,12 @@ struct tq4_weight {
   alignas(64) CUtensorMap gv_zmap;
   bool gv_maps_ok = false;
   int gv_gps = 1, gv_nbs = 1;
+  // TMA descriptors of the 32-row-unit M = 1 GEMV (4-bit weights of at most 8 packed groups per
+  // row): 32 packed rows x 64 bytes, and 40 rows x all blocks of the scales / zero points
+  alignas(64) CUtensorMap rw_wmap;
+  alignas(64) CUtensorMap rw_smap;
+  alignas(64) CUtensorMap rw_zmap;
+  bool rw_ok = false;
 };
 
 namespace tq4 {

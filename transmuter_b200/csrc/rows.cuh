@@ -1,0 +1,31 @@
+// Host-side interface of the 32-row-unit M = 1 GEMV (gemv_rows.cu), shared with the dispatcher
+// (gemv.cu) and the N-sharded push path (sharded.cu).
+#pragma once
+
+#include "internal.cuh"
+
+namespace tq4 {
+
+constexpr int kRowsMaxDst = 8;  // Y itself, or one assembly buffer per rank (at most 8 ranks)
+
+// Where a call's outputs go: row n of the weight is Y column col0 + n of each destination; with
+// `epoch` set (N-sharded calls) the outputs land in the half ((*epoch + 1) & 1) of every
+// destination buffer, halves of half_elems elements.
+struct RowsDst {
+  void* y[kRowsMaxDst] = {};
+  int ndst = 1;
+  int64_t col0 = 0;
+  const unsigned long long* epoch = nullptr;
+  int64_t half_elems = 0;
+};
+
+// 4-bit weights of at most 8 packed groups per row whose unit descriptors were made.
+bool rows_eligible(const Weight& w);
+// The unit descriptors of a new handle (a no-op for handles the kernel does not take).
+tq4_status make_rows_maps(Weight& w);
+// Y = A . W^T (+ bias) for one activation row; `counter` is one int of device memory that is zero
+// before the call and left at zero by it (per stream: calls that overlap must not share it).
+tq4_status run_gemv_rows(const Weight& w, const void* a, tq4_dtype a_t, const void* bias, tq4_dtype bias_t,
+                         tq4_dtype y_t, const RowsDst& dst, int* counter, cudaStream_t st);
+
+}  // namespace tq4
