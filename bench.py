@@ -196,7 +196,8 @@ def workload_config(cfg, world):
     per_copy = cfg.algorithmic_bytes() / (world if sharded else 1)
     copies = rotation_copies(per_copy)
     if sharded:
-        par = f"N-sharded over {world} GPUs (each rank 1/{world} of the weight rows); Y assembled on every rank over NVLink"
+        par = (f"N-sharded over {world} GPUs (each rank 1/{world} of the weight rows); Y assembled on every rank over "
+               f"NVLink (M = 1: each GPU's kernel stores its columns into every rank's buffer)")
     else:
         par = "single GPU" if world == 1 else f"{world} independent replicas (dp{world})"
     return {"workload": cfg.name, "M": cfg.m, "K": cfg.k, "N": cfg.n, "bits": cfg.bits,
@@ -224,6 +225,9 @@ def launches_per_call(cfg, m, sharded_world=1):
     else:
         n = -(-m // 16)                         # GEMV slices of 16 rows
     if sharded_world > 1:
+        groups = -(-(cfg.blocks * cfg.block_size * cfg.bits // 8) // 64)
+        if m == 1 and cfg.bits == 4 and groups <= 8 and sharded_world <= 8:
+            return n + 1                        # the assembly kernel of the push path
         share = (-(-cfg.n // sharded_world) + 15) // 16 * 16
         if m * share * (4 if cfg.a_type == "f32" else 2) >= 4 << 20:
             n += 1                              # the NVLink exchange kernel

@@ -107,6 +107,17 @@ tq4_status tq4_weight_create_from(const tq4_weight_desc* desc, const tq4_source*
 
 tq4_status tq4_weight_destroy(tq4_weight* w);
 
+/* Merges sibling MatMulNBits weights along N, the packed form of Fusion.matmuls/2
+ * (lib/transmuter/fusion.ex:430-540, which concatenates the moved float {N, K} weights of matmuls
+ * that read one input, such as q, k and v, or gate and up, and adds a Split): a new handle whose
+ * rows are the rows of parts[0], then parts[1], ..., N the sum of the parts' N. The parts must
+ * share K, bits, block_size, the scale and zero-point types, the dequantize type and the device;
+ * the copies stay on the device, and the parts remain valid (the caller destroys them). One call
+ * on the merged handle gives every part's Y: columns [off_i, off_i + N_i) are part i's, off_i the
+ * sum of the N before it (the Split). Its dequantized weight is the row concatenation of the
+ * parts', bit for bit. */
+tq4_status tq4_weight_merge(const tq4_weight* const* parts, int count, tq4_weight** out);
+
 /* The handle's attributes and the device bytes it holds. */
 tq4_status tq4_weight_info(const tq4_weight* w, tq4_weight_desc* desc, int64_t* device_bytes);
 
@@ -144,8 +155,26 @@ tq4_status tq4_gather_rows(const tq4_weight* w, const int64_t* indices, int64_t 
                            void* stream);
 
 /* Reads and clears the device status word that bounded waits and device-side checks write.
- * Synchronizes the handle's device. *code = 0 when no kernel reported an error. */
+ * Synchronizes the handle's device. *code = 0 when no kernel reported an error. Codes: 0x101-0x104
+ * a tensor-core GEMM pipeline wait ran out, 0x105 a split-K counter was inconsistent, 0x106 a
+ * peer's flag did not arrive (N-sharded calls), 0x107 a decode-attention copy, 0x108 the GEMV's
+ * activation staging, 0x200 a device-side argument check (decoder positions).
+ * Failure detection of the reference: test/support/hang_watchdog.exs:1-40 flags a call that makes
+ * no progress; here every device wait gives up after a limit and reports instead. */
 tq4_status tq4_device_status(int device, int32_t* code);
+
+/* The limit of every bounded device wait on `device` (mbarrier waits of the GEMV, GEMM and
+ * decoder kernels; the peer-flag waits of N-sharded calls), in SM clock cycles: 0 restores the
+ * default of 2e9 (about one second at the B200's clocks), other values must be at least 1000.
+ * Synchronizes the device first. Meant for failure tests and for watchdogs that must fire
+ * sooner; a limit below a healthy call's own waits makes that call report a timeout. */
+tq4_status tq4_set_wait_limit(int device, int64_t cycles);
+
+/* Runs the peer-flag wait of the N-sharded kernels on `stream` against a flag that nothing ever
+ * sets: after the device's wait limit the kernel gives up, reports 0x106 in the device status and
+ * returns, and the context stays usable. A self-test of the timeout path (no counterpart in the
+ * reference). */
+tq4_status tq4_selftest_peer_wait(int device, void* stream);
 
 /* The message of the last failure on the calling thread ("" when none). Returns the length
  * of the full message; at most len-1 bytes and a NUL are written to buf. */
@@ -186,8 +215,15 @@ tq4_status tq4_sharded_create_from(const tq4_weight_desc* desc, const tq4_source
 /* This rank's first row and row count. */
 tq4_status tq4_sharded_rows(const tq4_sharded* s, int64_t* first, int64_t* count);
 
-/* Y[M, N] on every rank: the local MatMulNBits on this rank's rows, then an NCCL all-gather.
- * A, bias (full N, or NULL) and Y are device pointers on the comm's device. */
+/* Y[M, N] on every rank: the local MatMulNBits on this rank's rows, then Y assembled on every rank.
+ * M = 1 with 4-bit weights of at most 8 packed groups per row (the lm_head): each rank's GEMV
+ * stores its columns straight into every rank's assembly buffer over NVLink, and one small kernel
+ * exchanges an epoch flag per peer (bounded wait, device status 0x106 on timeout) and copies the
+ * row into Y. Slices of 4 MB and more per rank: an NVLink exchange of the ranks' slices. Otherwise
+ * (or where peer mapping is not available on every rank): NCCL's all-gather. A, bias (full N, or
+ * NULL) and Y are device pointers on the comm's device. Every rank makes the same calls in the
+ * same order; the first call of a new shape maps peer memory (a collective) and must come before
+ * any stream capture. */
 tq4_status tq4_sharded_matmul(const tq4_sharded* s, const void* a, int64_t m, tq4_dtype a_dtype,
                               const void* bias, tq4_dtype bias_dtype, void* y, tq4_dtype y_dtype,
                               void* stream);

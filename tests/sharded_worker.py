@@ -38,6 +38,10 @@ CASES = [  # (K, N, M, zero points, A type, scale type)
     # slices of 4 MB and more per rank: the NVLink peer exchange instead of NCCL's all-gather
     (4096, 14336, 512, "packed", "f16", "f16"),
     (1024, 151936, 16, "none", "f32", "f32"),
+    # M = 1 with at most 8 packed groups per row: each rank's GEMV pushes its columns into every
+    # rank's assembly buffer (ragged N; a last rank with few rows; f16 outputs)
+    (1000, 4099, 1, "packed", "f16", "f16"),
+    (1024, 40, 1, "none", "f32", "f32"),
 ]
 TT = {"f32": torch.float32, "f16": torch.float16}
 
@@ -79,6 +83,44 @@ def external_case(comm, rank, dev):
     return ("shard-gpu-external", 0.0 if exact else 1.0, 0.5)
 
 
+def push_graph_case(comm, rank, dev):
+    """The M = 1 push path with a bias, captured in a CUDA graph of three calls (alternating
+    inputs) and replayed twice: the epoch that picks the assembly half lives in device memory, so
+    replays keep advancing it. Every call must equal the eager unsharded one."""
+    k, n = 1024, 151936
+    cfg = workloads.Config("shard-gpu-push-graph", k, n, 1, bias=True)
+    p = workloads.make(cfg)
+    b, s = torch.from_numpy(p["B"]).to(dev), torch.from_numpy(p["scales"]).to(dev)
+    bias = torch.from_numpy(p["bias"]).to(dev)
+    a = torch.from_numpy(np.ascontiguousarray(p["A"])).to(dev)
+    ins = [a, torch.flip(a, dims=[1]).contiguous(), -a]
+    sw = sharded.ShardedWeight(comm, (k, n, 4, 32), b, s, None, dtype=torch.float32)
+    pw = PackedWeight((k, n, 4, 32), b, s, None, dtype=torch.float32, device=dev)
+    refs = [pw.matmul(x, bias) for x in ins]
+    outs = [torch.empty(1, n, device=dev) for _ in ins]
+    gs = torch.cuda.Stream(dev)
+    with torch.cuda.stream(gs):
+        for x, y in zip(ins, outs):  # warm-up outside the capture (maps peer memory once)
+            sw.matmul(x, bias, out=y)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=gs):
+        for x, y in zip(ins, outs):
+            sw.matmul(x, bias, out=y)
+    worst = 0.0
+    for _ in range(2):
+        for y in outs:
+            y.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        for y, ref in zip(outs, refs):
+            worst = max(worst, o.rel_l2(y.double().cpu().numpy(), ref.double().cpu().numpy()))
+    del graph
+    sw.close()
+    pw.close()
+    return ("shard-gpu-push-graph", worst, 1e-6)
+
+
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(rank)
@@ -108,6 +150,7 @@ def main():
         sw.close()
         pw.close()
     worst.append(external_case(comm, rank, dev))
+    worst.append(push_graph_case(comm, rank, dev))
     comm.close()
     ok = all(e < tol for _, e, tol in worst)
     flags = torch.tensor([int(ok)])

@@ -458,3 +458,50 @@ def test_lm_head_row_tiles_handed_out_in_arrival_order():
     for x, y in ((a, ys[0]), (a2, ys[1])):
         want = x.double() @ wd.T
         assert ((y.double() - want).norm() / want.norm()).item() < 1e-3
+
+
+MERGE = [
+    # K, part N, bs, zp, scale type, T: Qwen3's q/k/v (f32 scales) and gate/up; f16 with packed
+    # zero points; float zero points; 2- and 8-bit weights
+    (1024, (2048, 1024, 1024), 32, "none", "f32", "f32"),
+    (1024, (3072, 3072), 32, "none", "f32", "f32"),
+    (4096, (1000, 333, 17), 128, "packed", "f16", "f16"),
+    (640, (64, 100), 64, "float", "bf16", "bf16"),
+    (512, (40, 24), 32, "packed", "f32", "f32"),
+]
+
+
+@pytest.mark.parametrize("k,parts,bs,zp,st,t", MERGE)
+@pytest.mark.parametrize("bits", [4, 2, 8])
+def test_merged_siblings(k, parts, bs, zp, st, t, bits):
+    """tq4_weight_merge (the packed form of Fusion.matmuls/2, lib/transmuter/fusion.ex:430-540):
+    the merged handle's dequantized weight is the row concatenation of the parts', bit for bit,
+    and one call gives every part's Y (the Split): the same bits where each row's arithmetic does
+    not depend on N (M = 1 over 32-row units), within the summation order otherwise."""
+    ws, ps = [], []
+    for i, n in enumerate(parts):
+        cfg = workloads.Config(f"merge-{k}-{n}-{i}-{bs}-{zp}-{st}-{bits}", k, n, 1, bits=bits, block_size=bs,
+                               scale_type=st, zp=zp, a_type=t)
+        ps.append(workloads.make(cfg, m=40))
+        ws.append(weight_for(cfg, ps[-1], t))
+    merged = PackedWeight.merge(ws)
+    assert merged.n == sum(parts)
+    want = torch.cat([w.dequantize() for w in ws], dim=0)
+    got = merged.dequantize()
+    assert torch.equal(got.view(torch.int16 if t != "f32" else torch.int32),
+                       want.view(torch.int16 if t != "f32" else torch.int32))
+    a = to_dev(ps[0]["A"], t)
+    for m in (1, 40):
+        y = merged.matmul(a[:m])
+        ys = torch.cat([w.matmul(a[:m]) for w in ws], dim=1)
+        torch.cuda.synchronize()
+        if m == 1 and bits == 4 and k <= 1024:  # the 32-row-unit kernel: per-row arithmetic
+            assert torch.equal(y, ys), (y - ys).abs().max()
+        else:  # split-K plans follow N, so the summation order may differ
+            assert ((y.double() - ys.double()).norm() / ys.double().norm()).item() < 1e-3
+    for w in ws:  # the parts stay valid after the merge
+        w.close()
+    y1 = merged.matmul(a[:1])
+    torch.cuda.synchronize()
+    assert torch.isfinite(y1).all()
+    assert device_status() == 0

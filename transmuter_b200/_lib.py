@@ -21,9 +21,10 @@ UNIQUE_ID_BYTES = 128
 
 # Every symbol include/tq4.h declares (the CPU tests check the library exports each one).
 EXPORTS = [
-    "tq4_weight_input_sizes", "tq4_weight_create", "tq4_weight_create_from", "tq4_weight_destroy",
+    "tq4_weight_input_sizes", "tq4_weight_create", "tq4_weight_create_from", "tq4_weight_destroy", "tq4_weight_merge",
     "tq4_weight_info",
-    "tq4_matmul", "tq4_matmul_noalloc", "tq4_dequantize", "tq4_gather_rows", "tq4_device_status", "tq4_last_error",
+    "tq4_matmul", "tq4_matmul_noalloc", "tq4_dequantize", "tq4_gather_rows", "tq4_device_status",
+    "tq4_set_wait_limit", "tq4_selftest_peer_wait", "tq4_last_error",
     "tq4_status_string", "tq4_comm_unique_id", "tq4_comm_create", "tq4_comm_destroy",
     "tq4_sharded_create", "tq4_sharded_create_from", "tq4_sharded_rows", "tq4_sharded_matmul", "tq4_sharded_destroy",
     # include/tq4_decoder.h
@@ -78,12 +79,15 @@ def load():
             "tq4_weight_create": [P(WeightDesc), vp, i64, vp, vp, ctypes.c_int, P(vp)],
             "tq4_weight_create_from": [P(WeightDesc), P(Source), P(Source), P(Source), ctypes.c_int, P(vp)],
             "tq4_weight_destroy": [vp],
+            "tq4_weight_merge": [P(vp), ctypes.c_int, P(vp)],
             "tq4_weight_info": [vp, P(WeightDesc), P(i64)],
             "tq4_matmul": [vp, vp, i64, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int, vp],
             "tq4_matmul_noalloc": [vp, vp, i64, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int, vp],
             "tq4_dequantize": [vp, vp, vp],
             "tq4_gather_rows": [vp, vp, i64, vp, vp],
             "tq4_device_status": [ctypes.c_int, P(i32)],
+            "tq4_set_wait_limit": [ctypes.c_int, i64],
+            "tq4_selftest_peer_wait": [ctypes.c_int, vp],
             "tq4_comm_unique_id": [ctypes.c_char_p],
             "tq4_comm_create": [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P(vp)],
             "tq4_comm_destroy": [vp],

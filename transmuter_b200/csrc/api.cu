@@ -76,20 +76,11 @@ static tq4_status check_desc(const tq4_weight_desc* d) {
   return TQ4_OK;
 }
 
-// The handle of a checked description and resolved inputs, on `device`.
-static tq4_status create_weight(const tq4_weight_desc* d, const Source& b, const Source& s,
-                                const Source* z, int device, tq4_weight** out, const char* fn) {
-  int ndev = 0;
-  TQ4_CUDA(cudaGetDeviceCount(&ndev));
-  if (device < 0 || device >= ndev) {
-    set_error("%s: device %d out of range (%d devices)", fn, device, ndev);
-    return TQ4_ERR_INVALID_ARGUMENT;
-  }
-  int prev = 0;
-  TQ4_CUDA(cudaGetDevice(&prev));
-  TQ4_CUDA(cudaSetDevice(device));
-
+// A new handle for a checked description on `device` (made current by the caller): the layout,
+// the handle's stream and its device buffers, zero-filled (padding rows and blocks stay zero).
+static tq4_status layout_weight(const tq4_weight_desc* d, int device, const char* fn, tq4_weight** out) {
   tq4_weight* w = new tq4_weight();
+  *out = w;
   w->desc = *d;
   w->device = device;
   w->blocks = (d->K + d->block_size - 1) / d->block_size;
@@ -104,20 +95,80 @@ static tq4_status create_weight(const tq4_weight_desc* d, const Source& b, const
   while ((1 << w->bs_log2) < d->block_size) ++w->bs_log2;
   w->z_const = (float)(1 << (d->bits - 1));
   cudaDeviceProp prop;
-  tq4_status st = TQ4_OK;
   if (cudaGetDeviceProperties(&prop, device) == cudaSuccess) w->num_sms = prop.multiProcessorCount;
   if (cudaStreamCreateWithFlags(&w->stream, cudaStreamNonBlocking) != cudaSuccess) {
     set_error("%s: cudaStreamCreate failed", fn);
-    st = TQ4_ERR_CUDA;
+    return TQ4_ERR_CUDA;
   }
   const int tsz = dtype_size(d->dequant_dtype);
-  if (st == TQ4_OK) st = w->q.alloc(w->n_pad * w->row_bytes);
-  if (st == TQ4_OK) st = w->scales.alloc(w->n_pad * w->blocks_pad * tsz);
-  if (st == TQ4_OK && d->zp_kind != TQ4_ZP_NONE) st = w->zps.alloc(w->n_pad * w->blocks_pad * tsz);
+  TQ4_TRY(w->q.alloc(w->n_pad * w->row_bytes));
+  TQ4_TRY(w->scales.alloc(w->n_pad * w->blocks_pad * tsz));
+  if (d->zp_kind != TQ4_ZP_NONE) TQ4_TRY(w->zps.alloc(w->n_pad * w->blocks_pad * tsz));
+  return TQ4_OK;
+}
+
+static tq4_status make_maps(tq4_weight* w) {
+  TQ4_TRY(make_weight_maps(*w));
+  TQ4_TRY(make_gemv_maps(*w));
+  return make_rows_maps(*w);
+}
+
+// The handle of a checked description and resolved inputs, on `device`.
+static tq4_status create_weight(const tq4_weight_desc* d, const Source& b, const Source& s,
+                                const Source* z, int device, tq4_weight** out, const char* fn) {
+  int ndev = 0;
+  TQ4_CUDA(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) {
+    set_error("%s: device %d out of range (%d devices)", fn, device, ndev);
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  int prev = 0;
+  TQ4_CUDA(cudaGetDevice(&prev));
+  TQ4_CUDA(cudaSetDevice(device));
+  tq4_weight* w = nullptr;
+  tq4_status st = layout_weight(d, device, fn, &w);
   if (st == TQ4_OK) st = prepare_weight(*w, b, s, z);
-  if (st == TQ4_OK) st = make_weight_maps(*w);
-  if (st == TQ4_OK) st = make_gemv_maps(*w);
-  if (st == TQ4_OK) st = make_rows_maps(*w);
+  if (st == TQ4_OK) st = make_maps(w);
+  cudaSetDevice(prev);
+  if (st != TQ4_OK) {
+    tq4_weight_destroy(w);
+    return st;
+  }
+  *out = w;
+  return TQ4_OK;
+}
+
+// One handle over the rows of `parts` in order (tq4_weight_merge).
+static tq4_status merge_handles(const tq4_weight* const* parts, int count, tq4_weight** out) {
+  const tq4_weight_desc& d0 = parts[0]->desc;
+  tq4_weight_desc d = d0;
+  int64_t n = 0;
+  for (int i = 0; i < count; ++i) {
+    const tq4_weight* p = parts[i];
+    const tq4_weight_desc& di = p->desc;
+    if (di.K != d0.K || di.bits != d0.bits || di.block_size != d0.block_size || di.scale_dtype != d0.scale_dtype ||
+        di.zp_kind != d0.zp_kind || (di.zp_kind != TQ4_ZP_NONE && di.zp_dtype != d0.zp_dtype) ||
+        di.dequant_dtype != d0.dequant_dtype || p->device != parts[0]->device) {
+      set_error("tq4_weight_merge: part %d differs from part 0 (K, bits, block_size, scale or zero-point type, "
+                "dequantize type or device)", i);
+      return TQ4_ERR_INVALID_ARGUMENT;
+    }
+    n += di.N;
+  }
+  d.N = n;
+  TQ4_TRY(check_desc(&d));
+  int prev = 0;
+  TQ4_CUDA(cudaGetDevice(&prev));
+  TQ4_CUDA(cudaSetDevice(parts[0]->device));
+  tq4_weight* w = nullptr;
+  tq4_status st = layout_weight(&d, parts[0]->device, "tq4_weight_merge", &w);
+  if (st == TQ4_OK && cudaMemsetAsync(w->q.ptr, 0, w->q.bytes, w->stream) != cudaSuccess) st = TQ4_ERR_CUDA;
+  if (st == TQ4_OK && cudaMemsetAsync(w->scales.ptr, 0, w->scales.bytes, w->stream) != cudaSuccess) st = TQ4_ERR_CUDA;
+  if (st == TQ4_OK && w->zps.ptr && cudaMemsetAsync(w->zps.ptr, 0, w->zps.bytes, w->stream) != cudaSuccess)
+    st = TQ4_ERR_CUDA;
+  if (st == TQ4_ERR_CUDA) set_error("tq4_weight_merge: cudaMemsetAsync failed");
+  if (st == TQ4_OK) st = merge_weight(*w, parts, count);
+  if (st == TQ4_OK) st = make_maps(w);
   cudaSetDevice(prev);
   if (st != TQ4_OK) {
     tq4_weight_destroy(w);
@@ -251,6 +302,21 @@ tq4_status tq4_weight_destroy(tq4_weight* w) {
   return TQ4_OK;
 }
 
+tq4_status tq4_weight_merge(const tq4_weight* const* parts, int count, tq4_weight** out) {
+  clear_error();
+  if (!out || !parts || count < 1) {
+    set_error("tq4_weight_merge: null output, no parts");
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  *out = nullptr;
+  for (int i = 0; i < count; ++i)
+    if (!parts[i]) {
+      set_error("tq4_weight_merge: part %d is null", i);
+      return TQ4_ERR_INVALID_ARGUMENT;
+    }
+  return merge_handles(parts, count, out);
+}
+
 tq4_status tq4_weight_info(const tq4_weight* w, tq4_weight_desc* d, int64_t* device_bytes) {
   clear_error();
   if (!w) {
@@ -307,6 +373,25 @@ tq4_status tq4_gather_rows(const tq4_weight* w, const int64_t* indices, int64_t 
   }
   DeviceGuard guard(w->device);
   return run_dequant(*w, indices, count, out, static_cast<cudaStream_t>(stream));
+}
+
+tq4_status tq4_set_wait_limit(int device, int64_t cycles) {
+  clear_error();
+  int ndev = 0;
+  TQ4_CUDA(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) {
+    set_error("tq4_set_wait_limit: device %d out of range (%d devices)", device, ndev);
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  if (cycles < 0 || (cycles > 0 && cycles < 1000)) {
+    set_error("tq4_set_wait_limit: %lld cycles (0 for the default, else at least 1000)", (long long)cycles);
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  DeviceGuard guard(device);
+  const long long v = cycles == 0 ? 2000000000LL : (long long)cycles;
+  TQ4_CUDA(cudaDeviceSynchronize());  // no kernel of this device waits while the limit changes
+  TQ4_CUDA(cudaMemcpyToSymbol(g_wait_cycles, &v, sizeof(v)));
+  return TQ4_OK;
 }
 
 tq4_status tq4_device_status(int device, int32_t* code) {

@@ -33,6 +33,11 @@ extern __device__ int32_t g_device_status;
 
 __device__ __forceinline__ void report(int32_t code) { atomicCAS(&g_device_status, 0, code); }
 
+// The limit of every bounded wait, in SM clock cycles (defined in weight.cu; about one second by
+// default, set per device with tq4_set_wait_limit).
+extern __device__ long long g_wait_cycles;
+__device__ __forceinline__ long long wait_limit() { return *reinterpret_cast<volatile long long*>(&g_wait_cycles); }
+
 // Programmatic dependent launch. A kernel launched with launch_pdl may start while the kernel
 // before it on the stream is still running: everything it does before pdl_wait() must touch only
 // memory no earlier kernel writes (weights, its own shared memory). pdl_wait() returns once the

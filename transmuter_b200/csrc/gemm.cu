@@ -407,7 +407,7 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM>::CTAS)
     const long long t0 = clock64();
     bool ok = true;
     while (!mbar_test(accum, 0)) {
-      if (clock64() - t0 > kWaitCycles) {
+      if (clock64() - t0 > wait_limit()) {
         report(kDevTimeoutAccum);
         *abort_flag = 1;
         ok = false;

@@ -199,6 +199,8 @@ tq4_status fill_device(void* dst, const Source& src, int device, cudaStream_t st
 // Stages the raw inputs on the device and rewrites them into the handle's layout; `zp` is null
 // when the weight has no zero-point input.
 tq4_status prepare_weight(Weight& w, const Source& b, const Source& scales, const Source* zp);
+// Fills a handle laid out for the summed N with the rows of `parts` in order (tq4_weight_merge).
+tq4_status merge_weight(Weight& w, const Weight* const* parts, int count);
 tq4_status make_weight_maps(Weight& w);
 tq4_status make_gemv_maps(Weight& w);
 // A 2-D tiled TMA descriptor (cuTensorMapEncodeTiled through the runtime's driver entry point).

@@ -26,6 +26,7 @@
 #include <thread>
 
 #include "internal.cuh"
+#include "rows.cuh"
 
 namespace tq4 {
 
@@ -109,7 +110,6 @@ static ncclDataType_t nccl_type(tq4_dtype t) {
 }
 
 constexpr int kMaxPeers = 8;
-constexpr long long kPeerWaitCycles = 2000000000LL;  // about one second
 
 // Flag words of a rank: ready[kMaxPeers], read[kMaxPeers], then the block counter and the epoch.
 constexpr int kFlagReady = 0, kFlagRead = kMaxPeers, kFlagCounter = 2 * kMaxPeers, kFlagEpoch = 2 * kMaxPeers + 1;
@@ -130,14 +130,15 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   return v;
 }
 
-// Bounded wait until flags[base + q] >= epoch for every rank q; false (and the device status) on
-// timeout.
+// Bounded wait until flags[base + q] >= epoch for every rank q other than `skip`; false (and the
+// device status) on timeout.
 __device__ __forceinline__ bool wait_flags(const unsigned long long* flags, int base, int nranks,
-                                           unsigned long long epoch) {
-  const long long t0 = clock64();
+                                           unsigned long long epoch, int skip = -1) {
+  const long long t0 = clock64(), limit = wait_limit();
   for (int q = 0; q < nranks; ++q) {
+    if (q == skip) continue;
     while (ld_acquire_sys(flags + base + q) < epoch) {
-      if (clock64() - t0 > kPeerWaitCycles) {
+      if (clock64() - t0 > limit) {
         report(kDevTimeoutPeer);
         return false;
       }
@@ -198,6 +199,59 @@ __global__ void __launch_bounds__(kExThreads) exchange_kernel(PeerArgs pa, unsig
   }
 }
 
+// The assembly of an N-sharded M = 1 call (the push path). Every rank's GEMV (gemv_rows.cu) has
+// stored its columns into half (e & 1) of every rank's assembly buffer over NVLink, e being this
+// call's epoch. Block 0 publishes e in every peer's ready flags (release, system scope, after the
+// GEMV's stores: the previous kernel on the stream); every block waits, bounded, for every
+// peer's flag, then copies its share of the assembled row into Y; the last block to finish
+// advances the epoch. Two halves suffice: a rank's GEMV of call e + 1 runs only after its own
+// assembly of call e, which saw every peer's flag e, set by each peer after its assembly of
+// call e - 1, the last reader of the half that call e + 1 writes.
+__global__ void __launch_bounds__(kExThreads) push_finish_kernel(PeerArgs pa, unsigned long long* own, int rank,
+                                                                 int nranks, const uint8_t* assembly,
+                                                                 int64_t half_bytes, uint8_t* y, int64_t y_bytes) {
+  __shared__ int s_ok;
+  const unsigned long long epoch = *reinterpret_cast<volatile unsigned long long*>(own + kFlagEpoch) + 1;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) {
+      __threadfence_system();  // the GEMV's stores (the previous kernel) before the flags
+      for (int q = 0; q < nranks; ++q)
+        if (q != rank) st_release_sys(pa.flags[q] + kFlagReady + rank, epoch);
+    }
+    s_ok = wait_flags(own, kFlagReady, nranks, epoch, rank);
+  }
+  __syncthreads();
+  if (s_ok) {
+    const uint8_t* src = assembly + (int64_t)(epoch & 1) * half_bytes;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    int64_t head = 0;
+    if ((reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+      const int64_t n16 = y_bytes / 16;
+      for (int64_t i = tid; i < n16; i += stride)
+        reinterpret_cast<uint4*>(y)[i] = __ldcg(reinterpret_cast<const uint4*>(src) + i);
+      head = n16 * 16;
+    }
+    for (int64_t i = head + tid; i < y_bytes; i += stride) y[i] = src[i];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    unsigned int* counter = reinterpret_cast<unsigned int*>(own + kFlagCounter);
+    if (atomicAdd(counter, 1u) == gridDim.x - 1) {  // the last block: the call is over
+      *counter = 0;
+      *reinterpret_cast<volatile unsigned long long*>(own + kFlagEpoch) = epoch;
+    }
+  }
+}
+
+// The peer-flag wait of the kernels above on a flag that nothing sets (tq4_selftest_peer_wait):
+// it runs out after the device's wait limit and reports kDevTimeoutPeer.
+__device__ unsigned long long g_never_set[kMaxPeers];
+__global__ void selftest_peer_wait_kernel() {
+  if (threadIdx.x == 0) wait_flags(g_never_set, 0, 2, 1);
+}
+
 // [P][M][share] (the all-gather order) -> Y [M][N]
 template <typename T>
 __global__ void unshard_kernel(const T* __restrict__ g, int64_t m, int64_t share, int nranks,
@@ -230,113 +284,155 @@ struct tq4_sharded {
   std::mutex mu;
   DeviceBuffer part;    // this rank's [M][share] output (NCCL path)
   DeviceBuffer gather;  // [P][M][share] (NCCL path)
-  // peer exchange
-  bool peer_tried = false, peer_ok = false;
-  int64_t peer_cap = 0;              // bytes of the slice buffer
-  DeviceBuffer slice, flags;         // this rank's [M][share] slice and its flag words
-  void* peer_slice[kMaxPeers] = {};  // mapped peer buffers (own entries point at our own)
+  // Peer memory (CUDA IPC mappings; each set is mapped on every rank or on none).
+  // The flag words of every rank (ready, read, block counter, epoch):
+  bool flags_tried = false, flags_ok = false;
+  DeviceBuffer flags;
   void* peer_flags[kMaxPeers] = {};
+  // The exchange's [M][share] slices:
+  bool slice_tried = false, slice_ok = false;
+  int64_t slice_cap = 0;
+  DeviceBuffer slice;
+  void* peer_slice[kMaxPeers] = {};
+  // The M = 1 push path's assembly buffers (two halves of N outputs, 4 bytes each at most):
+  bool asm_tried = false, asm_ok = false;
+  DeviceBuffer assembly;
+  void* peer_asm[kMaxPeers] = {};
 };
 
 namespace tq4 {
 
-static void close_peers(tq4_sharded* s) {
-  for (int q = 0; q < s->comm->nranks && q < kMaxPeers; ++q) {
-    if (q == s->comm->rank) continue;
-    if (s->peer_slice[q]) cudaIpcCloseMemHandle(s->peer_slice[q]);
-    if (s->peer_flags[q]) cudaIpcCloseMemHandle(s->peer_flags[q]);
-  }
-  for (int q = 0; q < kMaxPeers; ++q) s->peer_slice[q] = s->peer_flags[q] = nullptr;
-  s->peer_ok = false;
+tq4_status gemv_workspace(const Weight& w, cudaStream_t st, int64_t ws_bytes, int64_t ctr_count, float** ws,
+                          int** counters);
+
+static void close_set(tq4_sharded* s, void** mapped, bool* ok) {
+  for (int q = 0; q < s->comm->nranks && q < kMaxPeers; ++q)
+    if (q != s->comm->rank && mapped[q]) cudaIpcCloseMemHandle(mapped[q]);
+  for (int q = 0; q < kMaxPeers; ++q) mapped[q] = nullptr;
+  *ok = false;
 }
 
-// Collective (every rank, same call): slice buffers of at least `bytes`, their IPC handles
-// exchanged, the peers' buffers mapped. Sets peer_ok only when every rank mapped every peer.
-static tq4_status peer_setup(tq4_sharded* s, NcclApi* api, int64_t bytes, cudaStream_t st) {
-  const int P = s->comm->nranks, R = s->comm->rank;
-  if (s->peer_tried && (!s->peer_ok || s->peer_cap >= bytes)) return TQ4_OK;
-  if (P > kMaxPeers) {
-    s->peer_tried = true;
-    return TQ4_OK;
-  }
-  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  TQ4_CUDA(cudaStreamIsCapturing(st, &cs));
-  if (cs != cudaStreamCaptureStatusNone) {
-    set_error("tq4_sharded_matmul: the first call with a larger M must come before stream capture");
-    return TQ4_ERR_INVALID_ARGUMENT;
-  }
-  TQ4_CUDA(cudaStreamSynchronize(st));
-  if (s->peer_tried) {  // growing: every rank is here too (the same collective call)
-    close_peers(s);
-    TQ4_CUDA(cudaDeviceSynchronize());
-  }
-  s->peer_tried = true;
-  const int64_t cap = (bytes + (2 << 20) - 1) / (2 << 20) * (2 << 20);
-  TQ4_TRY(s->slice.alloc(cap));
-  if (!s->flags.ptr) {  // the epochs only grow: the flag words outlive a slice regrowth
-    TQ4_TRY(s->flags.alloc(kFlagWords * sizeof(unsigned long long)));
-    TQ4_CUDA(cudaMemset(s->flags.ptr, 0, kFlagWords * sizeof(unsigned long long)));
-  }
-  // handles of the slice and the flag words; then one byte: did every open succeed
-  struct Handles {
-    cudaIpcMemHandle_t h[2];
-  } mine{};
-  bool ok = cudaIpcGetMemHandle(&mine.h[0], s->slice.ptr) == cudaSuccess &&
-            cudaIpcGetMemHandle(&mine.h[1], s->flags.ptr) == cudaSuccess;
-  cudaGetLastError();
-  DeviceBuffer xbuf;
-  TQ4_TRY(xbuf.alloc((int64_t)(P + 1) * sizeof(Handles) + 2 * P));
-  uint8_t* dbuf = static_cast<uint8_t*>(xbuf.ptr);
-  TQ4_CUDA(cudaMemcpy(dbuf + P * sizeof(Handles), &mine, sizeof(Handles), cudaMemcpyHostToDevice));
-  ncclResult_t r = api->AllGather(dbuf + P * sizeof(Handles), dbuf, sizeof(Handles), ncclUint8, s->comm->comm, st);
+static tq4_status allgather_bytes(tq4_sharded* s, NcclApi* api, const void* mine, void* all, size_t bytes,
+                                  cudaStream_t st) {
+  const int P = s->comm->nranks;
+  DeviceBuffer buf;
+  TQ4_TRY(buf.alloc((int64_t)(P + 1) * bytes));
+  uint8_t* d = static_cast<uint8_t*>(buf.ptr);
+  TQ4_CUDA(cudaMemcpy(d + P * bytes, mine, bytes, cudaMemcpyHostToDevice));
+  ncclResult_t r = api->AllGather(d + P * bytes, d, bytes, ncclUint8, s->comm->comm, st);
   if (r == ncclInProgress) {
     TQ4_TRY(nccl_wait(api, s->comm->comm, std::chrono::steady_clock::now() + std::chrono::seconds(60), "ncclAllGather"));
   } else if (r != ncclSuccess) {
+    s->comm->broken = true;
     set_error("ncclAllGather: %s", api->GetErrorString(r));
     return TQ4_ERR_NCCL;
   }
   TQ4_CUDA(cudaStreamSynchronize(st));
-  Handles all[kMaxPeers];
-  TQ4_CUDA(cudaMemcpy(all, dbuf, P * sizeof(Handles), cudaMemcpyDeviceToHost));
+  TQ4_CUDA(cudaMemcpy(all, d, P * bytes, cudaMemcpyDeviceToHost));
+  return TQ4_OK;
+}
+
+// Collective (every rank, same call, outside stream capture): the IPC handle of `local` on every
+// rank, each peer's buffer mapped into mapped[] (the own entry is `local`). *ok is set only when
+// every rank mapped every peer; otherwise nothing stays mapped.
+static tq4_status map_set(tq4_sharded* s, NcclApi* api, void* local, void** mapped, bool* ok, cudaStream_t st) {
+  const int P = s->comm->nranks, R = s->comm->rank;
+  *ok = false;
+  cudaIpcMemHandle_t mine{};
+  bool good = cudaIpcGetMemHandle(&mine, local) == cudaSuccess;
+  cudaGetLastError();
+  cudaIpcMemHandle_t all[kMaxPeers];
+  TQ4_TRY(allgather_bytes(s, api, &mine, all, sizeof(mine), st));
   for (int q = 0; q < P; ++q) {
     if (q == R) {
-      s->peer_slice[q] = s->slice.ptr;
-      s->peer_flags[q] = s->flags.ptr;
+      mapped[q] = local;
       continue;
     }
-    for (int k = 0; k < 2 && ok; ++k) {
-      void* ptr = nullptr;
-      if (cudaIpcOpenMemHandle(&ptr, all[q].h[k], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
-        cudaGetLastError();
-        ok = false;
-        break;
-      }
-      if (k == 0) s->peer_slice[q] = ptr;
-      else s->peer_flags[q] = ptr;
+    void* ptr = nullptr;
+    if (!good || cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      good = false;
+      continue;
     }
+    mapped[q] = ptr;
   }
-  // agree: peer exchange only if every rank mapped every peer
-  const uint8_t mine_ok = ok ? 1 : 0;
-  TQ4_CUDA(cudaMemcpy(dbuf + P * sizeof(Handles) + P, &mine_ok, 1, cudaMemcpyHostToDevice));
-  r = api->AllGather(dbuf + P * sizeof(Handles) + P, dbuf + P * sizeof(Handles), 1, ncclUint8, s->comm->comm, st);
-  if (r == ncclInProgress) {
-    TQ4_TRY(nccl_wait(api, s->comm->comm, std::chrono::steady_clock::now() + std::chrono::seconds(60), "ncclAllGather"));
-  } else if (r != ncclSuccess) {
-    set_error("ncclAllGather: %s", api->GetErrorString(r));
-    return TQ4_ERR_NCCL;
-  }
-  TQ4_CUDA(cudaStreamSynchronize(st));
+  const uint8_t mine_ok = good ? 1 : 0;
   uint8_t oks[kMaxPeers];
-  TQ4_CUDA(cudaMemcpy(oks, dbuf + P * sizeof(Handles), P, cudaMemcpyDeviceToHost));
+  TQ4_TRY(allgather_bytes(s, api, &mine_ok, oks, 1, st));
   bool all_ok = true;
   for (int q = 0; q < P; ++q) all_ok = all_ok && oks[q];
   if (!all_ok) {
-    close_peers(s);
+    close_set(s, mapped, ok);
     return TQ4_OK;
   }
-  s->peer_ok = true;
-  s->peer_cap = cap;
+  *ok = true;
   return TQ4_OK;
+}
+
+static tq4_status not_capturing(cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  TQ4_CUDA(cudaStreamIsCapturing(st, &cs));
+  if (cs != cudaStreamCaptureStatusNone) {
+    set_error("tq4_sharded_matmul: the first call of a new shape must come before stream capture");
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  return TQ4_OK;
+}
+
+// Collective: every rank's flag words mapped (once; the epochs only grow, so they outlive any
+// regrowth of the data buffers).
+static tq4_status ensure_flags(tq4_sharded* s, NcclApi* api, cudaStream_t st) {
+  if (s->flags_tried) return TQ4_OK;
+  if (s->comm->nranks > kMaxPeers) {
+    s->flags_tried = true;
+    return TQ4_OK;
+  }
+  TQ4_TRY(not_capturing(st));
+  TQ4_CUDA(cudaStreamSynchronize(st));
+  s->flags_tried = true;
+  TQ4_TRY(s->flags.alloc(kFlagWords * sizeof(unsigned long long)));
+  TQ4_CUDA(cudaMemset(s->flags.ptr, 0, kFlagWords * sizeof(unsigned long long)));
+  return map_set(s, api, s->flags.ptr, s->peer_flags, &s->flags_ok, st);
+}
+
+// Collective: slice buffers of at least `bytes` on every rank, mapped by every peer.
+static tq4_status ensure_slices(tq4_sharded* s, NcclApi* api, int64_t bytes, cudaStream_t st) {
+  TQ4_TRY(ensure_flags(s, api, st));
+  if (!s->flags_ok) return TQ4_OK;
+  if (s->slice_tried && (!s->slice_ok || s->slice_cap >= bytes)) return TQ4_OK;
+  TQ4_TRY(not_capturing(st));
+  TQ4_CUDA(cudaStreamSynchronize(st));
+  if (s->slice_tried) {  // growing: every rank is here too (the same collective call)
+    close_set(s, s->peer_slice, &s->slice_ok);
+    TQ4_CUDA(cudaDeviceSynchronize());
+  }
+  s->slice_tried = true;
+  const int64_t cap = (bytes + (2 << 20) - 1) / (2 << 20) * (2 << 20);
+  TQ4_TRY(s->slice.alloc(cap));
+  TQ4_TRY(map_set(s, api, s->slice.ptr, s->peer_slice, &s->slice_ok, st));
+  if (s->slice_ok) s->slice_cap = cap;
+  return TQ4_OK;
+}
+
+// Collective: the M = 1 assembly buffers (2 x N outputs of up to 4 bytes), mapped by every peer.
+static tq4_status ensure_assembly(tq4_sharded* s, NcclApi* api, cudaStream_t st) {
+  TQ4_TRY(ensure_flags(s, api, st));
+  if (!s->flags_ok || s->asm_tried) return TQ4_OK;
+  TQ4_TRY(not_capturing(st));
+  TQ4_CUDA(cudaStreamSynchronize(st));
+  s->asm_tried = true;
+  TQ4_TRY(s->assembly.alloc(2 * s->desc.N * 4));
+  return map_set(s, api, s->assembly.ptr, s->peer_asm, &s->asm_ok, st);
+}
+
+// Whether an N-sharded M = 1 call takes the push path: the 32-row-unit GEMV takes every rank's
+// rows (4-bit weights of at most 8 packed groups per row; a property of the full weight, so every
+// rank decides alike) and there are at most 8 ranks.
+static bool push_shape(const tq4_sharded* s, int64_t m) {
+  const tq4_weight_desc& d = s->desc;
+  const int64_t blocks = (d.K + d.block_size - 1) / d.block_size;
+  const int64_t groups = (blocks * d.block_size * d.bits / 8 + 63) / 64;
+  return m == 1 && d.bits == 4 && groups <= 8 && s->comm->nranks > 1 && s->comm->nranks <= kMaxPeers;
 }
 
 }  // namespace tq4
@@ -536,9 +632,44 @@ tq4_status tq4_sharded_matmul(const tq4_sharded* cs, const void* a, int64_t m, t
   const int ys = dtype_size(y_t);
   std::lock_guard<std::mutex> lock(s->mu);
   TQ4_CUDA(cudaSetDevice(s->comm->device));
+  if (push_shape(s, m)) {
+    // One activation row: every rank's GEMV stores its columns straight into every rank's
+    // assembly buffer, then push_finish_kernel exchanges one epoch flag per peer and copies the
+    // assembled row into Y.
+    TQ4_TRY(ensure_assembly(s, api, st));
+    if (s->asm_ok) {
+      if (s->local) {
+        if (!rows_eligible(*s->local)) {
+          set_error("tq4_sharded_matmul: this rank's rows have no 32-row unit descriptors");
+          return TQ4_ERR_UNSUPPORTED;
+        }
+        float* ws = nullptr;
+        int* ctr = nullptr;
+        TQ4_TRY(gemv_workspace(*s->local, st, 0, 1, &ws, &ctr));
+        RowsDst dst;
+        for (int q = 0; q < P; ++q) dst.y[q] = s->peer_asm[q];
+        dst.ndst = (int)P;
+        dst.col0 = s->first;
+        dst.epoch = static_cast<const unsigned long long*>(s->flags.ptr) + kFlagEpoch;
+        dst.half_elems = s->desc.N;
+        const void* lb = bias ? static_cast<const uint8_t*>(bias) + s->first * dtype_size(bias_t) : nullptr;
+        TQ4_TRY(run_gemv_rows(*s->local, a, a_t, lb, bias_t, y_t, dst, ctr, st));
+      }
+      PeerArgs pa{};
+      for (int q = 0; q < P; ++q) pa.flags[q] = static_cast<unsigned long long*>(s->peer_flags[q]);
+      const int64_t y_bytes = s->desc.N * ys;
+      const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((y_bytes / 16 + kExThreads - 1) / kExThreads, 148));
+      push_finish_kernel<<<grid, kExThreads, 0, st>>>(pa, static_cast<unsigned long long*>(s->flags.ptr),
+                                                      s->comm->rank, (int)P,
+                                                      static_cast<const uint8_t*>(s->assembly.ptr), y_bytes,
+                                                      static_cast<uint8_t*>(y), y_bytes);
+      TQ4_CUDA(cudaGetLastError());
+      return TQ4_OK;
+    }
+  }
   const bool large = m * s->share * ys >= kPeerMinSlice;
-  if (large) TQ4_TRY(peer_setup(s, api, m * s->share * ys, st));
-  if (large && s->peer_ok) {
+  if (large) TQ4_TRY(ensure_slices(s, api, m * s->share * ys, st));
+  if (large && s->slice_ok) {
     if (s->local) {
       const void* lb = bias ? static_cast<const uint8_t*>(bias) + s->first * dtype_size(bias_t) : nullptr;
       TQ4_TRY(run_matmul(*s->local, a, m, a_t, lb, bias_t, s->slice.ptr, y_t, s->share, st));
@@ -605,13 +736,29 @@ tq4_status tq4_sharded_matmul(const tq4_sharded* cs, const void* a, int64_t m, t
   return TQ4_OK;
 }
 
+tq4_status tq4_selftest_peer_wait(int device, void* stream) {
+  clear_error();
+  int ndev = 0;
+  TQ4_CUDA(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) {
+    set_error("tq4_selftest_peer_wait: device %d out of range", device);
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  DeviceGuard guard(device);
+  selftest_peer_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>();
+  TQ4_CUDA(cudaGetLastError());
+  return TQ4_OK;
+}
+
 tq4_status tq4_sharded_destroy(tq4_sharded* s) {
   if (!s) return TQ4_OK;
   if (s->local) tq4_weight_destroy(s->local);
-  if (s->peer_tried) {
+  if (s->flags_tried || s->slice_tried || s->asm_tried) {
     cudaSetDevice(s->comm->device);
     cudaDeviceSynchronize();
-    close_peers(s);
+    close_set(s, s->peer_slice, &s->slice_ok);
+    close_set(s, s->peer_asm, &s->asm_ok);
+    close_set(s, s->peer_flags, &s->flags_ok);
   }
   s->part.release();
   s->gather.release();

@@ -40,9 +40,6 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// About one second at the B200's clocks; a healthy stage completes in microseconds.
-constexpr long long kWaitCycles = 2000000000LL;
-
 // Waits for the phase `parity` of `bar`, unless the CTA aborted; false on timeout or abort.
 // Polls with the non-blocking test_wait: clock stamps of the GEMM and GEMV stage rings showed
 // waiters resuming 500-900 cycles after the phase had completed when they polled with
@@ -50,10 +47,10 @@ constexpr long long kWaitCycles = 2000000000LL;
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int32_t code) {
   if (mbar_test(bar, parity)) return true;
-  const long long t0 = clock64();
+  const long long t0 = clock64(), limit = wait_limit();  // a healthy stage takes microseconds
   while (!mbar_test(bar, parity)) {
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       report(code);
       *abort_flag = 1;
       return false;
@@ -64,8 +61,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 
 // Waits (bounded) for a phase that is known to complete; used when winding down.
 __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
-  const long long t0 = clock64();
-  while (!mbar_test(bar, parity) && clock64() - t0 < kWaitCycles) {
+  const long long t0 = clock64(), limit = wait_limit();
+  while (!mbar_test(bar, parity) && clock64() - t0 < limit) {
   }
 }
 
@@ -74,6 +71,24 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
       ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// An L2 policy for data read once per call (streamed weights): evict it first, so that the
+// small tensors a call reuses (activations, outputs, the next kernel's inputs) stay in L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// tma_load_2d with an L2 cache policy (l2_evict_first_policy).
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;"
+      ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar), "l"(policy)
       : "memory");
 }
 

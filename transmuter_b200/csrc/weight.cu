@@ -9,6 +9,7 @@
 namespace tq4 {
 
 __device__ int32_t g_device_status = 0;
+__device__ long long g_wait_cycles = 2000000000LL;  // about one second at the B200's clocks
 
 // One thread per output 32-bit word of the packed layout: gathers its 32/BITS elements from
 // the raw rows (element k of row n = bits [(k%per)*BITS, ...) of byte k/per, packed.ex:11-23).
@@ -256,6 +257,48 @@ tq4_status prepare_weight(Weight& w, const Source& b_src, const Source& s_src, c
     }
   }
   // The staging buffers are freed when this function returns; finish the kernels first.
+  TQ4_CUDA(cudaStreamSynchronize(st));
+  return TQ4_OK;
+}
+
+// Fusion.matmuls/2 for packed weights (lib/transmuter/fusion.ex:430-540): the rows of parts[0],
+// then parts[1], ... copied into w's buffers (already laid out for the summed N, zero-filled by the
+// caller where the copies do not reach). The packed rows are contiguous per part; the block-major
+// scales and zero points are pitched copies (one run of N_i entries per block row). The per-row
+// exponents and the f16 block scales of f32 weights derive from the scales, so they are computed
+// again over the merged scales, exactly as for a handle built from the concatenated inputs.
+tq4_status merge_weight(Weight& w, const Weight* const* parts, int count) {
+  const tq4_weight_desc& d = w.desc;
+  cudaStream_t st = w.stream;
+  const int tsz = dtype_size(d.dequant_dtype);
+  int64_t off = 0;
+  for (int i = 0; i < count; ++i) {
+    const Weight& p = *parts[i];
+    const int64_t n = p.desc.N;
+    TQ4_CUDA(cudaMemcpyAsync(static_cast<uint8_t*>(w.q.ptr) + off * w.row_bytes, p.q.ptr, n * w.row_bytes,
+                             cudaMemcpyDeviceToDevice, st));
+    TQ4_CUDA(cudaMemcpy2DAsync(static_cast<uint8_t*>(w.scales.ptr) + off * tsz, w.n_pad * tsz, p.scales.ptr,
+                               p.n_pad * tsz, n * tsz, w.blocks_pad, cudaMemcpyDeviceToDevice, st));
+    if (w.zps.ptr)
+      TQ4_CUDA(cudaMemcpy2DAsync(static_cast<uint8_t*>(w.zps.ptr) + off * tsz, w.n_pad * tsz, p.zps.ptr,
+                                 p.n_pad * tsz, n * tsz, w.blocks_pad, cudaMemcpyDeviceToDevice, st));
+    off += n;
+  }
+  if (d.dequant_dtype == TQ4_F32 && d.bits == 4) {
+    TQ4_TRY(w.wexp.alloc(w.n_pad * 4));
+    row_exponent_kernel<<<grid_for(w.n_pad, 256), 256, 0, st>>>(
+        static_cast<const float*>(w.scales.ptr), static_cast<const float*>(w.zps.ptr), w.z_const, w.blocks,
+        d.N, w.n_pad, 15.f, static_cast<int32_t*>(w.wexp.ptr));
+    TQ4_CUDA(cudaGetLastError());
+    if (d.zp_kind == TQ4_ZP_NONE) {
+      const int64_t total = w.n_pad * w.blocks_pad;
+      TQ4_TRY(w.scales16.alloc(total * 2));
+      scale16_kernel<<<grid_for(total, 256), 256, 0, st>>>(static_cast<const float*>(w.scales.ptr),
+                                                            static_cast<const int32_t*>(w.wexp.ptr), w.n_pad,
+                                                            total, static_cast<__half*>(w.scales16.ptr));
+      TQ4_CUDA(cudaGetLastError());
+    }
+  }
   TQ4_CUDA(cudaStreamSynchronize(st));
   return TQ4_OK;
 }

@@ -156,6 +156,26 @@ class PackedWeight:
         self._handle = handle
         self._lib = lib
 
+    @classmethod
+    def merge(cls, parts):
+        """One weight over the rows of ``parts`` in order (``tq4_weight_merge``; the packed form of
+        ``Fusion.matmuls/2``, lib/transmuter/fusion.ex:430-540). The parts stay valid."""
+        if not parts:
+            raise ArgumentError("merge needs at least one weight")
+        lib = _lib.load()
+        arr = (ctypes.c_void_p * len(parts))(*[p._handle.value for p in parts])
+        handle = ctypes.c_void_p()
+        _lib.check(lib.tq4_weight_merge(arr, len(parts), ctypes.byref(handle)))
+        w = cls.__new__(cls)
+        first = parts[0]
+        w.k, w.bits, w.block_size = first.k, first.bits, first.block_size
+        w.n = sum(p.n for p in parts)
+        w.dtype, w.device, w._lib, w._handle = first.dtype, first.device, lib, handle
+        w.desc = _lib.WeightDesc()
+        ctypes.memmove(ctypes.byref(w.desc), ctypes.byref(first.desc), ctypes.sizeof(_lib.WeightDesc))
+        w.desc.N = w.n
+        return w
+
     @property
     def shape(self):
         return (self.n, self.k)
