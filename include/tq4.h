@@ -40,7 +40,7 @@ typedef enum {
   TQ4_ERR_IO = 8                /* a file given to tq4_weight_create_from cannot be opened or read */
 } tq4_status;
 
-typedef enum { TQ4_F32 = 0, TQ4_F16 = 1, TQ4_BF16 = 2, TQ4_U8 = 3 } tq4_dtype;
+typedef enum { TQ4_F32 = 0, TQ4_F16 = 1, TQ4_BF16 = 2, TQ4_U8 = 3, TQ4_S8 = 4 } tq4_dtype;
 
 /* Zero points of block_zero_points/5 (quantized.ex:306-325). */
 typedef enum { TQ4_ZP_NONE = 0, TQ4_ZP_PACKED = 1, TQ4_ZP_FLOAT = 2 } tq4_zp_kind;
@@ -49,11 +49,17 @@ typedef enum { TQ4_ZP_NONE = 0, TQ4_ZP_PACKED = 1, TQ4_ZP_FLOAT = 2 } tq4_zp_kin
  *   K, N, bits, block_size: the node attributes (quantized.ex:226-228; bits 2, 4 or 8;
  *       block_size a power of two >= 16).
  *   scale_dtype: type of the scales input (F32, F16 or BF16), N*ceil(K/block_size) values.
- *   zp_kind / zp_dtype: zero points; zp_dtype is U8 for packed zero points (N rows of
- *       ceil(blocks*bits/8) bytes) or the float type of float zero points (N*blocks values).
+ *   zp_kind / zp_dtype: zero points; zp_dtype is U8 or S8 for packed zero points (N rows of
+ *       ceil(blocks*bits/8) bytes; S8 values are sign extended like signed data) or the float
+ *       type of float zero points (N*blocks values).
  *   dequant_dtype: the float type T the weight is dequantized in. In the graph it is A's type
  *       (quantized.ex:42); for a moved model it is the scales' type after :compute_type
- *       (lib/transmuter.ex:1230-1233). */
+ *       (lib/transmuter.ex:1230-1233).
+ *   b_signed: 0 for u8 data (MatMulNBits' B is always u8). 1 for s8 data, as int4 and int2 exports
+ *       of a GatherBlockQuantized table load it (quantized.ex:294-300): each value is sign
+ *       extended and the default zero point is 0. Signed data takes no float zero points, and
+ *       with u8 packed zero points not bits 8 with bf16 dequantization (the zero point plus
+ *       2^(bits-1) that the handle stores would round). */
 typedef struct {
   int64_t K;
   int64_t N;
@@ -63,6 +69,7 @@ typedef struct {
   tq4_zp_kind zp_kind;
   tq4_dtype zp_dtype;
   tq4_dtype dequant_dtype;
+  int32_t b_signed;
 } tq4_weight_desc;
 
 typedef struct tq4_weight tq4_weight;
@@ -136,7 +143,10 @@ tq4_status tq4_matmul(const tq4_weight* w, const void* a, int64_t m, tq4_dtype a
  * serves callers that cannot call cudaMalloc, such as a NIF sharing the GPU with EXLA's client
  * (which reserves most device memory up front) or a decode loop that must not risk the device
  * synchronization of cudaMalloc/cudaFree. Its split-K scratch is a static 4 MiB device array
- * (plus 64 KiB of counters) that every GPU loading the library holds until exit; a call that
+ * (plus 64 KiB of counters), held on a GPU from the moment the library's device code is loaded
+ * there until exit. With CUDA's default lazy module loading that is the first tq4 call on that
+ * GPU, not the library load: make one tq4 call per GPU before another allocator reserves its
+ * memory, or set CUDA_MODULE_LOADING=EAGER. A call that
  * would need more is rejected with TQ4_ERR_INVALID_ARGUMENT, and M > 16 with
  * TQ4_ERR_UNSUPPORTED. The first call on a device looks up the array's device address (make it
  * before any stream capture). Calls share the array: calls that overlap on the GPU race. */

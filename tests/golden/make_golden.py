@@ -153,7 +153,9 @@ def extract(reference, case):
 
 
 def main():
-    reference = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <checkout of georgeguimaraes/transmuter>")
+    reference = sys.argv[1]
     here = os.path.dirname(os.path.abspath(__file__))
     for case in CASES:
         out = extract(reference, case)

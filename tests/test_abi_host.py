@@ -39,6 +39,7 @@ def desc(**kw):
     d.K, d.N, d.bits, d.block_size = kw.get("K", 1024), kw.get("N", 3072), kw.get("bits", 4), kw.get("bs", 32)
     d.scale_dtype, d.zp_kind, d.zp_dtype = kw.get("st", _lib.F32), kw.get("zk", _lib.ZP_NONE), kw.get("zt", _lib.U8)
     d.dequant_dtype = kw.get("dt", _lib.F32)
+    d.b_signed = kw.get("signed", 0)
     return d
 
 
@@ -47,6 +48,18 @@ def sizes(d):
     out = [ctypes.c_int64() for _ in range(3)]
     st = lib.tq4_weight_input_sizes(ctypes.byref(d), *[ctypes.byref(x) for x in out])
     return st, [x.value for x in out]
+
+
+def test_signed_data_descriptions():
+    """s8 data (GatherBlockQuantized tables of int4 exports) with no, u8 or s8 packed zero points
+    has the sizes of u8 data."""
+    for zk, zt in ((_lib.ZP_NONE, _lib.U8), (_lib.ZP_PACKED, _lib.U8), (_lib.ZP_PACKED, _lib.S8)):
+        for bits in (2, 4, 8):
+            st, got = sizes(desc(K=64, N=8, bits=bits, signed=1, zk=zk, zt=zt))
+            assert st == 0, _lib.last_error()
+            assert got == sizes(desc(K=64, N=8, bits=bits, zk=zk, zt=zt))[1]
+    st, _ = sizes(desc(signed=1, bits=8, zk=_lib.ZP_PACKED, zt=_lib.S8, dt=_lib.BF16))
+    assert st == 0  # s8 zero points stay within bf16's exact integers
 
 
 def test_input_sizes():
@@ -62,6 +75,9 @@ def test_input_sizes():
     ({"bits": 3}, 2, "bits"), ({"bs": 24}, 1, "block_size"), ({"bs": 8}, 1, "block_size"),
     ({"K": 0}, 1, "positive"), ({"zk": _lib.ZP_PACKED, "zt": _lib.F32}, 1, "packed zero points"),
     ({"dt": _lib.U8}, 1, "dequantize type"),
+    # signed (s8) data: no float zero points; 8 bits with u8 zero points not in bf16
+    ({"signed": 2}, 1, "b_signed"), ({"signed": 1, "zk": _lib.ZP_FLOAT, "zt": _lib.F32}, 2, "float zero points"),
+    ({"signed": 1, "bits": 8, "zk": _lib.ZP_PACKED, "zt": _lib.U8, "dt": _lib.BF16}, 2, "bf16"),
 ])
 def test_bad_attributes_return_status(kw, status, msg):
     st, _ = sizes(desc(**kw))

@@ -505,3 +505,80 @@ def test_merged_siblings(k, parts, bs, zp, st, t, bits):
     torch.cuda.synchronize()
     assert torch.isfinite(y1).all()
     assert device_status() == 0
+
+
+# ---- signed (s8) data: GatherBlockQuantized tables of int4/int2 exports ----------------------
+
+SIGNED = [
+    # bits, block_size, K, rows, zero points ("none", "u8", "s8"), scale type
+    (4, 32, 256, 50, "none", "f32"),
+    (4, 16, 96, 33, "u8", "f16"),
+    (4, 64, 320, 20, "s8", "bf16"),
+    (2, 32, 128, 17, "none", "f16"),
+    (2, 16, 64, 9, "u8", "f32"),
+    (2, 32, 160, 12, "s8", "bf16"),
+    (8, 32, 64, 11, "none", "bf16"),
+    (8, 16, 48, 7, "u8", "f16"),
+    (8, 32, 96, 10, "s8", "f32"),
+]
+
+
+def signed_table(bits, bs, k, rows, zp, st, seed):
+    rng = np.random.default_rng(seed)
+    data = rng.integers(-128, 128, size=(rows, k * bits // 8), dtype=np.int16).astype(np.int8)
+    blocks = -(-k // bs)
+    scales = rng.uniform(0.01, 0.5, size=(rows, blocks)).astype(np.float32)
+    scales = scales.astype(np.float16) if st == "f16" else scales
+    zrow = -(-blocks * bits // 8)
+    zeros = None
+    if zp != "none":
+        zeros = rng.integers(0, 256, size=(rows, zrow), dtype=np.int16).astype(np.uint8)
+        zeros = zeros.view(np.int8) if zp == "s8" else zeros
+    return data, scales, zeros
+
+
+def signed_oracle(bits, data, idx, scales, zeros, t):
+    """oracle.gather_block_quantized with the type T named (the oracle tells f32 and f16 arrays
+    apart by dtype; bf16 values travel as float32)."""
+    q = o.as_type(o.unpack_signed(np.take(data, idx, axis=0), bits), t)
+    shape = q.shape[:-1] + (scales.shape[-1],)
+    zp = None if zeros is None else np.take(zeros, idx, axis=0)
+    zero = o.block_zero_points(zp, shape, bits, t, signed=True)
+    return o.dequantize(q, zero, o.as_type(np.take(scales, idx, axis=0).astype(np.float32), t), t)
+
+
+@pytest.mark.parametrize("bits,bs,k,rows,zp,st", SIGNED)
+def test_gather_signed_data_bit_exact(bits, bs, k, rows, zp, st):
+    """GatherBlockQuantized over s8 data (quantized.ex:49-66 with the sign extension of
+    :294-300 and the signed zero-point default of :306-310), bit for bit against the oracle."""
+    data, scales, zeros = signed_table(bits, bs, k, rows, zp, st, seed=bits * 1000 + k + rows)
+    attrs = {"bits": bits, "block_size": bs, "gather_axis": 0, "quantize_axis": 1}
+    idx = np.array([rows - 1, 0, 3, 3, rows // 2, 1], dtype=np.int64)
+    names = ["data", "indices", "scales"] + (["zp"] if zeros is not None else [])
+    node = Node("GatherBlockQuantized", attrs, names)
+    (y,) = quantized.apply(node, [to_dev(data), to_dev(idx), to_dev(scales, st), to_dev(zeros)])
+    want = signed_oracle(bits, data, idx, scales, zeros, st)
+    if st != "bf16":  # the oracle's own entry point agrees where it can name the type
+        np.testing.assert_array_equal(want, o.gather_block_quantized(attrs, data, idx, scales, zeros))
+    got = y.float().cpu().numpy()
+    np.testing.assert_array_equal(got.view(np.uint32), np.asarray(want, np.float32).view(np.uint32))
+    assert device_status() == 0
+
+
+@pytest.mark.parametrize("bits,zp", [(4, "none"), (4, "u8"), (4, "s8"), (2, "s8"), (8, "u8")])
+def test_matmul_over_signed_table(bits, zp):
+    """A signed handle multiplies like its dequantized rows (the stored form is the unsigned
+    data with flipped top bits and raised zero points): M = 1 and M = 40 within 1e-3."""
+    k, rows, bs = 512, 96, 32
+    data, scales, zeros = signed_table(bits, bs, k, rows, zp, "f32", seed=7 + bits)
+    w = PackedWeight((k, rows, bits, bs), to_dev(data), to_dev(scales), to_dev(zeros), dtype=torch.float32,
+                     device=DEV, signed_data=True)
+    table = signed_oracle(bits, data, np.arange(rows), scales, zeros, "f32").astype(np.float64)
+    np.testing.assert_array_equal(as_np32(w.dequantize()).view(np.uint32),
+                                  table.astype(np.float32).view(np.uint32))
+    a = np.random.default_rng(3).standard_normal((40, k)).astype(np.float32)
+    for m in (1, 40):
+        y = as_np32(w.matmul(to_dev(a[:m])))
+        assert o.rel_l2(y, a[:m].astype(np.float64) @ table.T) < 1e-3
+    w.close()
+    assert device_status() == 0

@@ -75,3 +75,34 @@ def test_noalloc_rejects_beyond_its_limits():
     y = w.matmul(a)  # the allocating entry point still takes it
     torch.cuda.synchronize()
     assert torch.count_nonzero(y) == 0
+
+
+def device_status():
+    code = ctypes.c_int32()
+    _lib.check(_lib.load().tq4_device_status(0, ctypes.byref(code)))
+    return code.value
+
+
+@pytest.mark.parametrize("k,n,m,bias,at,out", [
+    (4096, 4096, 4, True, torch.float16, torch.float16),    # 2 <= M <= 8 with a bias
+    (4096, 1024, 3, False, torch.float16, torch.float32),   # f32 output from f16 activations
+    (1024, 3072, 6, True, torch.float32, torch.float16),    # f16 output from f32 activations
+    (14336, 4096, 2, True, torch.float16, torch.float16),   # split-K over the long K
+])
+def test_noalloc_bias_out_dtype_and_status(k, n, m, bias, at, out):
+    st_name = "f16" if at == torch.float16 else "f32"
+    cfg = workloads.Config(f"noalloc-{k}-{n}-{m}-{bias}-{at}-{out}", k, n, m, block_size=128 if k >= 4096 else 32,
+                           scale_type=st_name, zp="packed" if k >= 4096 else "none", a_type=st_name, bias=bias)
+    w, p = make_weight(cfg)
+    a = torch.from_numpy(np.asarray(p["A"][:m])).to(DEV, at)
+    b = torch.from_numpy(np.asarray(p["bias"])).to(DEV, at) if bias else None
+    assert device_status() == 0
+    for x in (a, -a):  # two calls in a row through the shared scratch
+        st, y = noalloc(w, x, b, out_dtype=out)
+        assert st == 0, _lib.last_error()
+        ref = w.matmul(x, b, out_dtype=out)
+        torch.cuda.synchronize()
+        assert y.dtype == out
+        err = o.rel_l2(y.double().cpu().numpy(), ref.double().cpu().numpy())
+        assert err < TOL[at], err
+        assert device_status() == 0

@@ -15,7 +15,7 @@ STATUS = {
     0: "ok", 1: "invalid argument", 2: "unsupported", 3: "CUDA error", 4: "NCCL error",
     5: "out of device memory", 6: "timed out", 7: "device-side error", 8: "file error",
 }
-F32, F16, BF16, U8 = 0, 1, 2, 3
+F32, F16, BF16, U8, S8 = 0, 1, 2, 3, 4
 ZP_NONE, ZP_PACKED, ZP_FLOAT = 0, 1, 2
 UNIQUE_ID_BYTES = 128
 
@@ -37,7 +37,7 @@ class WeightDesc(ctypes.Structure):
     _fields_ = [
         ("K", ctypes.c_int64), ("N", ctypes.c_int64), ("bits", ctypes.c_int32),
         ("block_size", ctypes.c_int32), ("scale_dtype", ctypes.c_int), ("zp_kind", ctypes.c_int),
-        ("zp_dtype", ctypes.c_int), ("dequant_dtype", ctypes.c_int),
+        ("zp_dtype", ctypes.c_int), ("dequant_dtype", ctypes.c_int), ("b_signed", ctypes.c_int32),
     ]
 
 

@@ -57,9 +57,24 @@ static tq4_status check_desc(const tq4_weight_desc* d) {
     set_error("MatMulNBits: scales and the dequantize type must be f32, f16 or bf16");
     return TQ4_ERR_INVALID_ARGUMENT;
   }
-  if (d->zp_kind == TQ4_ZP_PACKED && d->zp_dtype != TQ4_U8) {
-    set_error("MatMulNBits: packed zero points must be u8");
+  if (d->zp_kind == TQ4_ZP_PACKED && d->zp_dtype != TQ4_U8 && d->zp_dtype != TQ4_S8) {
+    set_error("MatMulNBits: packed zero points must be u8 or s8");
     return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  if (d->b_signed != 0 && d->b_signed != 1) {
+    set_error("MatMulNBits: b_signed must be 0 (u8 data) or 1 (s8 data), got %d", d->b_signed);
+    return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  // Signed data is stored as unsigned data with each value's top bit flipped and every zero
+  // point raised by 2^(bits-1) (the same differences q - z); that raised zero point must be exact.
+  if (d->b_signed && d->zp_kind == TQ4_ZP_FLOAT) {
+    set_error("MatMulNBits: signed data with float zero points is not supported");
+    return TQ4_ERR_UNSUPPORTED;
+  }
+  if (d->b_signed && d->zp_kind == TQ4_ZP_PACKED && d->zp_dtype == TQ4_U8 && d->bits == 8 &&
+      d->dequant_dtype == TQ4_BF16) {
+    set_error("MatMulNBits: signed 8-bit data with u8 zero points cannot be dequantized in bf16");
+    return TQ4_ERR_UNSUPPORTED;
   }
   if (d->zp_kind == TQ4_ZP_FLOAT && !is_float(d->zp_dtype)) {
     set_error("MatMulNBits: float zero points must be f32, f16 or bf16");
@@ -148,9 +163,9 @@ static tq4_status merge_handles(const tq4_weight* const* parts, int count, tq4_w
     const tq4_weight_desc& di = p->desc;
     if (di.K != d0.K || di.bits != d0.bits || di.block_size != d0.block_size || di.scale_dtype != d0.scale_dtype ||
         di.zp_kind != d0.zp_kind || (di.zp_kind != TQ4_ZP_NONE && di.zp_dtype != d0.zp_dtype) ||
-        di.dequant_dtype != d0.dequant_dtype || p->device != parts[0]->device) {
+        di.dequant_dtype != d0.dequant_dtype || di.b_signed != d0.b_signed || p->device != parts[0]->device) {
       set_error("tq4_weight_merge: part %d differs from part 0 (K, bits, block_size, scale or zero-point type, "
-                "dequantize type or device)", i);
+                "dequantize type, signedness or device)", i);
       return TQ4_ERR_INVALID_ARGUMENT;
     }
     n += di.N;

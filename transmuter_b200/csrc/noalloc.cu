@@ -7,8 +7,11 @@
 // cannot afford cudaMalloc / cudaFree, which may synchronize the whole device. tq4_matmul grows a
 // per-stream split-K workspace with cudaMalloc on first use; this entry point never allocates.
 //
-// Its scratch is a file-scope __device__ array of a fixed size, which every GPU that loads the
-// library holds until the process exits. Host code cannot pass the array's name to a kernel (on
+// Its scratch is a file-scope __device__ array of a fixed size. A GPU holds it from the moment
+// the library's device code is loaded there until the process exits; under CUDA's default lazy
+// module loading that is the first tq4 call on that GPU (any entry point), not the dlopen of the
+// library, so a caller that shares the GPU with a preallocating allocator makes one tq4 call per
+// GPU before that allocator starts, or runs with CUDA_MODULE_LOADING=EAGER. Host code cannot pass the array's name to a kernel (on
 // the host that name is only a stand-in, not a device address), so the first call on each device
 // looks up the device address with cudaGetSymbolAddress, with that device current, and keeps it.
 // That first call should therefore come before any stream capture. All calls share the one

@@ -211,6 +211,12 @@ __global__ void __launch_bounds__(kExThreads) push_finish_kernel(PeerArgs pa, un
                                                                  int nranks, const uint8_t* assembly,
                                                                  int64_t half_bytes, uint8_t* y, int64_t y_bytes) {
   __shared__ int s_ok;
+  // Launched with programmatic dependent launch: the GEMV before it has finished (its stores to
+  // every rank's buffer performed) once pdl_wait() returns. Only then may the next call's GEMV
+  // start, and its weight loads (all it does before its own pdl_wait) overlap this kernel's wait
+  // for the peers and its copy.
+  pdl_wait();
+  pdl_trigger();
   const unsigned long long epoch = *reinterpret_cast<volatile unsigned long long*>(own + kFlagEpoch) + 1;
   if (threadIdx.x == 0) {
     if (blockIdx.x == 0) {
@@ -226,7 +232,7 @@ __global__ void __launch_bounds__(kExThreads) push_finish_kernel(PeerArgs pa, un
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     int64_t head = 0;
-    if ((reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    if (((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(src)) & 15) == 0) {
       const int64_t n16 = y_bytes / 16;
       for (int64_t i = tid; i < n16; i += stride)
         reinterpret_cast<uint4*>(y)[i] = __ldcg(reinterpret_cast<const uint4*>(src) + i);
@@ -414,14 +420,19 @@ static tq4_status ensure_slices(tq4_sharded* s, NcclApi* api, int64_t bytes, cud
   return TQ4_OK;
 }
 
-// Collective: the M = 1 assembly buffers (2 x N outputs of up to 4 bytes), mapped by every peer.
+// Elements of one half of an assembly buffer: N rounded up to 16, so that the second half starts
+// 16-byte aligned for 2- and 4-byte outputs (push_finish_kernel copies it in 16-byte words).
+static int64_t assembly_half_elems(const tq4_sharded* s) { return (s->desc.N + 15) / 16 * 16; }
+
+// Collective: the M = 1 assembly buffers (2 halves of N outputs of up to 4 bytes), mapped by every
+// peer.
 static tq4_status ensure_assembly(tq4_sharded* s, NcclApi* api, cudaStream_t st) {
   TQ4_TRY(ensure_flags(s, api, st));
   if (!s->flags_ok || s->asm_tried) return TQ4_OK;
   TQ4_TRY(not_capturing(st));
   TQ4_CUDA(cudaStreamSynchronize(st));
   s->asm_tried = true;
-  TQ4_TRY(s->assembly.alloc(2 * s->desc.N * 4));
+  TQ4_TRY(s->assembly.alloc(2 * assembly_half_elems(s) * 4));
   return map_set(s, api, s->assembly.ptr, s->peer_asm, &s->asm_ok, st);
 }
 
@@ -651,7 +662,7 @@ tq4_status tq4_sharded_matmul(const tq4_sharded* cs, const void* a, int64_t m, t
         dst.ndst = (int)P;
         dst.col0 = s->first;
         dst.epoch = static_cast<const unsigned long long*>(s->flags.ptr) + kFlagEpoch;
-        dst.half_elems = s->desc.N;
+        dst.half_elems = assembly_half_elems(s);
         const void* lb = bias ? static_cast<const uint8_t*>(bias) + s->first * dtype_size(bias_t) : nullptr;
         TQ4_TRY(run_gemv_rows(*s->local, a, a_t, lb, bias_t, y_t, dst, ctr, st));
       }
@@ -659,11 +670,10 @@ tq4_status tq4_sharded_matmul(const tq4_sharded* cs, const void* a, int64_t m, t
       for (int q = 0; q < P; ++q) pa.flags[q] = static_cast<unsigned long long*>(s->peer_flags[q]);
       const int64_t y_bytes = s->desc.N * ys;
       const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((y_bytes / 16 + kExThreads - 1) / kExThreads, 148));
-      push_finish_kernel<<<grid, kExThreads, 0, st>>>(pa, static_cast<unsigned long long*>(s->flags.ptr),
-                                                      s->comm->rank, (int)P,
-                                                      static_cast<const uint8_t*>(s->assembly.ptr), y_bytes,
-                                                      static_cast<uint8_t*>(y), y_bytes);
-      TQ4_CUDA(cudaGetLastError());
+      TQ4_CUDA(launch_pdl(push_finish_kernel, dim3(grid), dim3(kExThreads), 0, st, pa,
+                          static_cast<unsigned long long*>(s->flags.ptr), s->comm->rank, (int)P,
+                          static_cast<const uint8_t*>(s->assembly.ptr), assembly_half_elems(s) * ys,
+                          static_cast<uint8_t*>(y), y_bytes));
       return TQ4_OK;
     }
   }

@@ -13,10 +13,13 @@ __device__ long long g_wait_cycles = 2000000000LL;  // about one second at the B
 
 // One thread per output 32-bit word of the packed layout: gathers its 32/BITS elements from
 // the raw rows (element k of row n = bits [(k%per)*BITS, ...) of byte k/per, packed.ex:11-23).
+// `flip` is 2^(BITS-1) for signed data, 0 otherwise: a signed value v (sign extended,
+// quantized.ex:294-300) is stored as u = v + 2^(BITS-1), which is the raw bits with the top bit
+// flipped, and its zero point is raised by the same amount, so q - z is unchanged.
 template <int BITS>
 __global__ void repack_kernel(const uint8_t* __restrict__ raw, int64_t raw_row_bytes,
                               int64_t n_rows, int64_t k_valid, uint32_t* __restrict__ out,
-                              int64_t row_bytes, int64_t n_pad) {
+                              int64_t row_bytes, int64_t n_pad, uint32_t flip) {
   constexpr int PER = 8 / BITS;
   constexpr int MASK = (1 << BITS) - 1;
   const int64_t words_per_row = row_bytes / 4;
@@ -49,7 +52,7 @@ __global__ void repack_kernel(const uint8_t* __restrict__ raw, int64_t raw_row_b
         const int64_t k = c * (512 / BITS) + 16 * j + 4 * t + e;
         if (k < k_valid) {
           const uint8_t byte = raw[n * raw_row_bytes + k / PER];
-          const uint32_t v = (byte >> ((k % PER) * BITS)) & MASK;
+          const uint32_t v = ((byte >> ((k % PER) * BITS)) & MASK) ^ flip;
           word |= v << (slot * BITS);
         }
       }
@@ -76,12 +79,13 @@ __global__ void convert_blocks_kernel(const void* __restrict__ src, tq4_dtype sr
 }
 
 // Packed zero points: row r holds ceil(blocks*bits/8) bytes (the reshape to {N, :auto} of
-// quantized.ex:316-322); value b of the row is unpacked like B and cast to T (exact), stored
-// block-major like the scales.
+// quantized.ex:316-322); value b of the row is unpacked like B (sign extended when the zero
+// points are s8), raised by `offset` (2^(bits-1) for signed data, see repack_kernel) and cast to
+// T (exact), stored block-major like the scales.
 template <typename T>
 __global__ void unpack_zp_kernel(const uint8_t* __restrict__ zp, int64_t zp_row_bytes, int bits,
                                  int64_t n, int64_t blocks, T* __restrict__ dst, int64_t n_pad,
-                                 int64_t blocks_pad) {
+                                 int64_t blocks_pad, int zp_signed, float offset) {
   const int per = 8 / bits, mask = (1 << bits) - 1;
   const int64_t total = n_pad * blocks_pad;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -90,7 +94,9 @@ __global__ void unpack_zp_kernel(const uint8_t* __restrict__ zp, int64_t zp_row_
     float v = 0.f;
     if (r < n && b < blocks) {
       const uint8_t byte = zp[r * zp_row_bytes + b / per];
-      v = (float)((byte >> ((b % per) * bits)) & mask);
+      int q = (byte >> ((b % per) * bits)) & mask;
+      if (zp_signed && q >= (1 << (bits - 1))) q -= 1 << bits;
+      v = (float)q + offset;
     }
     dst[i] = from_f32<T>(v);
   }
@@ -160,8 +166,10 @@ template <typename T>
 static void launch_unpack_zp(const Weight& w, const uint8_t* zp, T* dst, cudaStream_t st) {
   const int64_t total = w.n_pad * w.blocks_pad;
   const int64_t zp_row = (w.blocks * w.desc.bits + 7) / 8;
-  unpack_zp_kernel<T><<<grid_for(total, 256), 256, 0, st>>>(zp, zp_row, w.desc.bits, w.desc.N,
-                                                              w.blocks, dst, w.n_pad, w.blocks_pad);
+  const float offset = w.desc.b_signed ? (float)(1 << (w.desc.bits - 1)) : 0.f;
+  unpack_zp_kernel<T><<<grid_for(total, 256), 256, 0, st>>>(zp, zp_row, w.desc.bits, w.desc.N, w.blocks, dst,
+                                                              w.n_pad, w.blocks_pad, w.desc.zp_dtype == TQ4_S8,
+                                                              offset);
 }
 
 // Per-row bound of the f32 weights: wexp[n] with max_b |s_b| * max(|z_b|, |2^bits - 1 - z_b|) <= 2^wexp[n]
@@ -218,9 +226,10 @@ tq4_status prepare_weight(Weight& w, const Source& b_src, const Source& s_src, c
   const int64_t k_valid = w.blocks * d.block_size;
   uint32_t* qdst = static_cast<uint32_t*>(w.q.ptr);
   const uint8_t* rb = static_cast<const uint8_t*>(raw_b.ptr);
-  if (d.bits == 4) repack_kernel<4><<<grid, 256, 0, st>>>(rb, raw_row, d.N, k_valid, qdst, w.row_bytes, w.n_pad);
-  else if (d.bits == 2) repack_kernel<2><<<grid, 256, 0, st>>>(rb, raw_row, d.N, k_valid, qdst, w.row_bytes, w.n_pad);
-  else repack_kernel<8><<<grid, 256, 0, st>>>(rb, raw_row, d.N, k_valid, qdst, w.row_bytes, w.n_pad);
+  const uint32_t flip = d.b_signed ? 1u << (d.bits - 1) : 0u;
+  if (d.bits == 4) repack_kernel<4><<<grid, 256, 0, st>>>(rb, raw_row, d.N, k_valid, qdst, w.row_bytes, w.n_pad, flip);
+  else if (d.bits == 2) repack_kernel<2><<<grid, 256, 0, st>>>(rb, raw_row, d.N, k_valid, qdst, w.row_bytes, w.n_pad, flip);
+  else repack_kernel<8><<<grid, 256, 0, st>>>(rb, raw_row, d.N, k_valid, qdst, w.row_bytes, w.n_pad, flip);
   TQ4_CUDA(cudaGetLastError());
 
   switch (d.dequant_dtype) {

@@ -26,7 +26,8 @@ import torch
 from . import _lib
 from .deferred import ArgumentError, DeferredTensor, shape_type
 
-TORCH_TO_TQ4 = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16, torch.uint8: _lib.U8}
+TORCH_TO_TQ4 = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16, torch.uint8: _lib.U8,
+                torch.int8: _lib.S8}
 TQ4_TO_TORCH = {v: k for k, v in TORCH_TO_TQ4.items()}
 NAME_TO_TORCH = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
 
@@ -99,15 +100,17 @@ def _source(x, nbytes):
 
 class PackedWeight:
     """A MatMulNBits weight held packed on one GPU by a tq4 handle (the "B:packed" value of a
-    moved model). ``dtype`` is the type T it dequantizes in."""
+    moved model). ``dtype`` is the type T it dequantizes in. ``signed_data`` takes s8 data (a
+    GatherBlockQuantized table of an int4 export; MatMulNBits' B is always u8): its values are
+    sign extended and the default zero point is 0 (quantized.ex:294-325)."""
 
-    def __init__(self, attrs, b, scales, zero_points=None, dtype=None, device=None):
+    def __init__(self, attrs, b, scales, zero_points=None, dtype=None, device=None, signed_data=False):
         k, n, bits, bs = attrs
         self.k, self.n, self.bits, self.block_size = k, n, bits, bs
         b_type, s_type = shape_type(b)[1], shape_type(scales)[1]
         z_type = shape_type(zero_points)[1] if zero_points is not None else None
-        if b_type != torch.uint8:
-            raise ArgumentError(f"MatMulNBits B must be u8, got {b_type}")
+        if b_type != (torch.int8 if signed_data else torch.uint8):
+            raise ArgumentError(f"MatMulNBits B must be {'s8' if signed_data else 'u8'}, got {b_type}")
         if s_type not in (torch.float32, torch.float16, torch.bfloat16):
             raise ArgumentError(f"MatMulNBits scales must be a float tensor, got {s_type}")
         self.dtype = dtype or s_type
@@ -115,14 +118,15 @@ class PackedWeight:
         desc.K, desc.N, desc.bits, desc.block_size = k, n, bits, bs
         desc.scale_dtype = TORCH_TO_TQ4[s_type]
         desc.dequant_dtype = TORCH_TO_TQ4[self.dtype]
+        desc.b_signed = 1 if signed_data else 0
         if zero_points is None:
             desc.zp_kind, desc.zp_dtype = _lib.ZP_NONE, _lib.U8
-        elif z_type == torch.uint8:
-            desc.zp_kind, desc.zp_dtype = _lib.ZP_PACKED, _lib.U8
+        elif z_type in (torch.uint8, torch.int8):
+            desc.zp_kind, desc.zp_dtype = _lib.ZP_PACKED, TORCH_TO_TQ4[z_type]
         elif z_type in (torch.float32, torch.float16, torch.bfloat16):
             desc.zp_kind, desc.zp_dtype = _lib.ZP_FLOAT, TORCH_TO_TQ4[z_type]
         else:
-            raise ArgumentError(f"MatMulNBits zero points must be u8 or float, got {z_type}")
+            raise ArgumentError(f"MatMulNBits zero points must be u8, s8 or float, got {z_type}")
         self.desc = desc
         if device is None:
             device = b.device if isinstance(b, torch.Tensor) and b.is_cuda else torch.device("cuda", torch.cuda.current_device())
@@ -281,8 +285,8 @@ def op(node, inputs):
         qa = attr(node, "quantize_axis", 1)
         if attr(node, "gather_axis", 0) != 0 or (qa % rank if qa is not None else rank - 1) != rank - 1:
             raise ArgumentError("GatherBlockQuantized supports gather_axis 0 and quantize_axis on the last axis")
-        if data.dtype != torch.uint8 or rank != 2:
-            raise ArgumentError("GatherBlockQuantized supports u8 data of rank 2")
+        if data.dtype not in (torch.uint8, torch.int8) or rank != 2:
+            raise ArgumentError("GatherBlockQuantized supports u8 or s8 data of rank 2")
         bits = attr(node, "bits", 4)
         bs = attr(node, "block_size", 128)
         rows, cols = data.shape
@@ -293,7 +297,8 @@ def op(node, inputs):
         # the table as a MatMulNBits weight: rows of B are rows of the table (same bit order)
         w = PackedWeight((k, rows, bits, bs), data.reshape(-1), scales.reshape(-1),
                          zero_points.reshape(-1) if zero_points is not None else None,
-                         dtype=scales.dtype, device=indices.device if indices.is_cuda else None)
+                         dtype=scales.dtype, device=indices.device if indices.is_cuda else None,
+                         signed_data=data.dtype == torch.int8)
         try:
             return w.gather(indices)
         finally:
