@@ -514,7 +514,7 @@ def decoder_bench(args, rank, world, local_rank):
     token (28 layers, lm_head, argmax) with the position and token in device memory. N > 1 runs
     independent replicas (the decoder does not shard)."""
     import zlib
-    from transmuter_b200.decoder import QWEN3_0_6B, Q4Decoder
+    from transmuter_b200.decoder import QWEN3_0_6B, Q4Decoder, random_weights, split_siblings
     cfg = QWEN3_0_6B
     seed = zlib.crc32(b"c4")
     config = {"workload": "c4 Qwen3-0.6B-shaped q4 decoder, batch 1, f32 KV cache",
@@ -547,7 +547,8 @@ def decoder_bench(args, rank, world, local_rank):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     config["parallelism"] = "single GPU" if world == 1 else f"{world} independent replicas"
-    dec = Q4Decoder(cfg, seed=seed, device=dev)
+    # q, k, v and gate, up as separate inputs (as an ONNX export stores them), merged at load
+    dec = Q4Decoder(cfg, device=dev, weights=split_siblings(random_weights(cfg, seed), cfg))
     prompt = np.random.default_rng(seed + rank).integers(0, cfg.vocab, DECODE_PROMPT)
     dec.reset(prompt)
     dec.capture()

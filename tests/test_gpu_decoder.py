@@ -19,7 +19,7 @@ import torch.nn.functional as F
 from oracle import matmul_nbits as o
 from oracle.decoder import OracleDecoder
 from transmuter_b200 import _lib
-from transmuter_b200.decoder import QWEN3_0_6B, DecoderConfig, Q4Decoder, random_weights, rope_tables
+from transmuter_b200.decoder import QWEN3_0_6B, DecoderConfig, Q4Decoder, random_weights, rope_tables, split_siblings
 
 pytestmark = pytest.mark.gpu
 
@@ -54,6 +54,22 @@ def test_tiny_decoder_matches_oracle(tiny):
     for i in range(len(logits)):
         assert o.rel_l2(logits[i], ref_logits[i]) < LOGIT_TOL, i
     assert np.array_equal(tokens, ref_tokens)
+
+
+def test_separate_sibling_inputs_merge_into_the_same_decoder(tiny):
+    """q, k, v and gate, up given as separate MatMulNBits inputs (an ONNX export) are merged at
+    load by tq4_weight_merge: the merged handles equal the pre-merged ones bit for bit, so the
+    logits and tokens are identical."""
+    weights, prompt, ref_tokens, _ = tiny
+    merged = Q4Decoder(TINY, weights=weights)
+    separate = Q4Decoder(TINY, weights=split_siblings(weights, TINY))
+    assert sorted(separate.weights) == sorted(merged.weights)
+    for name in merged.weights:
+        assert torch.equal(separate.weights[name].dequantize(), merged.weights[name].dequantize()), name
+    want_tokens, want_logits = step_logits(merged, prompt, 8)
+    got_tokens, got_logits = step_logits(separate, prompt, 8)
+    assert np.array_equal(got_tokens, want_tokens) and np.array_equal(got_tokens, ref_tokens)
+    assert np.array_equal(got_logits, want_logits)
 
 
 def test_tiny_graph_replay_matches_eager(tiny):

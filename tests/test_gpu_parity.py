@@ -207,6 +207,53 @@ def test_large_m_parity(k, n, m, bits, bs, zp, st, at, t, bias):
     assert o.rel_l2(got, want) < TOL[at], o.rel_l2(got, want)
 
 
+# 2- and 8-bit weights on the tensor-core GEMM (quantized.ex:226-240 takes bits 2, 4 and 8 on one
+# path): a stage of 128 k is two packed groups of 8-bit weights or half a group of 2-bit weights.
+# K not a multiple of 128 (the last 8-bit stage's second group lies past the row), f32 weights
+# (row exponent), bf16 with 8 bits (exact q through f32), narrow tiles (two CTAs per SM) and K
+# split over a cluster.
+LOW_HIGH_BITS = [
+    (1024, 384, 130, 8, 32, "packed", "f16", "f16", "f16", True),
+    (320, 256, 64, 8, 32, "none", "f16", "f16", "f16", False),
+    (1024, 300, 200, 8, 64, "float", "bf16", "bf16", "bf16", True),
+    (512, 256, 129, 8, 128, "packed", "bf16", "bf16", "bf16", False),
+    (1024, 256, 48, 8, 32, "none", "f32", "f32", "f32", True),
+    (4096, 512, 256, 8, 128, "packed", "f16", "f16", "f16", False),
+    (1024, 384, 130, 2, 32, "packed", "f16", "f16", "f16", True),
+    (640, 256, 64, 2, 16, "none", "bf16", "bf16", "bf16", False),
+    (1024, 300, 200, 2, 64, "float", "f16", "f16", "f16", False),
+    (512, 256, 40, 2, 32, "packed", "f32", "f32", "f32", True),
+    (4096, 512, 256, 2, 128, "packed", "bf16", "bf16", "bf16", True),
+    (1024, 128, 12, 2, 32, "packed", "f16", "f16", "f16", False),
+    (1024, 128, 16, 8, 32, "packed", "f16", "bf16", "f16", False),
+]
+
+
+@pytest.mark.parametrize("k,n,m,bits,bs,zp,st,at,t,bias", LOW_HIGH_BITS)
+def test_two_and_eight_bit_gemm_parity(k, n, m, bits, bs, zp, st, at, t, bias):
+    got, want, _ = run_case(k, n, m, bits, bs, zp, st, at, t, bias)
+    assert np.isfinite(got).all()
+    assert o.rel_l2(got, want) < TOL[at], o.rel_l2(got, want)
+
+
+@pytest.mark.parametrize("bits", [2, 8])
+def test_two_and_eight_bit_prefill_runs_on_the_tensor_core_gemm(bits):
+    """A prefill-sized call with 2- or 8-bit weights is one gemm_kernel launch, not GEMV slices."""
+    cfg = workloads.Config(f"route-{bits}", 1024, 512, 256, bits=bits, block_size=32, scale_type="f16",
+                           zp="packed", a_type="f16")
+    p = workloads.make(cfg)
+    w = weight_for(cfg, p, "f16")
+    a = to_dev(p["A"], "f16")
+    w.matmul(a)
+    torch.cuda.synchronize()
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        w.matmul(a)
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if "kernel" in e.name]
+    assert any("gemm_kernel" in n for n in names), names
+    assert not any("gemv" in n for n in names), names
+
+
 # f32 activations at M > 16 take the tensor cores as row-scaled f16 (and f32 weights as
 # row-scaled f16); the rel-L2 1e-3 bar of f32 activations still holds, for ordinary, wide and
 # tiny scales (the latter would sit in f16's subnormal range without the row exponent).

@@ -69,3 +69,21 @@ def test_rope_tables_identity_at_position_zero():
     cos, sin = rope_tables(TINY)
     assert np.all(cos[0] == 1) and np.all(sin[0] == 0)
     assert cos.shape == (TINY.max_len, TINY.head_dim // 2)
+
+
+def test_split_siblings_are_row_ranges_of_the_merged_projections():
+    """split_siblings gives the separate q/k/v and gate/up inputs of an ONNX export; their rows
+    concatenated are the merged projections (what tq4_weight_merge builds on the GPU)."""
+    from transmuter_b200.decoder import SIBLINGS, sibling_sizes, split_siblings
+    weights = random_weights(TINY, seed=5)
+    parts = split_siblings(weights, TINY)
+    sizes = sibling_sizes(TINY)
+    for layer in range(TINY.layers):
+        for merged, names in SIBLINGS.items():
+            b, s = weights[f"{layer}.{merged}"]
+            pb = [parts[f"{layer}.{n}"][0] for n in names]
+            ps = [parts[f"{layer}.{n}"][1] for n in names]
+            assert [x.shape[0] for x in pb] == sizes[merged]
+            assert np.array_equal(np.concatenate(pb), b) and np.array_equal(np.concatenate(ps), s)
+            assert f"{layer}.{merged}" not in parts
+    assert parts["lm_head"][0] is weights["lm_head"][0]

@@ -5,10 +5,11 @@
 //
 // computed as Y^T tile = W tile . A tile^T: a CTA takes 128 weight rows (the MMA's M, one TMEM
 // lane each) and TM activation rows (the MMA's N, 32..256). Per stage of 128 k (one 64-byte
-// packed group):
+// packed group of 4-bit weights; two groups of 8-bit weights; half a group of 2-bit weights,
+// whose group of 256 k is loaded whole by both of its stages):
 //   warp 0   TMA producer: the activation tile (two 64-k boxes, 128B swizzle: the K-major B
-//            operand), the packed weight tile (128 rows x 64 bytes) and the stage's block-major
-//            scales / zero points, completing on full[s].
+//            operand), the packed weight tile (128 rows x 64 bytes per group) and the stage's
+//            block-major scales / zero points, completing on full[s].
 //   warps 2-17 dequantise in registers: warp w owns TMEM lanes 32*(w%4).. (its 32 weight rows)
 //            and one 16-byte piece of each row (32 weights spread over the stage's k; the packed
 //            tile arrives with the 64-byte swizzle, so these loads are free of bank conflicts);
@@ -92,6 +93,43 @@ __device__ __forceinline__ void q_pairs4(uint32_t x, int j, bool bf, uint32_t& p
   }
 }
 
+// The pairs (e0, e1) and (e2, e3) of stage position j (k = 16j + 4tp + e) as O + q in the MMA
+// type, O = 1024 (f16) or 128 (bf16), for 2- and 8-bit weights (4-bit: q_pairs4 and the fused
+// path). `x` is the packed word holding position j and `sh` the shift of its pair within it, in
+// packed_position's order: 8 bits, byte e of the word; 2 bits, bits 4jj + 16(e & 1) + 2(e >> 1)
+// for jj = j mod 4. 8-bit weights only in f16 (128 + q is not exact in bf16 from q = 128).
+template <int BITS, bool BF>
+__device__ __forceinline__ void magic_pairs(uint32_t x, int sh, uint32_t& pa, uint32_t& pb) {
+  constexpr uint32_t M = BF ? 0x43004300u : 0x64006400u;
+  if constexpr (BITS == 8) {
+    static_assert(!BF, "8-bit magic pairs are f16 only");
+    pa = __byte_perm(x, 0x64646464u, 0x4140);  // bytes 0, 1 under the f16 exponent of 1024
+    pb = __byte_perm(x, 0x64646464u, 0x4342);
+  } else {
+    static_assert(BITS == 2, "4-bit weights take q_pairs4");
+    const uint32_t src = x >> sh;
+    pa = lop3_and_or(src, 0x00030003u, M);
+    pb = lop3_and_or(src >> 2, 0x00030003u, M);
+  }
+}
+
+// q of the pairs (e0, e1) and (e2, e3) as exact values of the MMA type (2- and 8-bit weights).
+template <int BITS, bool BF>
+__device__ __forceinline__ void exact_pairs(uint32_t x, int sh, uint32_t& q0, uint32_t& q1) {
+  if constexpr (BITS == 8 && BF) {  // q <= 255: exact in bf16
+    __nv_bfloat162 a = __floats2bfloat162_rn((float)(x & 0xFFu), (float)((x >> 8) & 0xFFu));
+    __nv_bfloat162 b = __floats2bfloat162_rn((float)((x >> 16) & 0xFFu), (float)(x >> 24));
+    q0 = *reinterpret_cast<uint32_t*>(&a);
+    q1 = *reinterpret_cast<uint32_t*>(&b);
+  } else {
+    constexpr uint32_t M = BF ? 0x43004300u : 0x64006400u;
+    uint32_t pa, pb;
+    magic_pairs<BITS, BF>(x, sh, pa, pb);
+    q0 = h2_sub(pa, M, BF);
+    q1 = h2_sub(pb, M, BF);
+  }
+}
+
 // (q - z) * s of one pair in the MMA type. T_SAME: T is the MMA type (exact reference math in
 // packed f16x2/bf16x2); otherwise computed in f32 with T's roundings, then converted.
 template <bool BF, tq4_dtype T>
@@ -156,7 +194,7 @@ struct GemmArgs {
   int bs_log2;
   int nb;          // scale blocks per stage (the TMA box height)
   int M, N, K;
-  int ktiles;      // 64-byte groups per row
+  int ktiles;      // 128-k stages per row
   int stages;
   int stage_bytes;
   int sc_off, zc_off;  // offsets of the staged scales / zero points within a stage
@@ -180,10 +218,12 @@ constexpr int kMaxStages = 8;      // shared-memory stages
 constexpr int kASlots = 4;         // dequantised weight stages in TMEM, 64 columns each (at most)
 constexpr int kSmemSM = 233472;    // shared memory of an SM
 
-template <int TM>
+// A stage covers 128 k: the packed weights of one 64-byte group for 4 bits, two groups for 8
+// bits, and for 2 bits the group of 256 k whose half the stage uses (the group is loaded whole).
+template <int TM, int BITS>
 struct GemmTile {
   static constexpr int ACT_BYTES = TM * 128 * 2;  // TM rows x 128 k x 2 B (two SW128 halves)
-  static constexpr int WP_BYTES = WN * 64;        // packed
+  static constexpr int WP_BYTES = WN * (BITS == 8 ? 128 : 64);  // packed
   static constexpr int FIXED = ACT_BYTES + WP_BYTES;
   static_assert(TM % 32 == 0 && TM >= 32 && TM <= 256, "MMA N");
   // Tiles of at most 64 activation rows: 3 weight slots in 256 TMEM columns, two CTAs per SM (the
@@ -195,12 +235,12 @@ struct GemmTile {
   static_assert(TM + SLOTS * 64 <= COLS && SLOTS <= kASlots, "TMEM columns");
 };
 
-template <int TM, bool BF, tq4_dtype T>
-__global__ void __launch_bounds__(kGemmThreads, GemmTile<TM>::CTAS)
+template <int TM, bool BF, tq4_dtype T, int BITS>
+__global__ void __launch_bounds__(kGemmThreads, GemmTile<TM, BITS>::CTAS)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                 const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_z,
                 const GemmArgs p) {
-  using L = GemmTile<TM>;
+  using L = GemmTile<TM, BITS>;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -261,6 +301,17 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM>::CTAS)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+      // The packed weights of stage kt (absolute): 64-byte groups of 512 / BITS k each.
+      auto load_w = [&](uint32_t st, int kt, uint32_t bar) {
+        if constexpr (BITS == 8) {
+          tma_load_2d(st + L::ACT_BYTES, &map_w, kt * 128, n0, bar);
+          tma_load_2d(st + L::ACT_BYTES + WN * 64, &map_w, kt * 128 + 64, n0, bar);
+        } else if constexpr (BITS == 2) {
+          tma_load_2d(st + L::ACT_BYTES, &map_w, (kt >> 1) * 64, n0, bar);
+        } else {
+          tma_load_2d(st + L::ACT_BYTES, &map_w, kt * 64, n0, bar);
+        }
+      };
       // The first ring's weights, scales and zero points are constant: they load before the
       // previous kernel on the stream has finished (programmatic dependent launch); the
       // activations of those stages follow once it has.
@@ -269,7 +320,7 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM>::CTAS)
         const uint32_t st = base + kt * p.stage_bytes;
         const int b0 = ((kt0 + kt) * 128) >> p.bs_log2;
         mbar_expect_tx(wfull(kt), tx_w);
-        tma_load_2d(st + L::ACT_BYTES, &map_w, (kt0 + kt) * 64, n0, wfull(kt));
+        load_w(st, kt0 + kt, wfull(kt));
         tma_load_2d(st + p.sc_off, &map_s, n0, b0, wfull(kt));
         if (p.has_zp) tma_load_2d(st + p.zc_off, &map_z, n0, b0, wfull(kt));
       }
@@ -288,7 +339,7 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM>::CTAS)
         const uint32_t st = base + s * p.stage_bytes;
         const int b0 = ((kt0 + kt) * 128) >> p.bs_log2;
         mbar_expect_tx(wfull(s), tx_w);
-        tma_load_2d(st + L::ACT_BYTES, &map_w, (kt0 + kt) * 64, n0, wfull(s));
+        load_w(st, kt0 + kt, wfull(s));
         tma_load_2d(st + p.sc_off, &map_s, n0, b0, wfull(s));
         if (p.has_zp) tma_load_2d(st + p.zc_off, &map_z, n0, b0, wfull(s));
         mbar_expect_tx(full(s), tx_a);
@@ -345,7 +396,11 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM>::CTAS)
       const uint8_t* st = smem + s * p.stage_bytes;
       // the 64-byte swizzle puts piece tp of row r at 16 * (tp ^ ((r >> 1) & 3)): the 8 lanes of
       // each load phase read 8 different bank groups
-      const uint4 v = *reinterpret_cast<const uint4*>(st + L::ACT_BYTES + r * 64 + ((tp ^ ((r >> 1) & 3)) << 4));
+      const uint32_t piece = r * 64 + ((tp ^ ((r >> 1) & 3)) << 4);
+      const uint4 v = *reinterpret_cast<const uint4*>(st + L::ACT_BYTES + piece);
+      // 8 bits: the stage's second group (positions j = 4..7); 2 bits: which half of the group
+      const uint4 v1 = BITS == 8 ? *reinterpret_cast<const uint4*>(st + L::ACT_BYTES + WN * 64 + piece) : v;
+      const int half = (kt0 + kt) & 1;
       const uint8_t* sc = st + p.sc_off;
       const uint8_t* zc = st + p.zc_off;
       const int b0 = ((kt0 + kt) * 128) >> p.bs_log2;
@@ -356,9 +411,20 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM>::CTAS)
       for (int j = 0; j < 8; ++j) {
         const int lb = (((kt0 + kt) * 128 + 16 * j) >> p.bs_log2) - b0;  // staged block row
         const bool new_block = (j == 0) || (((16 * j) & ((1 << p.bs_log2) - 1)) == 0);
-        const uint32_t x = (j < 2) ? v.x : (j < 4) ? v.y : (j < 6) ? v.z : v.w;
+        uint32_t x;
+        int sh = 0;
+        if constexpr (BITS == 4) {
+          x = (j < 2) ? v.x : (j < 4) ? v.y : (j < 6) ? v.z : v.w;
+        } else if constexpr (BITS == 8) {
+          const uint4& vv = j < 4 ? v : v1;
+          x = ((j & 3) == 0) ? vv.x : ((j & 3) == 1) ? vv.y : ((j & 3) == 2) ? vv.z : vv.w;
+        } else {
+          x = half ? ((j < 4) ? v.z : v.w) : ((j < 4) ? v.x : v.y);
+          sh = 4 * (j & 3);
+        }
         uint32_t w0, w1;
-        if ((T_SAME || (T == TQ4_F32 && p.s16)) && p.int_zp) {
+        constexpr bool kFusedOk = !(BF && BITS == 8);
+        if (kFusedOk && (T_SAME || (T == TQ4_F32 && p.s16)) && p.int_zp) {
           // (O + q) - (O + z) is exact in the MMA type; one more multiply gives RN_T((q - z) * s)
           // (f32 weights: times the f16 s * 2^-we of the handle's scales16)
           if (new_block) {
@@ -370,7 +436,12 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM>::CTAS)
           }
           const uint32_t src = (j & 1) ? (x >> 8) : x;
           uint32_t d0, d1;
-          if (!BF) {
+          if constexpr (BITS != 4 && kFusedOk) {
+            uint32_t pa, pb;
+            magic_pairs<BITS, BF>(x, sh, pa, pb);
+            d0 = h2_sub(pa, oz2, BF);
+            d1 = h2_sub(pb, oz2, BF);
+          } else if (!BF) {
             d0 = h2_sub(lop3_and_or(src, 0x000F000Fu, 0x64006400u), oz2, false);
             const uint32_t r1 = lop3_and_or(src, 0x00F000F0u, 0x64006400u);  // 1024 + 16 q
             asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d1) : "r"(r1), "r"(0x2C002C00u), "r"(oz16n));
@@ -388,7 +459,8 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM>::CTAS)
             z = p.has_zp ? scale_to_f32(zc, lb * WN + r, p.st_bytes, T == TQ4_BF16) : p.z_const;
           }
           uint32_t q0, q1;
-          q_pairs4(x, j, BF, q0, q1);
+          if constexpr (BITS == 4) q_pairs4(x, j, BF, q0, q1);
+          else exact_pairs<BITS, BF>(x, sh, q0, q1);
           w0 = deq_pair<BF, T>(q0, z, scv);
           w1 = deq_pair<BF, T>(q1, z, scv);
         }
@@ -609,11 +681,11 @@ tq4_status make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, u
 
 static int gemm_scale_blocks(const Weight& w) { return std::max(1, 128 >> w.bs_log2); }
 
-// Descriptors of a new handle (4-bit weights only): the packed rows (box 128 rows x 64 bytes) and
-// the block-major scales / zero points (box 128 rows x the stage's blocks).
+// Descriptors of a new handle: the packed rows (box 128 rows x one 64-byte group, whatever the bit
+// width) and the block-major scales / zero points (box 128 rows x the stage's blocks).
 tq4_status make_weight_maps(Weight& w) {
   w.wmaps_ok = false;
-  if (w.desc.bits != 4 || encode_fn() == nullptr) return TQ4_OK;
+  if (encode_fn() == nullptr) return TQ4_OK;
   const int st = dtype_size(w.desc.dequant_dtype);
   const CUtensorMapDataType sdt = st == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
   const int nb = gemm_scale_blocks(w);
@@ -642,9 +714,9 @@ struct GemmPlan {
   int stages, stage_bytes, sc_off, zc_off, smem;
 };
 
-template <int TM>
+template <int TM, int BITS>
 static GemmPlan plan_gemm_smem(const Weight& w, int st) {  // st: bytes of a staged scale
-  using L = GemmTile<TM>;
+  using L = GemmTile<TM, BITS>;
   GemmPlan pl{};
   const int sc_bytes = WN * gemm_scale_blocks(w) * st;
   pl.sc_off = L::FIXED;
@@ -662,9 +734,9 @@ static GemmPlan plan_gemm_smem(const Weight& w, int st) {  // st: bytes of a sta
   return pl;
 }
 
-template <int TM, bool BF, tq4_dtype T>
+template <int TM, bool BF, tq4_dtype T, int BITS>
 static tq4_status launch_gemm_t(const CUtensorMap& ma, const Weight& w, GemmArgs args, cudaStream_t st) {
-  const GemmPlan pl = plan_gemm_smem<TM>(w, args.st_bytes);
+  const GemmPlan pl = plan_gemm_smem<TM, BITS>(w, args.st_bytes);
   if (pl.stages < 2) {
     set_error("GEMM: the stage does not fit shared memory");
     return TQ4_ERR_UNSUPPORTED;
@@ -673,7 +745,7 @@ static tq4_status launch_gemm_t(const CUtensorMap& ma, const Weight& w, GemmArgs
   args.stage_bytes = pl.stage_bytes;
   args.sc_off = pl.sc_off;
   args.zc_off = pl.zc_off;
-  auto kern = gemm_kernel<TM, BF, T>;
+  auto kern = gemm_kernel<TM, BF, T, BITS>;
   static std::atomic<uint64_t> attr_set{0};  // per device, at the largest size it can ask for
   TQ4_CUDA(set_smem_limit_once(kern, kSmemLimit, attr_set));
   const dim3 grid(((args.N + WN - 1) / WN) * args.ks, (args.M + TM - 1) / TM);
@@ -701,18 +773,30 @@ static tq4_status launch_gemm_t(const CUtensorMap& ma, const Weight& w, GemmArgs
   return TQ4_OK;
 }
 
-template <int TM, bool BF>
-static tq4_status launch_gemm_tm(const CUtensorMap& ma, const Weight& w, const GemmArgs& args, cudaStream_t st) {
+template <int TM, bool BF, int BITS>
+static tq4_status launch_gemm_b(const CUtensorMap& ma, const Weight& w, const GemmArgs& args, cudaStream_t st) {
   switch (w.desc.dequant_dtype) {
-    case TQ4_F16: return launch_gemm_t<TM, BF, TQ4_F16>(ma, w, args, st);
-    case TQ4_BF16: return launch_gemm_t<TM, BF, TQ4_BF16>(ma, w, args, st);
-    default: return launch_gemm_t<TM, BF, TQ4_F32>(ma, w, args, st);
+    case TQ4_F16: return launch_gemm_t<TM, BF, TQ4_F16, BITS>(ma, w, args, st);
+    case TQ4_BF16: return launch_gemm_t<TM, BF, TQ4_BF16, BITS>(ma, w, args, st);
+    default: return launch_gemm_t<TM, BF, TQ4_F32, BITS>(ma, w, args, st);
   }
 }
 
+template <int TM, bool BF>
+static tq4_status launch_gemm_tm(const CUtensorMap& ma, const Weight& w, const GemmArgs& args, cudaStream_t st) {
+  switch (w.desc.bits) {
+    case 2: return launch_gemm_b<TM, BF, 2>(ma, w, args, st);
+    case 8: return launch_gemm_b<TM, BF, 8>(ma, w, args, st);
+    default: return launch_gemm_b<TM, BF, 4>(ma, w, args, st);
+  }
+}
+
+// 128-k stages per row (the k-tiles of the GEMM), whatever the bit width.
+static int gemm_ktiles(const Weight& w) { return (int)((w.k_pad + 127) / 128); }
+
 // Whether the tcgen05 GEMM takes this call (else A goes through the GEMV in 16-row slices).
 static bool gemm_eligible(const Weight& w, const void* a, tq4_dtype a_t) {
-  if (w.desc.bits != 4) return false;
+  if (w.desc.bits != 2 && w.desc.bits != 4 && w.desc.bits != 8) return false;
   if (a_t != TQ4_F16 && a_t != TQ4_BF16 && a_t != TQ4_F32) return false;
   if ((w.desc.K * 2) % 16 != 0) return false;                    // TMA row stride
   if ((reinterpret_cast<uintptr_t>(a) & 15) != 0) return false;  // TMA base address
@@ -741,7 +825,7 @@ static int choose_tm(const Weight& w, int64_t m, int* ks) {
     if (tm / 2 >= m && tm > 32) continue;
     const int64_t tiles = ((m + tm - 1) / tm) * nt;
     int k = 1;
-    while (k < 8 && tiles * k * 2 <= w.num_sms && w.groups / (k * 2) >= 4) k *= 2;
+    while (k < 8 && tiles * k * 2 <= w.num_sms && gemm_ktiles(w) / (k * 2) >= 4) k *= 2;
     if (k > 1) {
       *ks = k;
       return tm;
@@ -777,7 +861,7 @@ tq4_status run_gemm_tc(const Weight& w, const void* a, int64_t m, tq4_dtype a_t,
   args.M = (int)m;
   args.N = (int)w.desc.N;
   args.K = (int)w.desc.K;
-  args.ktiles = (int)w.groups;
+  args.ktiles = gemm_ktiles(w);
   args.st_bytes = dtype_size(w.desc.dequant_dtype);
   args.int_zp = w.desc.zp_kind != TQ4_ZP_FLOAT;
   args.bias = bias;
@@ -800,8 +884,7 @@ tq4_status run_gemm_tc(const Weight& w, const void* a, int64_t m, tq4_dtype a_t,
   }
 }
 
-// Rows of A in slices of 16 through the fused GEMV kernel (2- and 8-bit weights, f32
-// activations, and A that TMA cannot address).
+// Rows of A in slices of 16 through the fused GEMV kernel (A that TMA cannot address).
 static tq4_status run_gemm_by_slices(const Weight& w, const void* a, int64_t m, tq4_dtype a_t,
                                      const void* bias, tq4_dtype bias_t, void* y, tq4_dtype y_t,
                                      int64_t ldy, cudaStream_t st) {

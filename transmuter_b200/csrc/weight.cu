@@ -250,11 +250,11 @@ tq4_status prepare_weight(Weight& w, const Source& b_src, const Source& s_src, c
       break;
   }
   TQ4_CUDA(cudaGetLastError());
-  if (d.dequant_dtype == TQ4_F32 && d.bits == 4) {
+  if (d.dequant_dtype == TQ4_F32) {  // the tensor-core GEMM's f16 form of f32 weights
     TQ4_TRY(w.wexp.alloc(w.n_pad * 4));
     row_exponent_kernel<<<grid_for(w.n_pad, 256), 256, 0, st>>>(
         static_cast<const float*>(w.scales.ptr), static_cast<const float*>(w.zps.ptr), w.z_const, w.blocks,
-        d.N, w.n_pad, 15.f, static_cast<int32_t*>(w.wexp.ptr));
+        d.N, w.n_pad, (float)((1 << d.bits) - 1), static_cast<int32_t*>(w.wexp.ptr));
     TQ4_CUDA(cudaGetLastError());
     if (d.zp_kind == TQ4_ZP_NONE) {
       const int64_t total = w.n_pad * w.blocks_pad;
@@ -293,11 +293,11 @@ tq4_status merge_weight(Weight& w, const Weight* const* parts, int count) {
                                  p.n_pad * tsz, n * tsz, w.blocks_pad, cudaMemcpyDeviceToDevice, st));
     off += n;
   }
-  if (d.dequant_dtype == TQ4_F32 && d.bits == 4) {
+  if (d.dequant_dtype == TQ4_F32) {  // the tensor-core GEMM's f16 form of f32 weights
     TQ4_TRY(w.wexp.alloc(w.n_pad * 4));
     row_exponent_kernel<<<grid_for(w.n_pad, 256), 256, 0, st>>>(
         static_cast<const float*>(w.scales.ptr), static_cast<const float*>(w.zps.ptr), w.z_const, w.blocks,
-        d.N, w.n_pad, 15.f, static_cast<int32_t*>(w.wexp.ptr));
+        d.N, w.n_pad, (float)((1 << d.bits) - 1), static_cast<int32_t*>(w.wexp.ptr));
     TQ4_CUDA(cudaGetLastError());
     if (d.zp_kind == TQ4_ZP_NONE) {
       const int64_t total = w.n_pad * w.blocks_pad;

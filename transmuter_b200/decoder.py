@@ -6,8 +6,10 @@ and no zero points. The embedding is the GatherBlockQuantized of the tied lm_hea
 (lib/transmuter/emlx.ex:50-53 describes the tied q4 exports). The operators around the projections
 follow lib/transmuter/ops/transformer.ex: RMSNorm (:1056-1069), Qwen3's per-head QK-norm,
 rotate-half RoPE with theta 1e6 (:558-590), GroupQueryAttention with 16 query / 8 KV heads over an
-f32 cache (:106-175), SwiGLU. q/k/v and gate/up are merged along N into one MatMulNBits each (the
-packed form of the sibling merge in lib/transmuter/fusion.ex:430-540).
+f32 cache (:106-175), SwiGLU. q/k/v and gate/up run as one MatMulNBits each, merged along N (the
+packed form of the sibling merge in lib/transmuter/fusion.ex:430-540): weights given as separate
+q, k, v, gate and up inputs, as an ONNX export stores them (``split_siblings``), are merged at load
+by ``tq4_weight_merge``.
 
 A step reads its position and token from device memory; one CUDA graph of a step, replayed,
 runs prompt prefill (forced tokens) and greedy decoding without the host. A layer is five
@@ -76,6 +78,33 @@ def random_weights(cfg, seed=0):
     return w
 
 
+# The sibling projections that read one input, merged along N (the packed form of
+# Fusion.matmuls/2, lib/transmuter/fusion.ex:430-540).
+SIBLINGS = {"qkv": ("q", "k", "v"), "gate_up": ("gate", "up")}
+
+
+def sibling_sizes(cfg):
+    return {"qkv": [cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim],
+            "gate_up": [cfg.inter, cfg.inter]}
+
+
+def split_siblings(weights, cfg):
+    """The weights as a q4 ONNX export stores them: one MatMulNBits input each for q, k, v, gate
+    and up (the row ranges of the merged projections of ``random_weights``)."""
+    sizes = sibling_sizes(cfg)
+    out = {}
+    for name, (b, s) in weights.items():
+        layer, _, proj = name.rpartition(".")
+        if proj not in SIBLINGS:
+            out[name] = (b, s)
+            continue
+        blocks, r0 = b.shape[1], 0
+        for part, n in zip(SIBLINGS[proj], sizes[proj]):
+            out[f"{layer}.{part}"] = (b[r0:r0 + n], s[r0 * blocks:(r0 + n) * blocks])
+            r0 += n
+    return out
+
+
 class Q4Decoder:
     """The decoder on one GPU. Norm weights are 1 (the configuration's choice)."""
 
@@ -90,6 +119,16 @@ class Q4Decoder:
             k = cfg.inter if name.endswith(".down") else (cfg.heads * cfg.head_dim if name.endswith(".o") else cfg.hidden)
             self.weights[name] = PackedWeight((k, n, 4, cfg.block_size), torch.from_numpy(b).to(dev),
                                               torch.from_numpy(s).to(dev), None, dtype=torch.float32, device=dev)
+        # Separate sibling inputs (an ONNX export's q, k, v and gate, up) merge into one handle
+        # each, so one GEMV streams the whole group's rows.
+        for layer in range(cfg.layers):
+            for merged, parts in SIBLINGS.items():
+                names = [f"{layer}.{p}" for p in parts]
+                if all(n in self.weights for n in names):
+                    ws = [self.weights.pop(n) for n in names]
+                    self.weights[f"{layer}.{merged}"] = PackedWeight.merge(ws)
+                    for w in ws:
+                        w.close()
         f32 = dict(dtype=torch.float32, device=dev)
         self.ones_h = torch.ones(cfg.hidden, **f32)
         self.ones_d = torch.ones(cfg.head_dim, **f32)
