@@ -42,7 +42,10 @@ tq4_status tq4_attention_decode(const float* q, const float* k_new, const float*
 /* tq4_attention_decode with Qwen3's per-head RMSNorm (weights q_w / k_w over head_dim, eps) and
  * rotate-half RoPE at *pos (cos/sin tables [max_len][head_dim/2]) applied to q and k_new first,
  * as tq4_qk_norm_rope would: the normalised, rotated key is the one written into the cache.
- * q and k_new are read, not modified. */
+ * q and k_new are read, not modified. This is the decode step's form: the cache rows before *pos
+ * are read while the previous kernel on the stream may still run (programmatic dependent
+ * launch), so they must be complete before that kernel started, as in a decode loop where
+ * earlier steps wrote them (the row at *pos comes from k_new / v_new). */
 tq4_status tq4_attention_decode_rope(const float* q, const float* k_new, const float* v_new,
                                      const float* q_w, const float* k_w, const float* cos_table,
                                      const float* sin_table, float eps, float* k_cache,

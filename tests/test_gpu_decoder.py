@@ -291,6 +291,7 @@ def test_attention_decode_rope_matches_separate_steps(pos):
     fr.argtypes = [ctypes.c_void_p] * 7 + [ctypes.c_float] + [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
     out1, kc1, vc1 = torch.empty(heads, hd, device=dev), kc.clone(), vc.clone()
     q0, k0 = q.clone(), k.clone()
+    torch.cuda.synchronize()  # the caches are complete before the call (its earlier rows load early)
     _lib.check(fr(vp(q), vp(k), vp(v), vp(qw), vp(kw), vp(cos), vp(sin), 1e-6, vp(kc1), vp(vc1), vp(p), vp(out1),
                   heads, kv_heads, hd, max_len, st))
     torch.cuda.synchronize()

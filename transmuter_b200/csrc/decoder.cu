@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
     float* __restrict__ k_cache, float* __restrict__ v_cache, const int32_t* __restrict__ pos,
     float* __restrict__ out, int heads, int kv_heads, int head_dim, int max_len, float scale,
     const float* __restrict__ q_w, const float* __restrict__ k_w, const float* __restrict__ cos_t,
-    const float* __restrict__ sin_t, float eps) {
+    const float* __restrict__ sin_t, float eps, int early) {
   __shared__ __align__(16) float qs[kAttnMaxGroup * kAttnMaxDim];
   __shared__ __align__(16) float kn_s[kAttnMaxDim];
   __shared__ __align__(16) float vn_s[kAttnMaxDim];
@@ -169,10 +169,13 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
   float* kc = k_cache + (int64_t)kvh * max_len * D;
   float* vc = v_cache + (int64_t)kvh * max_len * D;
 
-  pdl_wait();
-  pdl_trigger();
-  // Trip 1: the first chunk's rows (bulk copies), the position, q, the new row, the norm weights.
+  // Trip 1: the first chunk's cache rows (bulk copies). With `early` they are issued before the
+  // wait for the previous kernel: the caller guarantees that the rows before this step's position
+  // were complete before that kernel started (in a decode step, earlier steps wrote them and every
+  // kernel waits for the one before it), and the row of this step's position is taken from
+  // k_new / v_new below.
   const int rows0 = min(kAttnChunk, max_len - r * kAttnChunk);  // >= 1: C <= ceil(max_len / 32)
+  if (!early) pdl_wait();
   if (tid == 0) {
     s_abort = 0;
     mbar_init(bar_a, 1);
@@ -183,6 +186,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
     bulk_load(smem_u32(ks), kc + (int64_t)r * kAttnChunk * D, bytes, bar_a);
     bulk_load(smem_u32(vs), vc + (int64_t)r * kAttnChunk * D, bytes, bar_a);
   }
+  if (early) pdl_wait();
+  pdl_trigger();
+  // Then the position, q, the new row and the norm weights.
   const int L = *pos + 1;
   const float4* q4 = reinterpret_cast<const float4*>(q + (int64_t)kvh * G * D);
   float4 qr[kAttnMaxGroup * kAttnMaxDim / 4 / kAttnThreads];
@@ -494,6 +500,7 @@ struct RopeArgs {
   const float* cos_t = nullptr;
   const float* sin_t = nullptr;
   float eps = 0.f;
+  int early = 0;  // the first cache chunk is loaded before the wait for the previous kernel
 };
 tq4_status attention_impl(const float* q, const float* k_new, const float* v_new, float* k_cache, float* v_cache,
                           const int32_t* pos, float* out, int heads, int kv_heads, int head_dim, int max_len,
@@ -522,6 +529,7 @@ tq4_status tq4_attention_decode_rope(const float* q, const float* k_new, const f
   r.k_w = k_w;
   r.cos_t = cos_table;
   r.sin_t = sin_table;
+  r.early = 1;
   r.eps = eps;
   return attention_impl(q, k_new, v_new, k_cache, v_cache, pos, out, heads, kv_heads, head_dim, max_len, stream, r);
 }
@@ -573,7 +581,7 @@ tq4_status attention_impl(const float* q, const float* k_new, const float* v_new
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   TQ4_CUDA(cudaLaunchKernelEx(&cfg, attention_decode_kernel, q, k_new, v_new, k_cache, v_cache, pos, out, heads,
                               kv_heads, head_dim, max_len, 1.f / sqrtf((float)head_dim), rope.q_w, rope.k_w,
-                              rope.cos_t, rope.sin_t, rope.eps));
+                              rope.cos_t, rope.sin_t, rope.eps, rope.early));
   return TQ4_OK;
 }
 }  // namespace

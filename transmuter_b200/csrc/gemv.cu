@@ -1228,15 +1228,21 @@ static tq4_status gemv_launch(const Weight& w, const void* a, int64_t m, tq4_dty
     set_error("GEMV: the handle has no TMA descriptors");
     return TQ4_ERR_CUDA;
   }
-  if (m == 1 && !(pro && pro->mode) && rows_eligible(w)) {
-    // one activation row, at most 8 packed groups: the 32-row-unit kernel (gemv_rows.cu)
+  if (m == 1 && (!pro || pro->mode <= 1) && rows_eligible(w)) {
+    // one activation row, at most 8 packed groups: the 32-row-unit kernel (gemv_rows.cu), with
+    // the RMSNorm prologue of the decoder's fused projections when asked
     if (counters == nullptr || ctr_capacity < 1) {
       set_error("GEMV: the unit hand-out needs one counter");
       return TQ4_ERR_INVALID_ARGUMENT;
     }
     RowsDst dst;
     dst.y[0] = y;
-    return run_gemv_rows(w, a, a_t, bias, bias_t, y_t, dst, counters, st);
+    RowsNorm norm;
+    if (pro && pro->mode == 1) {
+      norm.w = pro->w;
+      norm.eps = pro->eps;
+    }
+    return run_gemv_rows(w, a, a_t, bias, bias_t, y_t, dst, counters, st, pro && pro->mode == 1 ? &norm : nullptr);
   }
   const GemvPlan pl = plan_gemv(w, m);
   GemvArgs args{};
@@ -1337,8 +1343,9 @@ tq4_status run_gemv_fused(const Weight& w, const float* x, const float* x2, cons
                           int mode, const float* residual, float* y, cudaStream_t st) {
   float* ws = nullptr;
   int* ctr = nullptr;
-  // a staging transform runs in the 128-row kernel; without one the call is a plain M = 1 call
-  const bool plain = mode == 0 && rows_eligible(w);
+  // the 32-row-unit kernel takes plain calls and the RMSNorm prologue; SwiGLU runs in the 128-row
+  // kernel
+  const bool plain = mode <= 1 && rows_eligible(w);
   const int64_t need = plain ? 0 : plan_gemv(w, 1).ws_floats;
   const int64_t nctr = plain ? 1 : tile_counter_count(w, 1);
   if (need > 0 || nctr > 0) TQ4_TRY(gemv_workspace(w, st, need * 4, nctr, &ws, &ctr));

@@ -97,6 +97,8 @@ struct RowsArgs {
   int stage_bytes, sc_off, zc_off;
   int part_off, tail_off;
   int* counter;  // the unit tickets (zero between calls)
+  const float* norm_w;  // RMSNorm weights of an f32 activation row (RowsNorm), or null
+  float norm_eps;
 };
 
 template <tq4_dtype AT, int SPS>
@@ -274,6 +276,21 @@ __global__ void __launch_bounds__(kRowsThreads, kRowsCtas)
     float a4[4] = {0.f, 0.f, 0.f, 0.f};
     const int64_t k = (int64_t)warp * 128 + 4 * lane;
     if (active) load_act4<AT>(p.a, 0, k, p.K, (p.K & 3) == 0, a4);
+    if (AT == TQ4_F32 && p.norm_w) {
+      // RMSNorm prologue: the 8 consumer warps hold the whole row (groups * 128 >= K, zeros past
+      // K); its mean square is summed in a fixed order, then a = (x * rs) * w.
+      __shared__ float red[kRowsWarps];
+      float ss = fmaf(a4[3], a4[3], fmaf(a4[2], a4[2], fmaf(a4[1], a4[1], a4[0] * a4[0])));
+      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (lane == 0) red[warp] = ss;
+      asm volatile("bar.sync 1, %0;" ::"n"(kRowsWarps * 32) : "memory");
+      float tot = 0.f;
+#pragma unroll
+      for (int i = 0; i < kRowsWarps; ++i) tot += red[i];
+      const float rs = 1.f / sqrtf(tot / (float)p.K + p.norm_eps);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) a4[e] = (k + e < p.K) ? a4[e] * rs * p.norm_w[k + e] : 0.f;
+    }
     float mx = fmaxf(fmaxf(fabsf(a4[0]), fabsf(a4[1])), fmaxf(fabsf(a4[2]), fabsf(a4[3])));
 #pragma unroll
     for (int off = 1; off < LPS; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -479,7 +496,7 @@ static cudaError_t launch_rows_at(const Weight& w, const RowsArgs& args, int gri
 }
 
 tq4_status run_gemv_rows(const Weight& w, const void* a, tq4_dtype a_t, const void* bias, tq4_dtype bias_t,
-                         tq4_dtype y_t, const RowsDst& dst, int* counter, cudaStream_t st) {
+                         tq4_dtype y_t, const RowsDst& dst, int* counter, cudaStream_t st, const RowsNorm* norm) {
   if (!rows_eligible(w)) {
     set_error("GEMV: the handle has no 32-row unit descriptors");
     return TQ4_ERR_UNSUPPORTED;
@@ -487,6 +504,10 @@ tq4_status run_gemv_rows(const Weight& w, const void* a, tq4_dtype a_t, const vo
   if (dst.ndst < 1 || dst.ndst > kRowsMaxDst || counter == nullptr) {
     set_error("GEMV: bad destinations or no counter");
     return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  if (norm && a_t != TQ4_F32) {
+    set_error("GEMV: the RMSNorm prologue takes f32 activations");
+    return TQ4_ERR_UNSUPPORTED;
   }
   const RowsPlan pl = plan_rows(w);
   if (pl.stages < 2) {
@@ -503,6 +524,10 @@ tq4_status run_gemv_rows(const Weight& w, const void* a, tq4_dtype a_t, const vo
   args.col0 = dst.col0;
   args.epoch = dst.epoch;
   args.half_elems = dst.half_elems;
+  if (norm) {
+    args.norm_w = norm->w;
+    args.norm_eps = norm->eps;
+  }
   args.z_const = w.z_const;
   args.has_zp = w.zps.ptr != nullptr;
   args.st_bytes = dtype_size(w.desc.dequant_dtype);

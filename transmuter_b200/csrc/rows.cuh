@@ -19,6 +19,13 @@ struct RowsDst {
   int64_t half_elems = 0;
 };
 
+// An RMSNorm of the f32 activation row before the product (the decoder's fused projections,
+// rms_norm/4 of transformer.ex:1056-1069): a = x * rsqrt(mean(x^2) + eps) * w.
+struct RowsNorm {
+  const float* w = nullptr;
+  float eps = 0.f;
+};
+
 // 4-bit weights of at most 8 packed groups per row whose unit descriptors were made.
 bool rows_eligible(const Weight& w);
 // The unit descriptors of a new handle (a no-op for handles the kernel does not take).
@@ -26,6 +33,7 @@ tq4_status make_rows_maps(Weight& w);
 // Y = A . W^T (+ bias) for one activation row; `counter` is one int of device memory that is zero
 // before the call and left at zero by it (per stream: calls that overlap must not share it).
 tq4_status run_gemv_rows(const Weight& w, const void* a, tq4_dtype a_t, const void* bias, tq4_dtype bias_t,
-                         tq4_dtype y_t, const RowsDst& dst, int* counter, cudaStream_t st);
+                         tq4_dtype y_t, const RowsDst& dst, int* counter, cudaStream_t st,
+                         const RowsNorm* norm = nullptr);
 
 }  // namespace tq4
