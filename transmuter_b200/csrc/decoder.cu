@@ -139,6 +139,7 @@ constexpr int kAttnMaxGroup = 8;
 constexpr int kAttnMaxDim = 256;
 constexpr int kAttnMaxCluster = 8;
 
+template <int G>  // query heads per KV head
 __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
     const float* __restrict__ q, const float* __restrict__ k_new, const float* __restrict__ v_new,
     float* __restrict__ k_cache, float* __restrict__ v_cache, const int32_t* __restrict__ pos,
@@ -150,8 +151,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
   __shared__ __align__(16) float vn_s[kAttnMaxDim];
   __shared__ __align__(16) float qw_s[kAttnMaxDim];
   __shared__ __align__(16) float kw_s[kAttnMaxDim];
-  __shared__ float cs_s[kAttnMaxDim / 2], sn_s[kAttnMaxDim / 2];
+  __shared__ __align__(16) float cs_s[kAttnMaxDim / 2];
+  __shared__ __align__(16) float sn_s[kAttnMaxDim / 2];
   __shared__ float sc[kAttnMaxGroup][kAttnChunk];
+  __shared__ float spart[kAttnMaxGroup][kAttnChunk];  // partial scores of the D slices
   __shared__ float ml[kAttnMaxGroup][2];  // running max, running sum
   __shared__ float alpha_s[kAttnMaxGroup];
   __shared__ float part[kAttnMaxGroup * (kAttnMaxDim + 2)];  // o[g][0..D), m, l: read by the cluster
@@ -159,7 +162,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
   __shared__ int s_abort;
   extern __shared__ float4 kv_chunk[];  // K rows [kAttnChunk][D], then V rows
 
-  const int G = heads / kv_heads, D = head_dim, D4 = head_dim / 4;
+  const int D = head_dim, D4 = head_dim / 4;
   const int C = (int)gridDim.x;  // the cluster spans x
   const int r = (int)cluster_ctarank(), kvh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -241,9 +244,37 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
     return;
   }
 
-  if (q_w) {
+  if (q_w && D == 128) {
     // Qwen3's per-head RMSNorm then rotate-half RoPE at position L - 1 (rms_norm/4,
-    // transformer.ex:1056-1069; rotate/4, :558-590), on the G query heads and the new key.
+    // transformer.ex:1056-1069; rotate/4, :558-590), on the G query heads and the new key; a warp
+    // per row, lane l holding d = 4l .. 4l + 3 (its rotation partner d -/+ 64 is lane l ^ 16).
+    for (int row = warp; row <= G; row += kAttnThreads / 32) {
+      float* v = row < G ? qs + row * D : kn_s;
+      const float* w = row < G ? qw_s : kw_s;
+      float4 x = reinterpret_cast<const float4*>(v)[lane];
+      float ss = fmaf(x.w, x.w, fmaf(x.z, x.z, fmaf(x.y, x.y, x.x * x.x)));
+      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      const float inv = 1.f / sqrtf(ss / (float)D + eps);
+      const float4 wv = reinterpret_cast<const float4*>(w)[lane];
+      x = make_float4(x.x * inv * wv.x, x.y * inv * wv.y, x.z * inv * wv.z, x.w * inv * wv.w);
+      float4 pr;
+      pr.x = __shfl_xor_sync(0xffffffffu, x.x, 16);
+      pr.y = __shfl_xor_sync(0xffffffffu, x.y, 16);
+      pr.z = __shfl_xor_sync(0xffffffffu, x.z, 16);
+      pr.w = __shfl_xor_sync(0xffffffffu, x.w, 16);
+      const float4 c = reinterpret_cast<const float4*>(cs_s)[lane & 15];
+      const float4 sn = reinterpret_cast<const float4*>(sn_s)[lane & 15];
+      if (lane < 16)  // x = x1 (d < 64), pr = x2: x1 c - x2 s
+        x = make_float4(x.x * c.x - pr.x * sn.x, x.y * c.y - pr.y * sn.y, x.z * c.z - pr.z * sn.z,
+                        x.w * c.w - pr.w * sn.w);
+      else  // x = x2, pr = x1: x2 c + x1 s
+        x = make_float4(x.x * c.x + pr.x * sn.x, x.y * c.y + pr.y * sn.y, x.z * c.z + pr.z * sn.z,
+                        x.w * c.w + pr.w * sn.w);
+      reinterpret_cast<float4*>(v)[lane] = x;
+    }
+    __syncthreads();
+  } else if (q_w) {
+    // the same for other head sizes: a warp per row, lanes striding over d
     for (int row = warp; row <= G; row += kAttnThreads / 32) {
       float* v = row < G ? qs + row * D : kn_s;
       const float* w = row < G ? qw_s : kw_s;
@@ -293,24 +324,40 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
         vs[(np - 1) * D + d] = vn_s[d];
       }
     __syncthreads();
-    // scores: warp w takes positions w, w + 4, ...; lanes split head_dim
-    for (int i = warp; i < np; i += kAttnThreads / 32) {
-      const float* kp = ks + i * D;
-      float dot[kAttnMaxGroup];
-#pragma unroll
-      for (int g = 0; g < kAttnMaxGroup; ++g) dot[g] = 0.f;
-      for (int d = lane; d < D; d += 32) {
-        const float kv = kp[d];
-#pragma unroll
-        for (int g = 0; g < kAttnMaxGroup; ++g)
-          if (g < G) dot[g] = fmaf(qs[g * D + d], kv, dot[g]);
+    // scores: lane = position (rows past np are computed on whatever the buffer holds and never
+    // used); a warp takes one (head, slice of D) pair: G < 4 splits D into 4 / G slices so all
+    // four warps work. K rows and q are read as float4 in a lane-rotated chunk order, so the 8
+    // lanes of a quarter warp read 8 different 16-byte bank groups; no shuffles.
+    {
+      constexpr int NS = G >= 4 ? 1 : 4 / G;
+      for (int task = warp; task < G * NS; task += kAttnThreads / 32) {
+        const int g = task % G, sl = task / G;
+        const int c0 = sl * D4 / NS, len = (sl + 1) * D4 / NS - c0;
+        if (len == 0) {  // head_dim below 16: fewer chunks than slices
+          spart[task][lane] = 0.f;
+          continue;
+        }
+        const float4* kp = reinterpret_cast<const float4*>(ks + lane * D);
+        const float4* qp = reinterpret_cast<const float4*>(qs + g * D);
+        float a0 = 0.f, a1 = 0.f;
+        int c = c0 + lane % len;
+        for (int j = 0; j < len; ++j) {
+          const float4 kv = kp[c], qv = qp[c];
+          a0 = fmaf(qv.x, kv.x, a0);
+          a1 = fmaf(qv.y, kv.y, a1);
+          a0 = fmaf(qv.z, kv.z, a0);
+          a1 = fmaf(qv.w, kv.w, a1);
+          if (++c == c0 + len) c = c0;
+        }
+        spart[task][lane] = a0 + a1;
       }
+      __syncthreads();
+      for (int i = tid; i < G * kAttnChunk; i += kAttnThreads) {
+        const int g = i / kAttnChunk, pp = i % kAttnChunk;
+        float v = spart[g][pp];
 #pragma unroll
-      for (int g = 0; g < kAttnMaxGroup; ++g) {
-        if (g >= G) break;
-        float v = dot[g];
-        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0) sc[g][i] = v * scale;
+        for (int sl = 1; sl < NS; ++sl) v += spart[sl * G + g][pp];
+        sc[g][pp] = v * scale;
       }
     }
     __syncthreads();
@@ -342,6 +389,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
         float acc[kAttnMaxGroup];
 #pragma unroll
         for (int g = 0; g < kAttnMaxGroup; ++g) acc[g] = 0.f;
+#pragma unroll 4
         for (int i = 0; i < np; ++i) {
           const float vv = vs[i * D + d];
 #pragma unroll
@@ -546,6 +594,21 @@ tq4_status tq4_matmul_fused(const tq4_weight* w, const float* x, const float* x2
 }
 
 namespace {
+extern "C++" {  // a template inside the C-linkage block
+template <int G>
+static cudaError_t launch_attention(cudaLaunchConfig_t& cfg, const float* q, const float* k_new, const float* v_new,
+                                    float* k_cache, float* v_cache, const int32_t* pos, float* out, int heads,
+                                    int kv_heads, int head_dim, int max_len, float scale, const RopeArgs& rope) {
+  static std::atomic<uint64_t> attr_set{0};  // per device, per instantiation
+  const cudaError_t e =
+      set_smem_limit_once(attention_decode_kernel<G>, 2 * kAttnChunk * kAttnMaxDim * (int)sizeof(float), attr_set);
+  if (e != cudaSuccess) return e;
+  return cudaLaunchKernelEx(&cfg, attention_decode_kernel<G>, q, k_new, v_new, k_cache, v_cache, pos, out, heads,
+                            kv_heads, head_dim, max_len, scale, rope.q_w, rope.k_w, rope.cos_t, rope.sin_t, rope.eps,
+                            rope.early);
+}
+}  // extern "C++"
+
 tq4_status attention_impl(const float* q, const float* k_new, const float* v_new, float* k_cache, float* v_cache,
                           const int32_t* pos, float* out, int heads, int kv_heads, int head_dim, int max_len,
                           void* stream, const RopeArgs& rope) {
@@ -563,8 +626,6 @@ tq4_status attention_impl(const float* q, const float* k_new, const float* v_new
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int chunks = (max_len + kAttnChunk - 1) / kAttnChunk;
   const int C = std::min(kAttnMaxCluster, chunks);
-  static std::atomic<uint64_t> attr_set{0};  // per device
-  TQ4_CUDA(set_smem_limit_once(attention_decode_kernel, 2 * kAttnChunk * kAttnMaxDim * (int)sizeof(float), attr_set));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(C, kv_heads);
   cfg.blockDim = dim3(kAttnThreads);
@@ -579,9 +640,22 @@ tq4_status attention_impl(const float* q, const float* k_new, const float* v_new
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  TQ4_CUDA(cudaLaunchKernelEx(&cfg, attention_decode_kernel, q, k_new, v_new, k_cache, v_cache, pos, out, heads,
-                              kv_heads, head_dim, max_len, 1.f / sqrtf((float)head_dim), rope.q_w, rope.k_w,
-                              rope.cos_t, rope.sin_t, rope.eps, rope.early));
+  const float scale = 1.f / sqrtf((float)head_dim);
+  cudaError_t e;
+  switch (heads / kv_heads) {
+#define TQ4_ATTN_G(GG)                                                                                      \
+  case GG:                                                                                                  \
+    e = launch_attention<GG>(cfg, q, k_new, v_new, k_cache, v_cache, pos, out, heads, kv_heads, head_dim,  \
+                             max_len, scale, rope);                                                         \
+    break;
+    TQ4_ATTN_G(1) TQ4_ATTN_G(2) TQ4_ATTN_G(3) TQ4_ATTN_G(4) TQ4_ATTN_G(5) TQ4_ATTN_G(6) TQ4_ATTN_G(7)
+    TQ4_ATTN_G(8)
+#undef TQ4_ATTN_G
+    default:
+      set_error("tq4_attention_decode: more than %d query heads per KV head", kAttnMaxGroup);
+      return TQ4_ERR_INVALID_ARGUMENT;
+  }
+  TQ4_CUDA(e);
   return TQ4_OK;
 }
 }  // namespace
