@@ -75,3 +75,17 @@ def test_two_ranks_sharded_equals_unsharded():
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     assert '"ok": true' in r.stdout
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 3, reason="needs more than two GPUs")
+def test_all_ranks_sharded_equals_unsharded():
+    """The same cases on every GPU of the box (up to 8 ranks): ragged shares, a last rank with few
+    or no rows, both assembly paths and the M = 1 push path with 2 < P <= 8 destinations."""
+    n = min(torch.cuda.device_count(), 8)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={n}", "--master-addr=127.0.0.1", "--master-port=29518",
+           os.path.join(ROOT, "tests", "sharded_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=500)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    assert f'"world": {n}, "ok": true' in r.stdout
