@@ -220,14 +220,14 @@ def rotation_copies(per_copy_bytes):
 # ---- our path --------------------------------------------------------------------------------
 def launches_per_call(cfg, m, sharded_world=1):
     """libtq4 kernels per call (NCCL's own kernels are not counted)."""
-    if m <= 8 or (m <= 16 and cfg.bits != 4):
+    groups = -(-(cfg.blocks * cfg.block_size * cfg.bits // 8) // 64)   # packed groups of 64 bytes per row
+    if m == 1 and cfg.bits == 4 and groups > 8 and cfg.block_size <= 1024:
+        n = 2                                   # the K-sliced 32-row-unit GEMV + the sum of its slices
+    elif m <= 8:
         n = 1                                   # the GEMV
-    elif cfg.bits == 4:
-        n = 2 if cfg.a_type == "f32" else 1     # (row-scaled f16 copy of A) + the tcgen05 GEMM
     else:
-        n = -(-m // 16)                         # GEMV slices of 16 rows
+        n = 2 if cfg.a_type == "f32" else 1     # (row-scaled f16 copy of A) + the tcgen05 GEMM
     if sharded_world > 1:
-        groups = -(-(cfg.blocks * cfg.block_size * cfg.bits // 8) // 64)
         if m == 1 and cfg.bits == 4 and groups <= 8 and sharded_world <= 8:
             return n + 1                        # the assembly kernel of the push path
         share = (-(-cfg.n // sharded_world) + 15) // 16 * 16

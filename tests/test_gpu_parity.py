@@ -439,6 +439,16 @@ UNITS_M1 = [
     (768, 600, 32, "none", "f16", "f32", "f16", False),
     (1024, 70001, 32, "none", "f32", "bf16", "f32", False),
     (640, 33, 64, "float", "f16", "f16", "f16", True),
+    # rows of more than 8 packed groups run K-sliced (each CTA on one slice of 8 groups for the
+    # call, the slices' partial rows added in slice order by the last one to finish a unit): 2 to
+    # 14 slices, a last slice of one group, blocks up to 1024 spanning several groups
+    (1100, 640, 16, "packed", "f16", "f16", "f16", True),
+    (2048, 1000, 32, "none", "f32", "f32", "f32", True),
+    (3000, 777, 64, "float", "bf16", "bf16", "bf16", False),
+    (4096, 3000, 128, "packed", "f16", "f16", "f16", False),
+    (4096, 520, 256, "none", "f32", "f32", "f32", True),
+    (5120, 300, 1024, "packed", "f32", "bf16", "f32", False),
+    (14336, 600, 128, "packed", "f16", "f16", "f16", True),
 ]
 
 

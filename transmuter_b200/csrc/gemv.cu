@@ -1228,11 +1228,14 @@ static tq4_status gemv_launch(const Weight& w, const void* a, int64_t m, tq4_dty
     set_error("GEMV: the handle has no TMA descriptors");
     return TQ4_ERR_CUDA;
   }
-  if (m == 1 && (!pro || pro->mode <= 1) && rows_eligible(w)) {
-    // one activation row, at most 8 packed groups: the 32-row-unit kernel (gemv_rows.cu), with
-    // the RMSNorm prologue of the decoder's fused projections when asked
-    if (counters == nullptr || ctr_capacity < 1) {
-      set_error("GEMV: the unit hand-out needs one counter");
+  if (m == 1 && rows_eligible(w) && (!pro || (pro->mode <= 1 && rows_slices(w) == 1))) {
+    // one activation row: the 32-row-unit kernel (gemv_rows.cu), K-sliced for rows of more than
+    // 8 packed groups, with the RMSNorm prologue of the decoder's fused projections when asked (the
+    // decoder's other projections keep the 128-row kernel: measured faster within its step)
+    if (counters == nullptr || ctr_capacity < rows_counters(w) ||
+        (rows_ws_floats(w) > 0 && (ws == nullptr || ws_capacity_floats < rows_ws_floats(w)))) {
+      set_error("GEMV: the unit hand-out needs %lld counters and %lld workspace floats",
+                (long long)rows_counters(w), (long long)rows_ws_floats(w));
       return TQ4_ERR_INVALID_ARGUMENT;
     }
     RowsDst dst;
@@ -1242,7 +1245,7 @@ static tq4_status gemv_launch(const Weight& w, const void* a, int64_t m, tq4_dty
       norm.w = pro->w;
       norm.eps = pro->eps;
     }
-    return run_gemv_rows(w, a, a_t, bias, bias_t, y_t, dst, counters, st, pro && pro->mode == 1 ? &norm : nullptr);
+    return run_gemv_rows(w, a, a_t, bias, bias_t, y_t, dst, counters, st, pro && pro->mode == 1 ? &norm : nullptr, ws);
   }
   const GemvPlan pl = plan_gemv(w, m);
   GemvArgs args{};
@@ -1327,7 +1330,7 @@ static tq4_status gemv_launch(const Weight& w, const void* a, int64_t m, tq4_dty
 
 // Workspace of a plain call (tq4_matmul, tq4_matmul_noalloc): partial-sum floats and counters.
 int64_t gemv_workspace_floats(const Weight& w, int64_t m) {
-  if (m == 1 && rows_eligible(w)) return 0;
+  if (m == 1 && rows_eligible(w)) return rows_ws_floats(w);
   return plan_gemv(w, m).ws_floats;
 }
 
@@ -1343,9 +1346,9 @@ tq4_status run_gemv_fused(const Weight& w, const float* x, const float* x2, cons
                           int mode, const float* residual, float* y, cudaStream_t st) {
   float* ws = nullptr;
   int* ctr = nullptr;
-  // the 32-row-unit kernel takes plain calls and the RMSNorm prologue; SwiGLU runs in the 128-row
-  // kernel
-  const bool plain = mode <= 1 && rows_eligible(w);
+  // the 32-row-unit kernel takes plain calls and the RMSNorm prologue on rows of at most 8 groups;
+  // SwiGLU and longer rows run in the 128-row kernel
+  const bool plain = mode <= 1 && rows_eligible(w) && rows_slices(w) == 1;
   const int64_t need = plain ? 0 : plan_gemv(w, 1).ws_floats;
   const int64_t nctr = plain ? 1 : tile_counter_count(w, 1);
   if (need > 0 || nctr > 0) TQ4_TRY(gemv_workspace(w, st, need * 4, nctr, &ws, &ctr));
@@ -1356,7 +1359,7 @@ tq4_status run_gemv_fused(const Weight& w, const float* x, const float* x2, cons
 // Counters a plain call uses (zero-initialised, left at zero by the kernel): the unit hand-out of
 // the 32-row-unit kernel, or those of the 128-row kernels.
 int64_t gemv_counter_count(const Weight& w, int64_t m) {
-  if (m == 1 && rows_eligible(w)) return 1;
+  if (m == 1 && rows_eligible(w)) return rows_counters(w);
   return tile_counter_count(w, m);
 }
 

@@ -1,5 +1,5 @@
-// M = 1 MatMulNBits over 32-row units, for 4-bit weights of at most 8 packed groups per row
-// (K <= 1024): the 151936-column lm_head (C3) and the K = 1024 decode projections.
+// M = 1 MatMulNBits over 32-row units, for 4-bit weights: the 151936-column lm_head (C3), the
+// K = 1024 decode projections, and (K-sliced) the longer rows of the Llama-shaped decode calls.
 //
 // Math: the MatMulNBits clause (quantized.ex:30-46) over dequantize_weight/4 (:234-240),
 //   Y[n] = sum_k A[k] * (q[n][k] - z[n][b(k)]) * s[n][b(k)],
@@ -36,6 +36,12 @@
 //   - Destinations: Y itself, or (N-sharded calls, sharded.cu) every rank's assembly buffer over
 //     NVLink: the 32 outputs of a unit go to each destination with plain stores, into the half
 //     that this call's epoch selects.
+//   - Rows of more than 8 packed groups (K > 1024) run K-sliced: CTA b takes slice b % S of 8
+//     groups for the whole call (so its warps' B fragments stay fixed), the slice's CTAs take its
+//     units by their own ticket counter, and the reducer stores the slice's partial rows in a
+//     workspace; rows_slice_sum_kernel then adds the slices in slice order (deterministic) and
+//     applies the bias. (The cross-slice sum inside the reducer, with a fence and an arrival
+//     counter per unit, held the consumers back and was slower than the 128-row kernel.)
 // Every mbarrier wait is bounded; a wait that runs out writes the device status word and the CTA
 // winds down.
 #include "fragments.cuh"
@@ -96,9 +102,11 @@ struct RowsArgs {
   int stages;
   int stage_bytes, sc_off, zc_off;
   int part_off, tail_off;
-  int* counter;  // the unit tickets (zero between calls)
+  int* counter;  // the units' tickets, one per K slice (zero between calls)
   const float* norm_w;  // RMSNorm weights of an f32 activation row (RowsNorm), or null
   float norm_eps;
+  int slices;           // K slices of 8 packed groups (CTA b takes slice b % slices)
+  float* ws;            // K-sliced: [slices][units * kRU] partial rows
 };
 
 template <tq4_dtype AT, int SPS>
@@ -126,6 +134,11 @@ __global__ void __launch_bounds__(kRowsThreads, kRowsCtas)
   volatile int* tag = reinterpret_cast<volatile int*>(tail + 24 * kRowsMaxStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 28 * kRowsMaxStages);
   float* part = reinterpret_cast<float*>(smem + p.part_off);  // [lap parity][stage][warp][kRU rows]
+  // This CTA's K slice: packed groups [g0, g0 + sgroups), scale blocks from b0; the slice's CTAs
+  // are numbered bi = 0 .. Gs - 1 (the grid is a multiple of the slice count).
+  const int NS = p.slices, sl = blockIdx.x % NS, Gs = gridDim.x / NS, bi = blockIdx.x / NS;
+  const int g0 = sl * kRowsWarps, sgroups = min(kRowsWarps, p.groups - g0);
+  const int b0 = (g0 * 128) >> p.bs_log2;
 
   pdl_trigger();
   if (threadIdx.x == 0) {
@@ -143,8 +156,9 @@ __global__ void __launch_bounds__(kRowsThreads, kRowsCtas)
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       const uint32_t sc_bytes = (uint32_t)kSR * p.nbs * p.st_bytes;
-      const uint32_t tx = (uint32_t)p.groups * kRU * 64 + sc_bytes * (p.has_zp ? 2u : 1u);
-      const int G = gridDim.x;
+      const uint32_t tx = (uint32_t)sgroups * kRU * 64 + sc_bytes * (p.has_zp ? 2u : 1u);
+      const int G = Gs;  // the CTAs of this slice
+      int* const counter = p.counter + sl;
       const int statics = S * G;
       // A unit's packed weights are read once per call: they leave L2 first, so the activations,
       // the outputs and the next kernel's inputs stay there (C3: 22.4 -> 21.4 us; the same hint on
@@ -171,15 +185,15 @@ __global__ void __launch_bounds__(kRowsThreads, kRowsCtas)
         tag[s] = u;
         const uint32_t st = sbase + s * p.stage_bytes;
         mbar_expect_tx(full(s), tx);
-        for (int gi = 0; gi < p.groups; ++gi)
-          tma_load_2d_hint(st + gi * (kRU * 64), &map_w, gi * 64, u * kRU, full(s), pol_w);
-        tma_load_2d(st + p.sc_off, &map_s, u * kRU, 0, full(s));
-        if (p.has_zp) tma_load_2d(st + p.zc_off, &map_z, u * kRU, 0, full(s));
+        for (int gi = 0; gi < sgroups; ++gi)
+          tma_load_2d_hint(st + gi * (kRU * 64), &map_w, (g0 + gi) * 64, u * kRU, full(s), pol_w);
+        tma_load_2d(st + p.sc_off, &map_s, u * kRU, b0, full(s));
+        if (p.has_zp) tma_load_2d(st + p.zc_off, &map_z, u * kRU, b0, full(s));
       };
       bool ok = true;
       // the static units: issued before the previous kernel on the stream has finished
       for (int i = 0; i < S && ok; ++i) {
-        const int u = blockIdx.x + i * G;
+        const int u = bi + i * G;
         if (u >= p.units) break;
         ok = mbar_wait(empty(s), ph ^ 1u, abort_flag, kDevTimeoutStageEmpty);
         if (ok) {
@@ -190,7 +204,7 @@ __global__ void __launch_bounds__(kRowsThreads, kRowsCtas)
       pdl_wait();  // the ticket counter belongs to the stream's order
       // Runs ticket v's units; false once v fails (its partner then still has to be seen).
       auto run_ticket = [&](int v) {
-        if (v == tickets - 1) *p.counter = 0;  // the call's last ticket
+        if (v == tickets - 1) *counter = 0;  // the call's last ticket
         if (v >= succ) return false;
         ok = mbar_wait(empty(s), ph ^ 1u, abort_flag, kDevTimeoutStageEmpty);
         if (ok) {
@@ -199,19 +213,19 @@ __global__ void __launch_bounds__(kRowsThreads, kRowsCtas)
         }
         return ok;
       };
-      int qa = atomicAdd(p.counter, 1);
-      int qb = atomicAdd(p.counter, 1);
+      int qa = atomicAdd(counter, 1);
+      int qb = atomicAdd(counter, 1);
       for (;;) {
         if (!run_ticket(qa)) {
-          if (qb == tickets - 1) *p.counter = 0;
+          if (qb == tickets - 1) *counter = 0;
           break;
         }
-        qa = atomicAdd(p.counter, 1);  // lands while qb's units are issued
+        qa = atomicAdd(counter, 1);  // lands while qb's units are issued
         if (!run_ticket(qb)) {
-          if (qa == tickets - 1) *p.counter = 0;
+          if (qa == tickets - 1) *counter = 0;
           break;
         }
-        qb = atomicAdd(p.counter, 1);
+        qb = atomicAdd(counter, 1);
       }
       // no work left: a stage that only says so
       if (ok && mbar_wait(empty(s), ph ^ 1u, abort_flag, kDevTimeoutStageEmpty)) {
@@ -246,15 +260,28 @@ __global__ void __launch_bounds__(kRowsThreads, kRowsCtas)
       __syncwarp();
       if (lane == 0) mbar_arrive(empty(s));
       const float* pr = part + (ph * S + s) * kRowsWarps * kRU;
+      float vs[kRU / 32];
 #pragma unroll
-      for (int r = lane; r < kRU; r += 32) {
+      for (int r = lane, i = 0; r < kRU; r += 32, ++i) {
         float v = 0.f;
-        for (int w2 = 0; w2 < p.groups; ++w2) v += pr[w2 * kRU + r];
-        const int64_t n = (int64_t)u * kRU + r;
-        if (n < p.N) {
-          if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
-          const int64_t off = half + p.col0 + n;
-          for (int d = 0; d < p.ndst; ++d) store_from_f32(p.y[d], off, p.y_t, v);
+        for (int w2 = 0; w2 < sgroups; ++w2) v += pr[w2 * kRU + r];
+        vs[i] = v;
+      }
+      if (NS > 1) {
+        // K-sliced: this slice's partial rows; rows_slice_sum_kernel adds the slices afterwards
+        const int64_t n_ws = (int64_t)p.units * kRU;
+#pragma unroll
+        for (int r = lane, i = 0; r < kRU; r += 32, ++i) p.ws[sl * n_ws + (int64_t)u * kRU + r] = vs[i];
+      } else {
+#pragma unroll
+        for (int r = lane, i = 0; r < kRU; r += 32, ++i) {
+          float v = vs[i];
+          const int64_t n = (int64_t)u * kRU + r;
+          if (n < p.N) {
+            if (p.bias) v = round_to(v, p.y_t) + load_as_f32(p.bias, n, p.bias_t);
+            const int64_t off = half + p.col0 + n;
+            for (int d = 0; d < p.ndst; ++d) store_from_f32(p.y[d], off, p.y_t, v);
+          }
         }
       }
       if (++s == S) {
@@ -267,14 +294,14 @@ __global__ void __launch_bounds__(kRowsThreads, kRowsCtas)
 
   // ---------------- consumers ----------------
   const int g = lane >> 2, t = lane & 3;
-  const bool active = warp < p.groups;
+  const bool active = warp < sgroups;  // this warp's group: g0 + warp
   pdl_wait();  // the activations belong to the stream's order
   uint32_t bfr[8][2];
   float4 F[2];
   {
-    // This warp's group of activations: lane L holds k = 128 w + 4 L .. + 3.
+    // This warp's group of activations: lane L holds k = 128 (g0 + w) + 4 L .. + 3.
     float a4[4] = {0.f, 0.f, 0.f, 0.f};
-    const int64_t k = (int64_t)warp * 128 + 4 * lane;
+    const int64_t k = (int64_t)(g0 + warp) * 128 + 4 * lane;
     if (active) load_act4<AT>(p.a, 0, k, p.K, (p.K & 3) == 0, a4);
     if (AT == TQ4_F32 && p.norm_w) {
       // RMSNorm prologue: the 8 consumer warps hold the whole row (groups * 128 >= K, zeros past
@@ -381,7 +408,7 @@ __global__ void __launch_bounds__(kRowsThreads, kRowsCtas)
         for (int hh = 0; hh < 2; ++hh) {
           const int sg = 2 * t + hh;
           if (sg < NSEG) {
-            const int lb = (warp * 128 + sg * SEG) >> p.bs_log2;  // the segment's block
+            const int lb = (((g0 + warp) * 128 + sg * SEG) >> p.bs_log2) - b0;  // its block in the box
             const int r0 = rb * 16 + g;
             const float s0 = scale_to_f32(sc, lb * kSR + r0, p.st_bytes, p.st_bf16);
             const float s8 = scale_to_f32(sc, lb * kSR + r0 + 8, p.st_bytes, p.st_bf16);
@@ -421,21 +448,54 @@ __global__ void __launch_bounds__(kRowsThreads, kRowsCtas)
   }
 }
 
+// The sum of a K-sliced call: Y[n] = sum over the slices s of ws[s][n] in slice order
+// (deterministic), then the bias; launched after the main kernel with programmatic dependent
+// launch (griddepcontrol.wait: every slice's partial rows written).
+__global__ void __launch_bounds__(256) rows_slice_sum_kernel(const float* __restrict__ ws, int ns, int64_t n_ws,
+                                                             int64_t n, const void* bias, tq4_dtype bias_t,
+                                                             void* y, tq4_dtype y_t) {
+  pdl_wait();
+  pdl_trigger();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = 0.f;
+    for (int s = 0; s < ns; ++s) v += ws[s * n_ws + i];
+    if (bias) v = round_to(v, y_t) + load_as_f32(bias, i, bias_t);
+    store_from_f32(y, i, y_t, v);
+  }
+}
+
 // ---- host side --------------------------------------------------------------------------------
 
-// The unit's scale blocks: the (padded) K's blocks, at most the handle's block rows.
+// The scale blocks of a unit's K slice (its 8 packed groups, or the whole row when it has fewer),
+// at most the handle's block rows.
 static int rows_scale_blocks(const Weight& w) {
-  const int64_t nb = (w.groups * 128 + w.desc.block_size - 1) / w.desc.block_size;
+  const int64_t nb = (std::min<int64_t>(w.groups, kRowsWarps) * 128 + w.desc.block_size - 1) / w.desc.block_size;
   return (int)std::min<int64_t>(nb, w.blocks_pad);
 }
 
+#ifndef TQ4_ROWS_MAX_SLICES
+#define TQ4_ROWS_MAX_SLICES 1024  // K slices of 8 groups the kernel takes (rows of up to 8 * this many groups)
+#endif
+
 bool rows_eligible(const Weight& w) {
-  return w.rw_ok && w.desc.bits == 4 && w.groups <= kRowsWarps;
+  return w.rw_ok && w.desc.bits == 4 && w.desc.block_size <= 1024 &&
+         (w.groups + kRowsWarps - 1) / kRowsWarps <= TQ4_ROWS_MAX_SLICES;
 }
+
+int rows_slices(const Weight& w) { return (int)((w.groups + kRowsWarps - 1) / kRowsWarps); }
+
+static int64_t rows_units(const Weight& w) { return (w.desc.N + kRU - 1) / kRU; }
+
+int64_t rows_ws_floats(const Weight& w) {
+  return rows_slices(w) > 1 ? rows_slices(w) * rows_units(w) * kRU : 0;
+}
+
+int64_t rows_counters(const Weight& w) { return rows_slices(w); }
 
 tq4_status make_rows_maps(Weight& w) {
   w.rw_ok = false;
-  if (w.desc.bits != 4 || w.groups > kRowsWarps) return TQ4_OK;
+  // a slice of 8 groups (1024 k) holds whole blocks up to 1024
+  if (w.desc.bits != 4 || w.desc.block_size > 1024) return TQ4_OK;
   const int st = dtype_size(w.desc.dequant_dtype);
   const CUtensorMapDataType sdt = st == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
   const int nbs = rows_scale_blocks(w);
@@ -461,7 +521,7 @@ static RowsPlan plan_rows(const Weight& w) {
   const int st = dtype_size(w.desc.dequant_dtype);
   const int nbs = rows_scale_blocks(w);
   const int sc_bytes = (kSR * nbs * st + 127) / 128 * 128;
-  pl.sc_off = (int)w.groups * kRU * 64;
+  pl.sc_off = (int)std::min<int64_t>(w.groups, kRowsWarps) * kRU * 64;
   pl.zc_off = pl.sc_off + sc_bytes;
   pl.stage_bytes = (pl.zc_off + (w.zps.ptr ? sc_bytes : 0) + 1023) / 1024 * 1024;
   const int per_stage = pl.stage_bytes + 2 * kRowsWarps * kRU * 4;  // + the stage's partials (two laps)
@@ -469,8 +529,10 @@ static RowsPlan plan_rows(const Weight& w) {
   pl.part_off = pl.stages * pl.stage_bytes;
   pl.tail_off = pl.part_off + 2 * pl.stages * kRowsWarps * kRU * 4;
   pl.smem = pl.tail_off + kRowsTail;
-  const int units = (int)((w.desc.N + kRU - 1) / kRU);
-  pl.grid = std::min(units, kRowsCtas * w.num_sms);
+  // a multiple of the slice count, each slice's CTAs no more than its units
+  const int ns = rows_slices(w);
+  const int64_t per_slice = std::min<int64_t>(rows_units(w), std::max(1, kRowsCtas * w.num_sms / ns));
+  pl.grid = (int)(per_slice * ns);
   return pl;
 }
 
@@ -496,7 +558,8 @@ static cudaError_t launch_rows_at(const Weight& w, const RowsArgs& args, int gri
 }
 
 tq4_status run_gemv_rows(const Weight& w, const void* a, tq4_dtype a_t, const void* bias, tq4_dtype bias_t,
-                         tq4_dtype y_t, const RowsDst& dst, int* counter, cudaStream_t st, const RowsNorm* norm) {
+                         tq4_dtype y_t, const RowsDst& dst, int* counter, cudaStream_t st, const RowsNorm* norm,
+                         float* ws) {
   if (!rows_eligible(w)) {
     set_error("GEMV: the handle has no 32-row unit descriptors");
     return TQ4_ERR_UNSUPPORTED;
@@ -508,6 +571,11 @@ tq4_status run_gemv_rows(const Weight& w, const void* a, tq4_dtype a_t, const vo
   if (norm && a_t != TQ4_F32) {
     set_error("GEMV: the RMSNorm prologue takes f32 activations");
     return TQ4_ERR_UNSUPPORTED;
+  }
+  const int ns = rows_slices(w);
+  if (ns > 1 && (norm || dst.ndst != 1 || dst.epoch || ws == nullptr)) {
+    set_error("GEMV: K-sliced rows take one destination, no prologue, and a workspace");
+    return TQ4_ERR_INVALID_ARGUMENT;
   }
   const RowsPlan pl = plan_rows(w);
   if (pl.stages < 2) {
@@ -545,11 +613,19 @@ tq4_status run_gemv_rows(const Weight& w, const void* a, tq4_dtype a_t, const vo
   args.part_off = pl.part_off;
   args.tail_off = pl.tail_off;
   args.counter = counter;
+  args.slices = ns;
+  args.ws = ws;
   cudaError_t e;
   switch (a_t) {
     case TQ4_F16: e = launch_rows_at<TQ4_F16>(w, args, pl.grid, pl.smem, st); break;
     case TQ4_BF16: e = launch_rows_at<TQ4_BF16>(w, args, pl.grid, pl.smem, st); break;
     default: e = launch_rows_at<TQ4_F32>(w, args, pl.grid, pl.smem, st); break;
+  }
+  if (e == cudaSuccess && ns > 1) {
+    const int64_t n = w.desc.N;
+    const int grid = (int)std::min<int64_t>((n + 255) / 256, 2 * w.num_sms);
+    e = launch_pdl(rows_slice_sum_kernel, dim3(grid), dim3(256), 0, st, static_cast<const float*>(ws), ns,
+                   rows_units(w) * kRU, n, bias, bias_t, dst.y[0], y_t);
   }
   if (e != cudaSuccess) {
     set_error("GEMV (32-row units) launch failed: %s", cudaGetErrorString(e));
