@@ -235,7 +235,9 @@ struct GemmTile {
   static_assert(TM + SLOTS * 64 <= COLS && SLOTS <= kASlots, "TMEM columns");
 };
 
-template <int TM, bool BF, tq4_dtype T, int BITS>
+// HOIST: block_size >= 128, so one block covers each 128-k stage and its scale and zero point are
+// read once per stage instead of per position.
+template <int TM, bool BF, tq4_dtype T, int BITS, bool HOIST>
 __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM, BITS>::CTAS)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                 const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_z,
@@ -389,6 +391,9 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM, BITS>::CTAS)
     // are normal numbers; ldexpf itself for the rare rows outside that range
     const bool pw_ok = we > -126 && we < 126;
     const float pw_up = ldexpf(1.f, we), pw_down = ldexpf(1.f, -we);
+    constexpr bool kFusedOk = !(BF && BITS == 8);
+    // the packed f16 / bf16 path: exact (O + q) - (O + z), then one multiply (uniform for the call)
+    const bool fused = kFusedOk && (T_SAME || (T == TQ4_F32 && p.s16)) && p.int_zp;
     for (int kt = 0; kt < KT; ++kt) {
       const int s = kt % S, a = kt % L::SLOTS;
       if (!mbar_wait(wfull(s), (kt / S) & 1, abort_flag, kDevTimeoutTmaFull)) break;
@@ -407,10 +412,26 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM, BITS>::CTAS)
       const uint32_t col0 = lane_addr + TM + a * 64 + 2 * tp;  // column 8j + 2tp holds k = 16j + 4tp, +1
       uint32_t s2 = 0, oz2 = 0, oz16n = 0;
       float scv = 0.f, z = 0.f;
+      auto block_params = [&](int lb) {  // the scale and zero point of staged block row lb
+        if (fused) {
+          const uint32_t sv = reinterpret_cast<const uint16_t*>(sc)[lb * WN + r];
+          s2 = sv | (sv << 16);
+          z = p.has_zp ? scale_to_f32(zc, lb * WN + r, 2, BF) : p.z_const;
+          oz2 = h2_splat((BF ? 128.f : 1024.f) + z, BF);
+          oz16n = h2_splat(-(64.f + z), BF);
+        } else {
+          const float sraw = scale_to_f32(sc, lb * WN + r, p.st_bytes, T == TQ4_BF16);
+          scv = pw_ok ? sraw * pw_down : ldexpf(sraw, -we);
+          z = p.has_zp ? scale_to_f32(zc, lb * WN + r, p.st_bytes, T == TQ4_BF16) : p.z_const;
+        }
+      };
+      if constexpr (HOIST) block_params(0);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int lb = (((kt0 + kt) * 128 + 16 * j) >> p.bs_log2) - b0;  // staged block row
-        const bool new_block = (j == 0) || (((16 * j) & ((1 << p.bs_log2) - 1)) == 0);
+        if constexpr (!HOIST) {
+          const int lb = (((kt0 + kt) * 128 + 16 * j) >> p.bs_log2) - b0;  // staged block row
+          if ((j == 0) || (((16 * j) & ((1 << p.bs_log2) - 1)) == 0)) block_params(lb);
+        }
         uint32_t x;
         int sh = 0;
         if constexpr (BITS == 4) {
@@ -423,17 +444,9 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM, BITS>::CTAS)
           sh = 4 * (j & 3);
         }
         uint32_t w0, w1;
-        constexpr bool kFusedOk = !(BF && BITS == 8);
-        if (kFusedOk && (T_SAME || (T == TQ4_F32 && p.s16)) && p.int_zp) {
+        if (fused) {
           // (O + q) - (O + z) is exact in the MMA type; one more multiply gives RN_T((q - z) * s)
           // (f32 weights: times the f16 s * 2^-we of the handle's scales16)
-          if (new_block) {
-            const uint32_t sv = reinterpret_cast<const uint16_t*>(sc)[lb * WN + r];
-            s2 = sv | (sv << 16);
-            z = p.has_zp ? scale_to_f32(zc, lb * WN + r, 2, BF) : p.z_const;
-            oz2 = h2_splat((BF ? 128.f : 1024.f) + z, BF);
-            oz16n = h2_splat(-(64.f + z), BF);
-          }
           const uint32_t src = (j & 1) ? (x >> 8) : x;
           uint32_t d0, d1;
           if constexpr (BITS != 4 && kFusedOk) {
@@ -453,11 +466,6 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM, BITS>::CTAS)
           w1 = h2_mul(d1, s2, BF);
         } else {
           // f32 weights: (q - z) * s * 2^-we, exact scaling of the f32 product before its rounding
-          if (new_block) {
-            const float sraw = scale_to_f32(sc, lb * WN + r, p.st_bytes, T == TQ4_BF16);
-            scv = pw_ok ? sraw * pw_down : ldexpf(sraw, -we);
-            z = p.has_zp ? scale_to_f32(zc, lb * WN + r, p.st_bytes, T == TQ4_BF16) : p.z_const;
-          }
           uint32_t q0, q1;
           if constexpr (BITS == 4) q_pairs4(x, j, BF, q0, q1);
           else exact_pairs<BITS, BF>(x, sh, q0, q1);
@@ -734,21 +742,13 @@ static GemmPlan plan_gemm_smem(const Weight& w, int st) {  // st: bytes of a sta
   return pl;
 }
 
-template <int TM, bool BF, tq4_dtype T, int BITS>
-static tq4_status launch_gemm_t(const CUtensorMap& ma, const Weight& w, GemmArgs args, cudaStream_t st) {
-  const GemmPlan pl = plan_gemm_smem<TM, BITS>(w, args.st_bytes);
-  if (pl.stages < 2) {
-    set_error("GEMM: the stage does not fit shared memory");
-    return TQ4_ERR_UNSUPPORTED;
-  }
-  args.stages = pl.stages;
-  args.stage_bytes = pl.stage_bytes;
-  args.sc_off = pl.sc_off;
-  args.zc_off = pl.zc_off;
-  auto kern = gemm_kernel<TM, BF, T, BITS>;
-  static std::atomic<uint64_t> attr_set{0};  // per device, at the largest size it can ask for
+using GemmKernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs);
+
+// One launch of `kern` (its own once-per-device shared-memory attribute flag in `attr_set`).
+static tq4_status launch_gemm_kern(GemmKernel kern, std::atomic<uint64_t>& attr_set, const GemmPlan& pl, int tm,
+                                   const CUtensorMap& ma, const Weight& w, const GemmArgs& args, cudaStream_t st) {
   TQ4_CUDA(set_smem_limit_once(kern, kSmemLimit, attr_set));
-  const dim3 grid(((args.N + WN - 1) / WN) * args.ks, (args.M + TM - 1) / TM);
+  const dim3 grid(((args.N + WN - 1) / WN) * args.ks, (args.M + tm - 1) / tm);
   if (args.ks == 1) {
     TQ4_CUDA(launch_pdl(kern, grid, dim3(kGemmThreads), pl.smem, st, ma, w.wmaps[0], args.s16 ? w.smap16 : w.smaps[0],
                         w.zmaps[0], args));
@@ -771,6 +771,27 @@ static tq4_status launch_gemm_t(const CUtensorMap& ma, const Weight& w, GemmArgs
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   TQ4_CUDA(cudaLaunchKernelEx(&cfg, kern, ma, w.wmaps[0], args.s16 ? w.smap16 : w.smaps[0], w.zmaps[0], args));
   return TQ4_OK;
+}
+
+template <int TM, bool BF, tq4_dtype T, int BITS>
+static tq4_status launch_gemm_t(const CUtensorMap& ma, const Weight& w, GemmArgs args, cudaStream_t st) {
+  const GemmPlan pl = plan_gemm_smem<TM, BITS>(w, args.st_bytes);
+  if (pl.stages < 2) {
+    set_error("GEMM: the stage does not fit shared memory");
+    return TQ4_ERR_UNSUPPORTED;
+  }
+  args.stages = pl.stages;
+  args.stage_bytes = pl.stage_bytes;
+  args.sc_off = pl.sc_off;
+  args.zc_off = pl.zc_off;
+  if constexpr (BITS == 4) {
+    if (w.bs_log2 >= 7) {  // one block per 128-k stage (the instantiation is kept to 4-bit weights)
+      static std::atomic<uint64_t> attr_hoist{0};
+      return launch_gemm_kern(gemm_kernel<TM, BF, T, BITS, true>, attr_hoist, pl, TM, ma, w, args, st);
+    }
+  }
+  static std::atomic<uint64_t> attr_set{0};  // per device, at the largest size it can ask for
+  return launch_gemm_kern(gemm_kernel<TM, BF, T, BITS, false>, attr_set, pl, TM, ma, w, args, st);
 }
 
 template <int TM, bool BF, int BITS>
