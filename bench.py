@@ -125,6 +125,21 @@ class ClockSampler:
 
 
 # ---- reference (CPU) path --------------------------------------------------------------------
+_BLAS_LIMITS = None
+
+
+def use_all_host_threads():
+    """The CPU legs use every host core this process may run on, whatever OMP_NUM_THREADS the
+    launcher set (torchrun sets 1 per rank)."""
+    global _BLAS_LIMITS
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    try:
+        from threadpoolctl import threadpool_limits
+        _BLAS_LIMITS = threadpool_limits(limits=n, user_api="blas")
+    except Exception:
+        pass
+
+
 def blas_threads():
     try:
         from threadpoolctl import threadpool_info
@@ -139,6 +154,7 @@ def cpu_reference(cfg, p, steps, warmup, budget_s):
     dense f32 A @ W^T per call. `warmup` (at least 3) untimed calls, then `steps` (at least 20)
     timed calls, fewer only when the calls would exceed budget_s (at least 3). Returns (value in
     the metric's unit from the MEDIAN call time, calls timed, sample text)."""
+    use_all_host_threads()
     from oracle import matmul_nbits as o
     t = cfg.scale_type
     w = o.dequantize_weight(p["B"], p["scales"], p["zp"], cfg.k, cfg.n, cfg.bits, cfg.block_size, t)
@@ -530,6 +546,7 @@ def decoder_cpu(cfg, seed, steps, budget_s):
     """Moved-weight CPU path (oracle decoder in float32: dense weights, BLAS matrix-vector products)
     for a bounded number of decode steps at positions 127.. with the cache rows before them
     filled with seeded values (the attention work of a 128-token prefill, without running it)."""
+    use_all_host_threads()
     from oracle.decoder import OracleDecoder
     from transmuter_b200.decoder import random_weights, rope_tables
     weights = random_weights(cfg, seed)
