@@ -198,6 +198,10 @@ LARGE_M = [
     # f32 weights (row scale and weight exponent applied after the cross-CTA sum) with bias
     (4096, 1024, 256, 4, 128, "packed", "f16", "f16", "f16", False),
     (4096, 640, 100, 4, 32, "none", "f32", "f32", "f32", True),
+    # blocks that span several 128-k stages (one scale and zero point per stage, read once)
+    (2048, 256, 96, 4, 256, "packed", "f16", "f16", "f16", False),
+    (2048, 200, 64, 4, 1024, "none", "bf16", "bf16", "bf16", True),
+    (3000, 300, 140, 4, 512, "float", "f16", "f16", "f16", True),
 ]
 
 
@@ -264,6 +268,8 @@ F32_PREFILL = [
     (72, 16, 20, 32, "none", (0.005, 0.02)),
     (1024, 256, 64, 32, "packed", (1e-6, 1e-5)),
     (4096, 640, 300, 128, "packed", (0.002, 0.01)),
+    (1024, 384, 48, 128, "none", (0.005, 0.02)),   # f16 block scales of f32 weights, one per stage
+    (2048, 256, 64, 256, "none", (1e-6, 1e-5)),
 ]
 
 
