@@ -588,11 +588,12 @@ def decoder_bench(args, rank, world, local_rank):
     steps = args.steps or 128
     if steps > cfg.max_len - DECODE_PROMPT:
         raise SystemExit(f"--steps at most {cfg.max_len - DECODE_PROMPT} for c4 (cache of {cfg.max_len})")
+    # the same config for both arms (the driver compares them)
+    config["parallelism"] = "single GPU" if world == 1 else f"{world} independent replicas"
     if args.impl == "reference":
         if rank != 0:
             return
         value, n_timed, sample = decoder_cpu(cfg, seed, steps, budget_s=120.0)
-        config["parallelism"] = "host cores"
         line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
                 "steps": steps, "warmup": args.warmup, "ms_per_step": 1e3 / value, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -610,7 +611,6 @@ def decoder_bench(args, rank, world, local_rank):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    config["parallelism"] = "single GPU" if world == 1 else f"{world} independent replicas"
     # q, k, v and gate, up as separate inputs (as an ONNX export stores them), merged at load
     dec = Q4Decoder(cfg, device=dev, weights=split_siblings(random_weights(cfg, seed), cfg))
     prompt = np.random.default_rng(seed + rank).integers(0, cfg.vocab, DECODE_PROMPT)
