@@ -484,10 +484,18 @@ def main():
         peak = pk["hbm_gbs"]
         bound, unit = "hbm", "GB/s"
     traffic = None
+    traffic_source = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
             traffic = json.load(f).get(args.workload)
+    if traffic is not None:
+        traffic_source = "ncu capture of one launch on one GPU (profiles/traffic.json)"
+        if sharded_run and world > 1:
+            # a rank streams 1/N of the weight rows, which are all but a few KB of the capture
+            traffic = traffic / world
+            traffic_source = ("the one-GPU capture scaled by the rank's 1/N share of the weight rows "
+                              "(not captured on N GPUs)")
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": cfg.metric, "n_gpus": world, "steps": steps,
@@ -498,7 +506,7 @@ def main():
                 "dtype": cfg.a_type, "data": "synthetic (seeded; shapes and distributions of the config)",
                 "config": config,
                 "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
-                             "frac": achieved / peak, "traffic": traffic,
+                             "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_source,
                              "peak_source": f"{pk_kind} ({'burst' if bound == 'tensor' else 'copy'})",
                              "scope": ("one GPU's share of the whole step (its 1/N of the weight through the "
                                        "MatMulNBits kernel, plus the assembly of Y)") if sharded_run else
