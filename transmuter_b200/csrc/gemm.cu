@@ -11,9 +11,11 @@
 //            operand), the packed weight tile (128 rows x 64 bytes per group) and the stage's
 //            block-major scales / zero points, completing on full[s].
 //   warps 2-17 dequantise in registers: warp w owns TMEM lanes 32*(w%4).. (its 32 weight rows)
-//            and one 16-byte piece of each row (32 weights spread over the stage's k; the packed
-//            tile arrives with the 64-byte swizzle, so these loads are free of bank conflicts);
-//            each thread turns them into RN_T(RN_T(q - z) * s) (exactly the reference's weight
+//            and 16-byte pieces of each row (32 weights each, spread over the stage's k; the
+//            packed tile arrives with the 64-byte swizzle, so these loads are free of bank
+//            conflicts): with 256-row activation tiles all 16 warps take every stage, one piece
+//            each; with narrower tiles two teams of 8 take alternate stages, two pieces each.
+//            Each thread turns them into RN_T(RN_T(q - z) * s) (exactly the reference's weight
 //            when T is A's type) and writes them with tcgen05.st into one of 4 TMEM weight slots
 //            (64 columns each).
 //   warp 1   TMEM allocation, and one thread that issues tcgen05.mma (M=128, N=TM, K=16, A from
@@ -232,6 +234,13 @@ struct GemmTile {
   static constexpr int SLOTS = TM <= 64 ? 3 : 4;
   static constexpr int COLS = TM <= 64 ? 256 : 512;
   static constexpr int CTAS = TM <= 64 ? 2 : 1;
+  // Dequantising teams: up to 128 activation rows the MMAs of a stage are short and a stage took
+  // one warp's chain of latencies (waits, shared-memory loads, TMEM stores, tcgen05.wait::st)
+  // with all 16 warps on it; two teams of 8 on alternate stages, each warp converting two pieces
+  // of its row, overlap those chains (C2 11.3 -> 10.2 us, C3 M = 64 89.7 -> 75.8 us, C5 M = 16
+  // 37.6 -> 35.4 us). With 256 rows the MMAs bound the stage and one team measured 1-2% faster.
+  static constexpr int TEAMS = TM <= 128 ? 2 : 1;
+  static constexpr int PIECES = TEAMS;  // 16-byte pieces of its row a warp converts per stage
   static_assert(TM + SLOTS * 64 <= COLS && SLOTS <= kASlots, "TMEM columns");
 };
 
@@ -277,10 +286,10 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM, BITS>::CTAS)
     for (int s = 0; s < S; ++s) {
       mbar_init(full(s), 1);
       mbar_init(wfull(s), 1);
-      mbar_init(empty(s), 1 + kDeqWarps);  // the MMAs' commit + the dequantising warps
+      mbar_init(empty(s), 1 + kDeqWarps / L::TEAMS);  // the MMAs' commit + the stage's team
     }
     for (int a = 0; a < L::SLOTS; ++a) {
-      mbar_init(afull(a), kDeqWarps);
+      mbar_init(afull(a), kDeqWarps / L::TEAMS);
       mbar_init(aempty(a), 1);
     }
     mbar_init(accum, 1);
@@ -394,22 +403,33 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM, BITS>::CTAS)
     constexpr bool kFusedOk = !(BF && BITS == 8);
     // the packed f16 / bf16 path: exact (O + q) - (O + z), then one multiply (uniform for the call)
     const bool fused = kFusedOk && (T_SAME || (T == TQ4_F32 && p.s16)) && p.int_zp;
-    for (int kt = 0; kt < KT; ++kt) {
+    // L::TEAMS teams take alternate stages; with two, team (warp - 2) / 8 converts pieces 2 tpt
+    // and 2 tpt + 1 of each of its rows (GemmTile::TEAMS)
+    constexpr int PIECES = L::PIECES;
+    const int team = (warp - 2) / (kDeqWarps / L::TEAMS);
+    const int tpt = L::TEAMS == 2 ? ((warp - 2) >> 2) & 1 : tp;  // the warp's piece pair (or piece)
+    for (int kt = team; kt < KT; kt += L::TEAMS) {
       const int s = kt % S, a = kt % L::SLOTS;
       if (!mbar_wait(wfull(s), (kt / S) & 1, abort_flag, kDevTimeoutTmaFull)) break;
       if (!mbar_wait(aempty(a), ((kt / L::SLOTS) & 1) ^ 1, abort_flag, kDevTimeoutDequant)) break;
       const uint8_t* st = smem + s * p.stage_bytes;
-      // the 64-byte swizzle puts piece tp of row r at 16 * (tp ^ ((r >> 1) & 3)): the 8 lanes of
+      // the 64-byte swizzle puts piece q of row r at 16 * (q ^ ((r >> 1) & 3)): the 8 lanes of
       // each load phase read 8 different bank groups
-      const uint32_t piece = r * 64 + ((tp ^ ((r >> 1) & 3)) << 4);
-      const uint4 v = *reinterpret_cast<const uint4*>(st + L::ACT_BYTES + piece);
-      // 8 bits: the stage's second group (positions j = 4..7); 2 bits: which half of the group
-      const uint4 v1 = BITS == 8 ? *reinterpret_cast<const uint4*>(st + L::ACT_BYTES + WN * 64 + piece) : v;
+      uint4 vp[PIECES], vp1[PIECES];
+#pragma unroll
+      for (int pi = 0; pi < PIECES; ++pi) {
+        const int q = PIECES * tpt + pi;
+        const uint32_t piece = r * 64 + ((q ^ ((r >> 1) & 3)) << 4);
+        vp[pi] = *reinterpret_cast<const uint4*>(st + L::ACT_BYTES + piece);
+        // 8 bits: the stage's second group (positions j = 4..7); 2 bits: which half of the group
+        vp1[pi] = BITS == 8 ? *reinterpret_cast<const uint4*>(st + L::ACT_BYTES + WN * 64 + piece) : vp[pi];
+      }
       const int half = (kt0 + kt) & 1;
       const uint8_t* sc = st + p.sc_off;
       const uint8_t* zc = st + p.zc_off;
       const int b0 = ((kt0 + kt) * 128) >> p.bs_log2;
-      const uint32_t col0 = lane_addr + TM + a * 64 + 2 * tp;  // column 8j + 2tp holds k = 16j + 4tp, +1
+      // column 8j + 2q holds k = 16j + 4q, +1 (piece q)
+      const uint32_t col0 = lane_addr + TM + a * 64 + 2 * PIECES * tpt;
       uint32_t s2 = 0, oz2 = 0, oz16n = 0;
       float scv = 0.f, z = 0.f;
       auto block_params = [&](int lb) {  // the scale and zero point of staged block row lb
@@ -432,47 +452,52 @@ __global__ void __launch_bounds__(kGemmThreads, GemmTile<TM, BITS>::CTAS)
           const int lb = (((kt0 + kt) * 128 + 16 * j) >> p.bs_log2) - b0;  // staged block row
           if ((j == 0) || (((16 * j) & ((1 << p.bs_log2) - 1)) == 0)) block_params(lb);
         }
-        uint32_t x;
-        int sh = 0;
-        if constexpr (BITS == 4) {
-          x = (j < 2) ? v.x : (j < 4) ? v.y : (j < 6) ? v.z : v.w;
-        } else if constexpr (BITS == 8) {
-          const uint4& vv = j < 4 ? v : v1;
-          x = ((j & 3) == 0) ? vv.x : ((j & 3) == 1) ? vv.y : ((j & 3) == 2) ? vv.z : vv.w;
-        } else {
-          x = half ? ((j < 4) ? v.z : v.w) : ((j < 4) ? v.x : v.y);
-          sh = 4 * (j & 3);
-        }
-        uint32_t w0, w1;
-        if (fused) {
-          // (O + q) - (O + z) is exact in the MMA type; one more multiply gives RN_T((q - z) * s)
-          // (f32 weights: times the f16 s * 2^-we of the handle's scales16)
-          const uint32_t src = (j & 1) ? (x >> 8) : x;
-          uint32_t d0, d1;
-          if constexpr (BITS != 4 && kFusedOk) {
-            uint32_t pa, pb;
-            magic_pairs<BITS, BF>(x, sh, pa, pb);
-            d0 = h2_sub(pa, oz2, BF);
-            d1 = h2_sub(pb, oz2, BF);
-          } else if (!BF) {
-            d0 = h2_sub(lop3_and_or(src, 0x000F000Fu, 0x64006400u), oz2, false);
-            const uint32_t r1 = lop3_and_or(src, 0x00F000F0u, 0x64006400u);  // 1024 + 16 q
-            asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d1) : "r"(r1), "r"(0x2C002C00u), "r"(oz16n));
+#pragma unroll
+        for (int pi = 0; pi < PIECES; ++pi) {
+          const uint4& v = vp[pi];
+          const uint4& v1 = vp1[pi];
+          uint32_t x;
+          int sh = 0;
+          if constexpr (BITS == 4) {
+            x = (j < 2) ? v.x : (j < 4) ? v.y : (j < 6) ? v.z : v.w;
+          } else if constexpr (BITS == 8) {
+            const uint4& vv = j < 4 ? v : v1;
+            x = ((j & 3) == 0) ? vv.x : ((j & 3) == 1) ? vv.y : ((j & 3) == 2) ? vv.z : vv.w;
           } else {
-            d0 = h2_sub(lop3_and_or(src, 0x000F000Fu, 0x43004300u), oz2, true);
-            d1 = h2_sub(lop3_and_or(src >> 4, 0x000F000Fu, 0x43004300u), oz2, true);
+            x = half ? ((j < 4) ? v.z : v.w) : ((j < 4) ? v.x : v.y);
+            sh = 4 * (j & 3);
           }
-          w0 = h2_mul(d0, s2, BF);
-          w1 = h2_mul(d1, s2, BF);
-        } else {
-          // f32 weights: (q - z) * s * 2^-we, exact scaling of the f32 product before its rounding
-          uint32_t q0, q1;
-          if constexpr (BITS == 4) q_pairs4(x, j, BF, q0, q1);
-          else exact_pairs<BITS, BF>(x, sh, q0, q1);
-          w0 = deq_pair<BF, T>(q0, z, scv);
-          w1 = deq_pair<BF, T>(q1, z, scv);
+          uint32_t w0, w1;
+          if (fused) {
+            // (O + q) - (O + z) is exact in the MMA type; one more multiply gives RN_T((q - z) * s)
+            // (f32 weights: times the f16 s * 2^-we of the handle's scales16)
+            const uint32_t src = (j & 1) ? (x >> 8) : x;
+            uint32_t d0, d1;
+            if constexpr (BITS != 4 && kFusedOk) {
+              uint32_t pa, pb;
+              magic_pairs<BITS, BF>(x, sh, pa, pb);
+              d0 = h2_sub(pa, oz2, BF);
+              d1 = h2_sub(pb, oz2, BF);
+            } else if (!BF) {
+              d0 = h2_sub(lop3_and_or(src, 0x000F000Fu, 0x64006400u), oz2, false);
+              const uint32_t r1 = lop3_and_or(src, 0x00F000F0u, 0x64006400u);  // 1024 + 16 q
+              asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d1) : "r"(r1), "r"(0x2C002C00u), "r"(oz16n));
+            } else {
+              d0 = h2_sub(lop3_and_or(src, 0x000F000Fu, 0x43004300u), oz2, true);
+              d1 = h2_sub(lop3_and_or(src >> 4, 0x000F000Fu, 0x43004300u), oz2, true);
+            }
+            w0 = h2_mul(d0, s2, BF);
+            w1 = h2_mul(d1, s2, BF);
+          } else {
+            // f32 weights: (q - z) * s * 2^-we, exact scaling of the f32 product before its rounding
+            uint32_t q0, q1;
+            if constexpr (BITS == 4) q_pairs4(x, j, BF, q0, q1);
+            else exact_pairs<BITS, BF>(x, sh, q0, q1);
+            w0 = deq_pair<BF, T>(q0, z, scv);
+            w1 = deq_pair<BF, T>(q1, z, scv);
+          }
+          tmem_st2(col0 + 8 * j + 2 * pi, w0, w1);
         }
-        tmem_st2(col0 + 8 * j, w0, w1);
       }
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;");
