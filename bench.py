@@ -234,6 +234,23 @@ def rotation_copies(per_copy_bytes):
 
 
 # ---- our path --------------------------------------------------------------------------------
+def roofline_traffic(workload, sharded_world=1, path=None):
+    """DRAM bytes of one launch of the workload's dominant kernel, from the committed ncu capture
+    (profiles/traffic.json), and where the figure comes from. Under N-sharding a rank streams 1/N
+    of the weight rows, which are all but a few KB of the capture: the one-GPU figure / N."""
+    path = path or os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None, None
+    with open(path) as f:
+        traffic = json.load(f).get(workload)
+    if traffic is None:
+        return None, None
+    if sharded_world > 1:
+        return traffic / sharded_world, ("the one-GPU capture scaled by the rank's 1/N share of the "
+                                         "weight rows (not captured on N GPUs)")
+    return traffic, "ncu capture of one launch on one GPU (profiles/traffic.json)"
+
+
 def launches_per_call(cfg, m, sharded_world=1):
     """libtq4 kernels per call (NCCL's own kernels are not counted)."""
     groups = -(-(cfg.blocks * cfg.block_size * cfg.bits // 8) // 64)   # packed groups of 64 bytes per row
@@ -483,19 +500,7 @@ def main():
         achieved = cfg.algorithmic_bytes() / (world if sharded_run else 1) / sec_per_call / 1e9
         peak = pk["hbm_gbs"]
         bound, unit = "hbm", "GB/s"
-    traffic = None
-    traffic_source = None
-    tpath = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tpath):
-        with open(tpath) as f:
-            traffic = json.load(f).get(args.workload)
-    if traffic is not None:
-        traffic_source = "ncu capture of one launch on one GPU (profiles/traffic.json)"
-        if sharded_run and world > 1:
-            # a rank streams 1/N of the weight rows, which are all but a few KB of the capture
-            traffic = traffic / world
-            traffic_source = ("the one-GPU capture scaled by the rank's 1/N share of the weight rows "
-                              "(not captured on N GPUs)")
+    traffic, traffic_source = roofline_traffic(args.workload, world if sharded_run else 1)
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": cfg.metric, "n_gpus": world, "steps": steps,

@@ -26,3 +26,16 @@ def test_both_arms_print_one_config():
         for world in (1, 2, 8):
             assert bench.workload_config(C[name], world) == bench.workload_config(C[name], world)
             assert "parallelism" in bench.workload_config(C[name], world)
+
+
+def test_roofline_traffic(tmp_path):
+    path = tmp_path / "traffic.json"
+    path.write_text('{"c3m1": 100000000}')
+    assert bench.roofline_traffic("c3m1", 1, str(path))[0] == 100000000
+    t, src = bench.roofline_traffic("c3m1", 4, str(path))
+    assert t == 25000000 and "1/N" in src
+    assert bench.roofline_traffic("c2", 1, str(path)) == (None, None)
+    assert bench.roofline_traffic("c3m1", 1, str(tmp_path / "absent.json")) == (None, None)
+    # the committed captures: one per benchmarked GEMV / GEMM workload named in them
+    t, _ = bench.roofline_traffic("c3m1")
+    assert t is not None and t > workloads.CONFIGS["c3m1"].algorithmic_bytes()
