@@ -55,3 +55,56 @@ def test_what_does_not_merge():
     out, w = fusion.matmuls(nodes, weights, merge=fake_merge)
     assert [n.name for n in out] == ["a", "b", "c", "d", "e", "f", "g", ""]
     assert w.keys() == weights.keys()
+
+
+def test_merged_graph_gives_the_unmerged_outputs():
+    """fusion_test.exs:396-430: two 4-bit MatMulNBits nodes read x (K 1024, N 32 and 16, block 32,
+    no zero points, B an iota pattern, constant scales). The merged node and its Split give the
+    outputs of the graph without the rewrite, within the test's tolerance (atol = rtol = 1e-4).
+    Evaluated here with the oracle, the merged weight being the row concatenation of the parts'
+    B and scales (the layout tq4_weight_merge builds on the device, where the GPU tests check it
+    bit for bit)."""
+    import numpy as np
+    from oracle import matmul_nbits as o
+
+    def packed(n, factor):
+        return ((np.arange(n * 32 * 16).reshape(n, 32, 16) * factor) % 256).astype(np.uint8)
+
+    weights = {}
+    for name, b, s in (("bq", packed(32, 7), 0.01), ("bk", packed(16, 13), 0.02)):
+        w = fake_weight(1024, b.shape[0])
+        w.host = (b, np.full(b.shape[0] * 32, s, np.float32))
+        weights[name] = w
+
+    def merge(parts):
+        w = fake_weight(parts[0].k, sum(p.n for p in parts))
+        w.host = tuple(np.concatenate([p.host[i] for p in parts]) for i in range(2))
+        return w
+
+    attrs = {"K": 1024, "bits": 4, "block_size": 32}
+    nodes = [Node("MatMulNBits", dict(attrs, N=32), ["x", "bq"], ["q"], name="q"),
+             Node("MatMulNBits", dict(attrs, N=16), ["x", "bk"], ["k"], name="k")]
+    x = ((np.arange(2 * 1024) % 17.0) - 8.0).astype(np.float32).reshape(1, 2, 1024)
+
+    def run(graph, ws):
+        env = {"x": x}
+        for n in graph:
+            if n.op_type == "MatMulNBits":
+                b, s = ws[n.input[1]].host
+                env[n.output[0]] = o.matmul_nbits(n.attribute, env[n.input[0]], b, s)[0]
+            else:  # Split along the last axis
+                cuts = np.cumsum(n.attribute["split"])[:-1]
+                env.update(zip(n.output, np.split(env[n.input[0]], cuts, axis=-1)))
+        return env
+
+    fused, fw = fusion.matmuls(nodes, weights, outputs=["q", "k"], merge=merge)
+    assert [n.op_type for n in fused] == ["MatMulNBits", "Split"]
+    merged = fw["bq:merged"]
+    wq = o.dequantize_weight(*weights["bq"].host, None, 1024, 32, 4, 32, "f32")
+    wk = o.dequantize_weight(*weights["bk"].host, None, 1024, 16, 4, 32, "f32")
+    np.testing.assert_array_equal(o.dequantize_weight(*merged.host, None, 1024, 48, 4, 32, "f32"),
+                                  np.concatenate([wq, wk]))
+    want, got = run(nodes, weights), run(fused, fw)
+    for name in ("q", "k"):
+        assert got[name].shape == want[name].shape == (1, 2, {"q": 32, "k": 16}[name])
+        np.testing.assert_allclose(got[name], want[name], atol=1e-4, rtol=1e-4)
